@@ -1,0 +1,279 @@
+/*
+ * fg_b200.h -- C ABI of the B200 (sm_100a) MEDUSA tree-verify hot path.
+ *
+ * One MEDUSA tree-verify iteration of FlashGRPO's speculative rollout step:
+ * proposal candidates -> dense candidate tree -> tree attention inside the
+ * verify forward -> exact_target acceptance + extract_path KV compaction.
+ * Reference: ihbkaiser/ss-GRPO, package flashgrpo_b200 (paths below are
+ * inside that project).  The reference has no C/FFI layer; each entry point
+ * replaces the Python/PyTorch call named in its comment, and the Python
+ * package in ss-grpo_b200/flashgrpo_b200 binds them with ctypes.
+ *
+ * Conventions
+ *   - Every entry point returns an fg_status (0 = FG_OK) and never syncs the
+ *     host; work is enqueued on `stream` (a cudaStream_t passed as void*).
+ *   - No entry point allocates device memory.  Callers own every buffer;
+ *     scratch is passed as `workspace` with a matching *_workspace_size().
+ *   - Pointers are device pointers unless the comment says "host".
+ *   - Tensors are row-major; strides are in elements.
+ *   - Kernels that wait on shared-memory barriers give up after about one
+ *     second, record FG_ETIMEOUT in the device error word (fg_read_device_error)
+ *     and return instead of hanging.
+ *
+ * Sampler specification "fg-icdf-v1" (shared by the kernels and the CPU
+ * checker; the reference samples with torch.multinomial,
+ * flashgrpo_b200/decoding/acceptance.py:56-60, so supplied uniforms need a
+ * written definition to be reproducible):
+ *   u      = (Philox4x32-10(counter = (seq_id, round, draw, 0),
+ *                           key = (seed lo32, seed hi32)).x >> 8) * 2^-24
+ *   x_i    = float(logit_i) / T            (IEEE division, only when T > 0)
+ *   m      = max_i x_i;  e_i = fg_exp(x_i - m)   (Cody-Waite + degree-7
+ *            Taylor with fused Horner steps; 0 below -86)
+ *   the vocabulary is cut into 512 contiguous chunks of
+ *   C = roundup8(ceil(V / 512)) entries; c_i = left-to-right fp32 prefix sum
+ *   of e inside the chunk of i; s_t = chunk total;
+ *   P_0 = 0, P_{t+1} = P_t + s_t (sequential), target = u * P_512;
+ *   t* = the chunk with P_t <= target < P_{t+1};
+ *   token = first i of chunk t* with P_t* + c_i > target.
+ *   Greedy (do_sample == 0 or T == 0): first index of the maximum logit.
+ */
+#ifndef FG_B200_H_
+#define FG_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t fg_status;
+#define FG_OK 0
+#define FG_EINVAL 1       /* bad argument (shape, dtype, null pointer, alignment) */
+#define FG_ECAPACITY 2    /* a size exceeds a compile-time or buffer capacity */
+#define FG_ETIMEOUT 3     /* a device-side wait gave up */
+#define FG_ECUDA 4        /* a CUDA launch/runtime call failed; see fg_last_cuda_error */
+#define FG_EUNSUPPORTED 5 /* configuration not implemented (e.g. top_p < 1) */
+
+#define FG_DTYPE_F32 0
+#define FG_DTYPE_BF16 1
+#define FG_DTYPE_F16 2
+
+#define FG_MAX_TREE_NODES 128 /* nodes per candidate tree (ancestor mask words = 4) */
+#define FG_MAX_DEPTHS 8       /* MEDUSA heads / tree depth below the root */
+#define FG_MAX_TOPK 16        /* candidates per head and row */
+#define FG_MAX_PATH 16        /* accepted tokens per row and round */
+#define FG_MAX_LAYERS 128     /* layers addressed by one compaction call */
+
+/* ------------------------------------------------------------ housekeeping */
+const char *fg_version(void);
+const char *fg_status_string(fg_status status);
+/* Last cudaError_t recorded by any entry point in this process. */
+int32_t fg_last_cuda_error(void);
+/* Synchronously reads (and with clear != 0 resets) the device error word of
+ * the current device: 0 or the first FG_* status a kernel recorded. */
+fg_status fg_read_device_error(int32_t *host_out, int32_t clear);
+/* Failure-path check: a kernel waits on *flag (device int32) becoming
+ * nonzero for at most timeout_ns, then writes FG_OK or FG_ETIMEOUT to
+ * *status_out (device int32).  Used to test bounded device waits. */
+fg_status fg_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *status_out, void *stream);
+
+/* ------------------------------------------------------------- sampling */
+/* out[r * n_draws + d] = u(seed, seq_ids[r], round_idx, d).  Draw 0 is the
+ * root sample of a round, draw 1 + s is acceptance step s. */
+fg_status fg_philox_uniforms(uint64_t seed, const int32_t *seq_ids, int32_t n_rows, int32_t round_idx,
+                             int32_t n_draws, float *out, void *stream);
+
+/* One fg-icdf-v1 token per row of logits [n_rows, row_stride] (dtype
+ * FG_DTYPE_*), uniform uniforms[r * u_stride].  forced (nullable): rows with
+ * forced[r] >= 0 take that token instead (pending correction tokens).
+ * Replaces sample_from_logits with top_p = 1, top_k = None
+ * (flashgrpo_b200/decoding/acceptance.py:34-130) for the root token of a
+ * round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1717-1743). */
+fg_status fg_sample_rows(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
+                         const float *uniforms, int64_t u_stride, int32_t do_sample, float temperature,
+                         const int32_t *forced, int32_t *out_tokens, void *stream);
+
+/* Per row: the k best entries ordered by (value descending, index
+ * ascending), the row maximum and logsumexp (rounded to the logits dtype,
+ * as torch.logsumexp returns it).  k <= FG_MAX_TOPK.  Replaces torch.topk in
+ * build_batch_trees (flashgrpo_b200/decoding/medusa_tree.py:767) and the
+ * confidence reductions (flash_medusa_decoder.py:1034-1040). */
+fg_status fg_row_topk(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
+                      int32_t k, int32_t *out_idx, float *out_val, float *out_max, float *out_lse, void *stream);
+
+/* ------------------------------------------------------------ tree build */
+typedef struct fg_plan_params {
+    int32_t tree_mode;          /* 0 = "fixed", 1 = "concurrency_aware", 2 = explicit
+                                   (fixed_topk and max_tree_nodes_per_seq taken as a
+                                   finished TreePlan: no trimming, no planning) */
+    int32_t active_batch_size;  /* rows in the round (plan_tree active_batch_size) */
+    int32_t num_medusa_heads;
+    int32_t cpeak_nodes;
+    int32_t min_tree_nodes_per_seq;
+    int32_t max_tree_nodes_per_seq;
+    int32_t max_tree_depth;
+    int32_t n_fixed;            /* entries of fixed_tree_topk_by_depth */
+    int32_t fixed_topk[FG_MAX_DEPTHS];
+    int32_t adaptive;           /* adaptive_tree_enabled */
+    int32_t n_min;              /* entries of adaptive_min_topk_by_depth */
+    int32_t adaptive_min_topk[FG_MAX_DEPTHS];
+    int32_t confidence_metric;  /* 0 = "top1_prob", 1 = "margin" */
+    float confidence_quantile;
+    double confidence_low;
+    double confidence_high;
+    double depth_weight[FG_MAX_DEPTHS]; /* host: max(decay, 1e-3) ** d */
+    double log_gain[65];        /* host: log1p(v) - log(v) for v = 0..64 (index 0 unused) */
+} fg_plan_params;
+
+/* Plans and builds the shared-topology dense MEDUSA tree of one round:
+ * plan_tree (flashgrpo_b200/decoding/medusa_tree.py:342-459, dense layout),
+ * optional adaptive top-k (flash_medusa_decoder.py:1021-1095, from head_max /
+ * head_lse / cand_val), the BFS expansion with budget truncation
+ * (medusa_tree.py:758-799), the ancestor-only mask of
+ * build_tree_attention_inputs (flashgrpo_b200/decoding/tree_attention.py:6-67)
+ * as bits, logical positions row_len + depth - 1 (:58) and the packed
+ * internal-node logits layout (flash_medusa_decoder.py:1097-1118).
+ *   root [B], cand_idx/cand_val [n_heads][B][kmax] (fg_row_topk output),
+ *   head_max/head_lse [n_heads][B] (adaptive only), row_len [B].
+ * Outputs: tokens [B][nmax], positions [B][nmax], slot [B][nmax]
+ * (b * n_internal + rank, or -1 for leaves), parents/depths [nmax],
+ * anc_bits [nmax][4] (bit j of node i: j is i or an ancestor of i),
+ * internal [nmax] (node ids with children), plan_out [16] =
+ * {budget, n_depth, topk[8], n_nodes, n_internal, 0...}.
+ * Rows share one topology; nmax <= FG_MAX_TREE_NODES. */
+fg_status fg_build_tree(const fg_plan_params *plan, const int32_t *root, const int32_t *cand_idx,
+                        const float *cand_val, const float *head_max, const float *head_lse, int32_t n_heads,
+                        int32_t kmax, int32_t B, int32_t nmax, int32_t logits_dtype, const int32_t *row_len,
+                        int32_t *tokens, int32_t *positions, int32_t *slot, int32_t *parents, int32_t *depths,
+                        uint32_t *anc_bits, int32_t *internal, int32_t *plan_out, void *stream);
+
+/* -------------------------------------------------------- tree attention */
+typedef struct fg_kv_layer {
+    void *k;          /* [B, Hkv, capacity, D] addressed with the strides below */
+    void *v;
+    int64_t stride_b; /* elements */
+    int64_t stride_h;
+    int64_t stride_s;
+    int32_t capacity; /* positions per (row, head) */
+} fg_kv_layer;
+
+/* Flash-decoding GQA attention of the tree queries of one layer:
+ *   q   [B, n_nodes, Hq, D]  (RoPE applied), out [B, n_nodes, Hq, D]
+ *   key/value of row b: prefix slots [0, kv_len[b]) plus the tree nodes at
+ *   slots kv_len[b] + j; node i attends to every prefix slot and to tree
+ *   slot j iff bit j of anc_bits[i] is set (the additive mask of
+ *   tree_attention.py:6-67 as bits).
+ * Replaces HF eager/SDPA attention with the dense 4D mask inside
+ * forward_tree (flashgrpo_b200/models/qwen_flashgrpo_wrapper.py:220-239).
+ * dtype FG_DTYPE_BF16 (tensor cores, D = 128) or FG_DTYPE_F32 (D <= 128).
+ * num_splits 0 = automatic (from max_kv_len, the longest prefix of the
+ * batch).  workspace: fg_tree_attention_workspace_size bytes for the same
+ * arguments (0 when one split suffices), zero-filled before first use (the
+ * kernels leave it reusable). */
+size_t fg_tree_attention_workspace_size(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads,
+                                        int32_t head_dim, int32_t num_splits, int32_t max_kv_len);
+fg_status fg_tree_attention(const void *q, int32_t dtype, const fg_kv_layer *kv, const int32_t *kv_len,
+                            const uint32_t *anc_bits, int32_t B, int32_t n_nodes, int32_t n_q_heads,
+                            int32_t n_kv_heads, int32_t head_dim, float scale, void *out, void *workspace,
+                            size_t workspace_bytes, int32_t num_splits, int32_t max_kv_len, void *stream);
+
+/* ------------------------------------------------ acceptance + extraction */
+typedef struct fg_accept_args {
+    const void *logits;        /* tree logits rows (packed internal nodes) */
+    int32_t logits_dtype;
+    int64_t logits_row_stride;
+    int32_t vocab;
+    const int32_t *slot;       /* [B][nmax]: node -> logits row, -1 = none */
+    const int32_t *tokens;     /* [B][nmax] */
+    const int32_t *parents;    /* [B][parent_stride]; parent_stride 0 = shared */
+    int32_t parent_stride;
+    const int32_t *n_nodes;    /* [B] or NULL (then n_nodes_shared) */
+    int32_t n_nodes_shared;
+    int32_t nmax;
+    const float *uniforms;     /* walk step s of row b uses uniforms[b * u_stride + s] */
+    int32_t u_stride;
+    int32_t B;
+    int32_t do_sample;
+    float temperature;
+    int32_t eos_id;
+    int32_t max_length;
+    int32_t *row_len;          /* [B] logical length before the round; advanced if update_len */
+    int32_t update_len;
+    int32_t *active;           /* [B] or NULL; rows with 0 accept nothing; a row
+                                  that finishes this round is set to 0 */
+    int32_t dcap;              /* columns of acc_tokens / acc_nodes, <= FG_MAX_PATH */
+    int32_t *acc_tokens;       /* [B][dcap], -1 padded */
+    int32_t *acc_nodes;        /* [B][dcap], -1 padded */
+    int32_t *acc_len;          /* [B] */
+    int32_t *correction;       /* [B] target sample that missed, -1 none */
+    int32_t *pending;          /* [B] next round's forced root, -1 none */
+    int32_t *last_node;        /* [B] */
+    int32_t *finished;         /* [B] */
+    /* KV compaction (n_layers = 0 skips it) */
+    int32_t n_layers;
+    const uint64_t *k_layers;  /* host array [n_layers] of device pointers */
+    const uint64_t *v_layers;
+    int32_t kv_elem_bytes;     /* 2 or 4 */
+    int32_t n_kv_heads;
+    int32_t head_dim;
+    int64_t kv_stride_b;
+    int64_t kv_stride_h;
+    int64_t kv_stride_s;
+    /* next-round hidden state gather (hidden_out = NULL skips it) */
+    const void *tree_hidden;   /* [B][nmax][hidden_dim] */
+    void *hidden_out;          /* [B][hidden_dim] */
+    int32_t hidden_dim;
+    int32_t hidden_elem_bytes;
+} fg_accept_args;
+
+/* One CTA per row: the exact_target walk of exact_accept_paths_batch
+ * (flashgrpo_b200/decoding/acceptance.py:183-267), the post-accept clip /
+ * EOS / pending-correction rules (flash_medusa_decoder.py:2289-2343), the
+ * extract_path compaction of the accepted slots in every layer
+ * (flashgrpo_b200/decoding/kv_extraction.py:34-218, on per-row lengths), and
+ * current_hidden = tree_hidden[row, last node] (flash_medusa_decoder.py:2829-2835). */
+fg_status fg_accept_extract(const fg_accept_args *args, void *stream);
+
+/* Compaction alone, for callers that keep their own tree walk:
+ * moves slots row_len[b] + acc_nodes[b][j] to row_len[b] + j, j < acc_len[b],
+ * in every layer (extract_accepted_path_kv, kv_extraction.py:87-218). */
+fg_status fg_extract_path(int32_t n_layers, const uint64_t *k_layers, const uint64_t *v_layers,
+                          int32_t kv_elem_bytes, int32_t B, int32_t n_kv_heads, int32_t head_dim, int64_t stride_b,
+                          int64_t stride_h, int64_t stride_s, const int32_t *row_len, const int32_t *acc_nodes,
+                          const int32_t *acc_len, int32_t dcap, void *stream);
+
+/* ------------------------------------------------- verify-forward helpers */
+/* RoPE at the tree positions and the tree K/V write at the cache tail:
+ *   qkv [B * n_nodes, (Hq + 2 Hkv) * D] (projection output, bias added),
+ *   positions [B][n_nodes], inv_freq [D / 2] (fp32), q_out [B, n_nodes, Hq, D],
+ *   K/V of node j of row b go to slot kv_len[b] + j of `kv`.
+ * Replaces apply_rotary_pos_emb + DynamicCache.update (torch.cat) inside
+ * the verify forward (transformers Qwen2/Llama attention, called from
+ * qwen_flashgrpo_wrapper.py:150-186).  dtype bf16/f16 rounds like the
+ * reference's half-precision arithmetic; f32 stays in f32. */
+fg_status fg_rope_kv_write(const void *qkv, int32_t dtype, const int32_t *positions, const float *inv_freq,
+                           float attention_scaling, int32_t B, int32_t n_nodes, int32_t n_q_heads,
+                           int32_t n_kv_heads, int32_t head_dim, const int32_t *kv_len, const fg_kv_layer *kv,
+                           void *q_out, void *stream);
+/* y = weight * (x * rsqrt(mean(x^2) + eps)) per row (Qwen2RMSNorm / LlamaRMSNorm). */
+fg_status fg_rmsnorm(const void *x, const void *weight, int32_t dtype, int32_t n_rows, int32_t dim, float eps,
+                     void *y, void *stream);
+/* y = layer_norm(x) * weight + bias per row (MEDUSA head norm, eps 1e-5). */
+fg_status fg_layernorm(const void *x, const void *weight, const void *bias, int32_t dtype, int32_t n_rows,
+                       int32_t dim, float eps, void *y, void *stream);
+/* out[r, :I] = silu(gu[r, :I]) * gu[r, I:2I] (SwiGLU of the MLP). */
+fg_status fg_silu_mul(const void *gu, int32_t dtype, int32_t n_rows, int32_t inter, void *out, void *stream);
+/* out = x + silu(y) (residual of MedusaPredictionHead.project_hidden,
+ * flashgrpo_b200/models/medusa_heads.py:240-244). */
+fg_status fg_silu_residual(const void *x, const void *y, int32_t dtype, int64_t n, void *out, void *stream);
+/* out[r] = src[idx[r]] for rows of `row_bytes` bytes (embedding lookup,
+ * internal-node hidden gather).  Rows must be 16-byte multiples. */
+fg_status fg_gather_rows(const void *src, int64_t src_row_stride_bytes, const int32_t *idx, int32_t n_rows,
+                         int64_t row_bytes, void *out, int64_t out_row_stride_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FG_B200_H_ */

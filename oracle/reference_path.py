@@ -243,7 +243,8 @@ def confidences(head_logits, metric="top1_prob", quantile=0.25):
     scores = []
     for lg in head_logits:
         if metric == "margin":
-            v = stable_topk(lg, min(2, lg.shape[-1]))[0]
+            # values only (tie order is irrelevant), subtracted in the logits dtype
+            v = torch.topk(lg, k=min(2, lg.shape[-1]), dim=-1).values
             s = v[..., 0] if v.shape[-1] == 1 else v[..., 0] - v[..., 1]
         else:
             top1 = lg.max(dim=-1).values.float()

@@ -1,0 +1,10 @@
+// fg_b200_lib.cu -- single translation unit of libfgb200.so.
+//
+// The kernels share one device-side error word, so they are compiled as one
+// unit (no relocatable device code is needed).
+#include "fg_abi.cu"
+#include "fg_sampling.cu"
+#include "fg_tree.cu"
+#include "fg_accept.cu"
+#include "fg_layers.cu"
+#include "fg_attention.cu"

@@ -1,0 +1,229 @@
+// fg_sampling.cu -- Philox uniforms, root-token sampling, row top-k.
+#include "fg_common.cuh"
+#include "fg_sampler.cuh"
+
+namespace fg {
+
+__global__ void philox_uniforms_kernel(uint64_t seed, const int32_t* __restrict__ seq_ids, int32_t n_rows,
+                                       int32_t round_idx, int32_t n_draws, float* __restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n_rows * n_draws) return;
+    const int32_t r = (int32_t)(i / n_draws), d = (int32_t)(i % n_draws);
+    out[i] = philox_uniform(seed, (uint32_t)seq_ids[r], (uint32_t)round_idx, (uint32_t)d);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(FG_SAMPLE_LANES) sample_rows_kernel(
+    const T* __restrict__ logits, int64_t row_stride, int32_t V, const float* __restrict__ uniforms,
+    int64_t u_stride, int32_t do_sample, float temperature, const int32_t* __restrict__ forced,
+    int32_t* __restrict__ out) {
+    __shared__ SampleSmem sm;
+    const int32_t r = blockIdx.x;
+    if (forced != nullptr && forced[r] >= 0) {
+        if (threadIdx.x == 0) out[r] = forced[r];
+        return;
+    }
+    const int32_t tok = block_sample<T>(logits + (int64_t)r * row_stride, V, temperature, do_sample != 0,
+                                        uniforms[(int64_t)r * u_stride], sm);
+    if (threadIdx.x == 0) out[r] = tok;
+}
+
+// ----------------------------------------------------------------- top-k
+constexpr int kTopkThreads = 256;
+
+__device__ __forceinline__ bool better(float av, int32_t ai, float bv, int32_t bi) {
+    return av > bv || (av == bv && ai < bi);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restrict__ logits, int64_t row_stride,
+                                                                int32_t V, int32_t k, int32_t* __restrict__ out_idx,
+                                                                float* __restrict__ out_val,
+                                                                float* __restrict__ out_max,
+                                                                float* __restrict__ out_lse, int32_t round_lse) {
+    __shared__ float sv[kTopkThreads][FG_MAX_TOPK + 1];
+    __shared__ int32_t si[kTopkThreads][FG_MAX_TOPK + 1];
+    __shared__ float redv[kTopkThreads / 32];
+    __shared__ int32_t redi[kTopkThreads / 32];
+    __shared__ float reds[kTopkThreads / 32];
+    __shared__ int32_t winner;
+    const int tid = threadIdx.x;
+    const T* row = logits + (int64_t)blockIdx.x * row_stride;
+    float v[FG_MAX_TOPK];
+    int32_t id[FG_MAX_TOPK];
+#pragma unroll
+    for (int j = 0; j < FG_MAX_TOPK; ++j) {
+        v[j] = -INFINITY;
+        id[j] = 0x7fffffff;
+    }
+    float m = -INFINITY, s = 0.0f;
+    for (int32_t i = tid; i < V; i += kTopkThreads) {
+        const float x = to_f<T>(row[i]);
+        // online max / sum of exp for the logsumexp
+        if (x > m) {
+            s = (m == -INFINITY) ? 0.0f : s * expf(m - x);
+            m = x;
+        }
+        if (x != -INFINITY) s += expf(x - m);
+        // insertion into the sorted local list; indices arrive increasing, so
+        // an equal value stays behind the earlier index
+        if (better(x, i, v[FG_MAX_TOPK - 1], id[FG_MAX_TOPK - 1])) {
+            float cv = x;
+            int32_t ci = i;
+#pragma unroll
+            for (int j = 0; j < FG_MAX_TOPK; ++j) {
+                if (better(cv, ci, v[j], id[j])) {
+                    const float tv = v[j];
+                    const int32_t ti = id[j];
+                    v[j] = cv;
+                    id[j] = ci;
+                    cv = tv;
+                    ci = ti;
+                }
+            }
+        }
+    }
+    // logsumexp across the block
+    float gm = warp_max(m);
+    if ((tid & 31) == 0) redv[tid >> 5] = gm;
+    __syncthreads();
+    if (tid == 0) {
+        float t = redv[0];
+        for (int w = 1; w < kTopkThreads / 32; ++w) t = fmaxf(t, redv[w]);
+        redv[0] = t;
+    }
+    __syncthreads();
+    gm = redv[0];
+    float ls = (m == -INFINITY) ? 0.0f : s * expf(m - gm);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if ((tid & 31) == 0) reds[tid >> 5] = ls;
+#pragma unroll
+    for (int j = 0; j < FG_MAX_TOPK; ++j) {
+        sv[tid][j] = v[j];
+        si[tid][j] = id[j];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < kTopkThreads / 32; ++w) tot += reds[w];
+        float lse = gm + logf(tot);
+        if (round_lse == FG_DTYPE_BF16) lse = __bfloat162float(__float2bfloat16_rn(lse));
+        if (round_lse == FG_DTYPE_F16) lse = __half2float(__float2half_rn(lse));
+        out_lse[blockIdx.x] = lse;
+        out_max[blockIdx.x] = gm;
+    }
+    // k rounds of "best head among all thread lists"
+    int head = 0;
+    for (int r = 0; r < k; ++r) {
+        float hv = head < k ? sv[tid][head] : -INFINITY;
+        int32_t hi = head < k ? si[tid][head] : 0x7fffffff;
+        float bv = hv;
+        int32_t bi = hi;
+        int bt = tid;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const int ot = __shfl_xor_sync(0xffffffffu, bt, o);
+            if (better(ov, oi, bv, bi) || (ov == bv && oi == bi && ot < bt)) {
+                bv = ov;
+                bi = oi;
+                bt = ot;
+            }
+        }
+        if ((tid & 31) == 0) {
+            redv[tid >> 5] = bv;
+            redi[tid >> 5] = bi;
+            reds[tid >> 5] = __int_as_float(bt);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float wv = redv[0];
+            int32_t wi = redi[0];
+            int wt = __float_as_int(reds[0]);
+            for (int w = 1; w < kTopkThreads / 32; ++w) {
+                const int t2 = __float_as_int(reds[w]);
+                if (better(redv[w], redi[w], wv, wi) || (redv[w] == wv && redi[w] == wi && t2 < wt)) {
+                    wv = redv[w];
+                    wi = redi[w];
+                    wt = t2;
+                }
+            }
+            winner = wt;
+            out_idx[(int64_t)blockIdx.x * k + r] = (wi == 0x7fffffff) ? 0 : wi;
+            out_val[(int64_t)blockIdx.x * k + r] = wv;
+        }
+        __syncthreads();
+        if (tid == winner) ++head;
+        __syncthreads();
+    }
+}
+
+}  // namespace fg
+
+using namespace fg;
+
+extern "C" fg_status fg_philox_uniforms(uint64_t seed, const int32_t* seq_ids, int32_t n_rows, int32_t round_idx,
+                                        int32_t n_draws, float* out, void* stream) {
+    if (n_rows < 0 || n_draws < 0 || (n_rows > 0 && n_draws > 0 && (!seq_ids || !out))) return FG_EINVAL;
+    const int64_t n = (int64_t)n_rows * n_draws;
+    if (n == 0) return FG_OK;
+    philox_uniforms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(seed, seq_ids, n_rows,
+                                                                                          round_idx, n_draws, out);
+    return launch_status();
+}
+
+extern "C" fg_status fg_sample_rows(const void* logits, int32_t dtype, int64_t row_stride, int32_t vocab,
+                                    int32_t n_rows, const float* uniforms, int64_t u_stride, int32_t do_sample,
+                                    float temperature, const int32_t* forced, int32_t* out_tokens, void* stream) {
+    if (n_rows == 0) return FG_OK;
+    if (!logits || !uniforms || !out_tokens || vocab <= 0 || n_rows < 0 || row_stride < vocab) return FG_EINVAL;
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (dtype) {
+        case FG_DTYPE_F32:
+            sample_rows_kernel<float><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
+                (const float*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, forced,
+                out_tokens);
+            break;
+        case FG_DTYPE_BF16:
+            sample_rows_kernel<__nv_bfloat16><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
+                (const __nv_bfloat16*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, forced,
+                out_tokens);
+            break;
+        case FG_DTYPE_F16:
+            sample_rows_kernel<__half><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
+                (const __half*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, forced,
+                out_tokens);
+            break;
+        default:
+            return FG_EINVAL;
+    }
+    return launch_status();
+}
+
+extern "C" fg_status fg_row_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t vocab,
+                                 int32_t n_rows, int32_t k, int32_t* out_idx, float* out_val, float* out_max,
+                                 float* out_lse, void* stream) {
+    if (n_rows == 0) return FG_OK;
+    if (!logits || !out_idx || !out_val || !out_max || !out_lse || vocab <= 0 || row_stride < vocab) return FG_EINVAL;
+    if (k <= 0 || k > FG_MAX_TOPK || k > vocab) return FG_ECAPACITY;
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (dtype) {
+        case FG_DTYPE_F32:
+            row_topk_kernel<float><<<n_rows, kTopkThreads, 0, st>>>((const float*)logits, row_stride, vocab, k,
+                                                                   out_idx, out_val, out_max, out_lse, dtype);
+            break;
+        case FG_DTYPE_BF16:
+            row_topk_kernel<__nv_bfloat16><<<n_rows, kTopkThreads, 0, st>>>(
+                (const __nv_bfloat16*)logits, row_stride, vocab, k, out_idx, out_val, out_max, out_lse, dtype);
+            break;
+        case FG_DTYPE_F16:
+            row_topk_kernel<__half><<<n_rows, kTopkThreads, 0, st>>>((const __half*)logits, row_stride, vocab, k,
+                                                                    out_idx, out_val, out_max, out_lse, dtype);
+            break;
+        default:
+            return FG_EINVAL;
+    }
+    return launch_status();
+}

@@ -1,0 +1,295 @@
+"""Torch-tensor wrappers of the C ABI (include/fg_b200.h).
+
+Each wrapper checks devices, dtypes and layouts, then calls the entry point
+on the tensor's current CUDA stream.  Nothing here computes on the host or
+falls back to PyTorch kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.FG_DTYPE_F32, torch.bfloat16: N.FG_DTYPE_BF16, torch.float16: N.FG_DTYPE_F16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError as exc:
+        raise TypeError(f"unsupported dtype {t.dtype}") from exc
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, name: str, dtype=None, contiguous=True):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the hot path has no CPU implementation)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _rows(t: torch.Tensor, name: str) -> tuple[int, int]:
+    """(row stride, vocab) of a 2-D tensor whose last dim is contiguous."""
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with a contiguous last dimension")
+    return t.stride(0), t.shape[1]
+
+
+# ----------------------------------------------------------------- sampling
+def philox_uniforms(seed: int, seq_ids: torch.Tensor, round_idx: int, n_draws: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    _need(seq_ids, "seq_ids", torch.int32)
+    n = seq_ids.shape[0]
+    if out is None:
+        out = torch.empty((n, n_draws), dtype=torch.float32, device=seq_ids.device)
+    N.call("fg_philox_uniforms", ctypes.c_uint64(seed & (2 ** 64 - 1)), _ptr(seq_ids), n, int(round_idx),
+           int(n_draws), _ptr(out), _stream(seq_ids))
+    return out
+
+
+def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool = True, temperature: float = 1.0,
+                forced: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fg-icdf-v1 draw per row; uniforms [n] or [n, k] (column 0 is used)."""
+    _need(logits, "logits", contiguous=False)
+    stride, vocab = _rows(logits, "logits")
+    _need(uniforms, "uniforms", torch.float32, contiguous=False)
+    u_stride = uniforms.stride(0) if uniforms.dim() == 2 else 1
+    n = logits.shape[0]
+    if forced is not None:
+        _need(forced, "forced", torch.int32)
+    if out is None:
+        out = torch.empty(n, dtype=torch.int32, device=logits.device)
+    N.call("fg_sample_rows", _ptr(logits), dtype_code(logits), stride, vocab, n, _ptr(uniforms), u_stride,
+           int(bool(do_sample)), float(temperature), _ptr(forced), _ptr(out), _stream(logits))
+    return out
+
+
+def row_topk(logits: torch.Tensor, k: int, out=None):
+    """(idx int32 [n,k], val f32 [n,k], row max f32 [n], logsumexp f32 [n])."""
+    _need(logits, "logits", contiguous=False)
+    stride, vocab = _rows(logits, "logits")
+    n = logits.shape[0]
+    dev = logits.device
+    if out is None:
+        out = (torch.empty((n, k), dtype=torch.int32, device=dev), torch.empty((n, k), dtype=torch.float32, device=dev),
+               torch.empty(n, dtype=torch.float32, device=dev), torch.empty(n, dtype=torch.float32, device=dev))
+    idx, val, mx, lse = out
+    N.call("fg_row_topk", _ptr(logits), dtype_code(logits), stride, vocab, n, int(k), _ptr(idx), _ptr(val), _ptr(mx),
+           _ptr(lse), _stream(logits))
+    return out
+
+
+# ---------------------------------------------------------------- planning
+def plan_params(*, tree_mode: str, active_batch_size: int, num_medusa_heads: int, cpeak_nodes: int,
+                min_tree_nodes_per_seq: int, max_tree_nodes_per_seq: int, max_tree_depth: int,
+                fixed_tree_topk_by_depth, adaptive_tree_enabled: bool = False, adaptive_min_topk_by_depth=(1, 1, 1),
+                adaptive_confidence_metric: str = "top1_prob", adaptive_confidence_quantile: float = 0.25,
+                adaptive_confidence_low: float = 0.15, adaptive_confidence_high: float = 0.45,
+                adaptive_depth_weight_decay: float = 0.5) -> N.PlanParams:
+    modes = {"fixed": 0, "concurrency_aware": 1, "explicit": 2}
+    if tree_mode not in modes:
+        raise ValueError(f"Unsupported tree_mode={tree_mode}")
+    p = N.PlanParams()
+    p.tree_mode = modes[tree_mode]
+    p.active_batch_size = int(active_batch_size)
+    p.num_medusa_heads = int(num_medusa_heads)
+    p.cpeak_nodes = int(cpeak_nodes)
+    p.min_tree_nodes_per_seq = int(min_tree_nodes_per_seq)
+    p.max_tree_nodes_per_seq = int(max_tree_nodes_per_seq)
+    p.max_tree_depth = int(max_tree_depth)
+    fixed = [int(k) for k in fixed_tree_topk_by_depth][: N.FG_MAX_DEPTHS]
+    p.n_fixed = len(fixed)
+    for i, k in enumerate(fixed):
+        p.fixed_topk[i] = k
+    p.adaptive = int(bool(adaptive_tree_enabled))
+    mins = [int(k) for k in adaptive_min_topk_by_depth][: N.FG_MAX_DEPTHS]
+    p.n_min = len(mins)
+    for i, k in enumerate(mins):
+        p.adaptive_min_topk[i] = k
+    if adaptive_confidence_metric not in ("top1_prob", "margin"):
+        raise ValueError(f"unknown adaptive_confidence_metric {adaptive_confidence_metric}")
+    p.confidence_metric = 1 if adaptive_confidence_metric == "margin" else 0
+    p.confidence_quantile = float(adaptive_confidence_quantile)
+    p.confidence_low = float(adaptive_confidence_low)
+    p.confidence_high = float(adaptive_confidence_high)
+    w = max(float(adaptive_depth_weight_decay), 1e-3)
+    for d in range(N.FG_MAX_DEPTHS):
+        p.depth_weight[d] = w ** d
+    p.log_gain[0] = 0.0
+    for v in range(1, 65):
+        p.log_gain[v] = math.log1p(v) - math.log(v)
+    return p
+
+
+def build_tree(params: N.PlanParams, root: torch.Tensor, cand_idx: torch.Tensor | None, cand_val, head_max,
+               head_lse, *, nmax: int, logits_dtype: torch.dtype, row_len: torch.Tensor, out: dict | None = None):
+    """K2.  cand_* are [n_heads, B, kmax]; returns a dict of device tensors."""
+    _need(root, "root", torch.int32)
+    _need(row_len, "row_len", torch.int32)
+    B = root.shape[0]
+    dev = root.device
+    if cand_idx is not None:
+        _need(cand_idx, "cand_idx", torch.int32)
+        n_heads, _, kmax = cand_idx.shape
+    else:
+        n_heads, kmax = 0, 1
+    if out is None:
+        i32 = dict(dtype=torch.int32, device=dev)
+        out = {"tokens": torch.empty((B, nmax), **i32), "positions": torch.empty((B, nmax), **i32),
+               "slot": torch.empty((B, nmax), **i32), "parents": torch.empty(nmax, **i32),
+               "depths": torch.empty(nmax, **i32), "anc": torch.empty((nmax, 4), **i32),
+               "internal": torch.empty(nmax, **i32), "plan": torch.empty(16, **i32)}
+    N.call("fg_build_tree", ctypes.byref(params), _ptr(root), _ptr(cand_idx), _ptr(cand_val), _ptr(head_max),
+           _ptr(head_lse), n_heads, kmax, B, nmax, _DTYPES[logits_dtype], _ptr(row_len), _ptr(out["tokens"]),
+           _ptr(out["positions"]), _ptr(out["slot"]), _ptr(out["parents"]), _ptr(out["depths"]), _ptr(out["anc"]),
+           _ptr(out["internal"]), _ptr(out["plan"]), _stream(root))
+    return out
+
+
+# --------------------------------------------------------------- attention
+def kv_layer(k: torch.Tensor, v: torch.Tensor) -> N.KvLayer:
+    if k.shape != v.shape or k.stride() != v.stride() or k.dim() != 4 or k.stride(3) != 1:
+        raise ValueError("K and V caches must be [B, Hkv, capacity, D] views with identical strides")
+    return N.KvLayer(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[2])
+
+
+def attention_workspace_bytes(B, n_nodes, n_q_heads, n_kv_heads, head_dim, *, num_splits=0, max_kv_len=0) -> int:
+    return int(N.load().fg_tree_attention_workspace_size(B, n_nodes, n_q_heads, n_kv_heads, head_dim, num_splits,
+                                                         max_kv_len))
+
+
+def tree_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: torch.Tensor,
+                   anc: torch.Tensor, *, scale: float, out: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None, num_splits: int = 0, max_kv_len: int = 0,
+                   kv: N.KvLayer | None = None) -> torch.Tensor:
+    """K3.  q [B, N, Hq, D]; caches [B, Hkv, cap, D]; anc int32 [N, 4] bits."""
+    _need(q, "q")
+    _need(kv_len, "kv_len", torch.int32)
+    _need(anc, "anc", torch.int32)
+    B, n_nodes, hq, D = q.shape
+    hkv = k_cache.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    if kv is None:
+        kv = kv_layer(k_cache, v_cache)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    N.call("fg_tree_attention", _ptr(q), dtype_code(q), ctypes.byref(kv), _ptr(kv_len), _ptr(anc), B, n_nodes, hq,
+           hkv, D, float(scale), _ptr(out), _ptr(workspace), ws_bytes, int(num_splits), int(max_kv_len), _stream(q))
+    return out
+
+
+# ------------------------------------------------------ accept + extraction
+def layer_pointer_arrays(k_layers, v_layers):
+    n = len(k_layers)
+    kp = (ctypes.c_uint64 * max(n, 1))(*[t.data_ptr() for t in k_layers])
+    vp = (ctypes.c_uint64 * max(n, 1))(*[t.data_ptr() for t in v_layers])
+    return kp, vp
+
+
+def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
+                   row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
+                   tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0):
+    """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
+    acc_len/correction/pending/last_node/finished [B]."""
+    _need(logits, "logits", contiguous=False)
+    stride, vocab = _rows(logits, "logits")
+    for name, t in (("slot", slot), ("tokens", tokens), ("parents", parents), ("row_len", row_len)):
+        _need(t, name, torch.int32)
+    _need(uniforms, "uniforms", torch.float32)
+    B, nmax = tokens.shape
+    a = N.AcceptArgs()
+    a.logits, a.logits_dtype, a.logits_row_stride, a.vocab = logits.data_ptr(), dtype_code(logits), stride, vocab
+    a.slot, a.tokens, a.parents = slot.data_ptr(), tokens.data_ptr(), parents.data_ptr()
+    a.parent_stride = 0 if parents_shared else nmax
+    a.n_nodes = _ptr(n_nodes)
+    a.n_nodes_shared = int(n_nodes_shared)
+    a.nmax = nmax
+    a.uniforms, a.u_stride = uniforms.data_ptr(), uniforms.stride(0)
+    a.B, a.do_sample, a.temperature = B, int(bool(do_sample)), float(temperature)
+    a.eos_id, a.max_length = int(eos_id), int(max_length)
+    a.row_len, a.update_len, a.active, a.dcap = row_len.data_ptr(), int(bool(update_len)), _ptr(active), int(dcap)
+    for key in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):
+        setattr(a, key, outputs[key].data_ptr())
+    kp = vp = None
+    if k_layers:
+        ref = k_layers[0]
+        kp, vp = layer_pointer_arrays(k_layers, v_layers)
+        a.n_layers = len(k_layers)
+        a.k_layers, a.v_layers = kp, vp
+        a.kv_elem_bytes, a.n_kv_heads, a.head_dim = ref.element_size(), ref.shape[1], ref.shape[3]
+        a.kv_stride_b, a.kv_stride_h, a.kv_stride_s = ref.stride(0), ref.stride(1), ref.stride(2)
+    if hidden_out is not None:
+        a.tree_hidden, a.hidden_out = tree_hidden.data_ptr(), hidden_out.data_ptr()
+        a.hidden_dim, a.hidden_elem_bytes = hidden_out.shape[-1], hidden_out.element_size()
+    N.call("fg_accept_extract", ctypes.byref(a), _stream(tokens))
+    return outputs
+
+
+def extract_path(k_layers, v_layers, row_len, acc_nodes, acc_len) -> None:
+    """In-place compaction of accepted slots for caches [B, Hkv, S, D]."""
+    ref = k_layers[0]
+    kp, vp = layer_pointer_arrays(k_layers, v_layers)
+    N.call("fg_extract_path", len(k_layers), kp, vp, ref.element_size(), ref.shape[0], ref.shape[1], ref.shape[3],
+           ref.stride(0), ref.stride(1), ref.stride(2), _ptr(row_len), _ptr(acc_nodes), _ptr(acc_len),
+           acc_nodes.shape[1], _stream(ref))
+
+
+# ------------------------------------------------------------- layer pieces
+def rope_kv_write(qkv, positions, inv_freq, attention_scaling, *, B, n_nodes, n_q_heads, n_kv_heads, head_dim,
+                  kv_len, k_cache, v_cache, q_out, kv: N.KvLayer | None = None):
+    if kv is None:
+        kv = kv_layer(k_cache, v_cache)
+    N.call("fg_rope_kv_write", _ptr(qkv), dtype_code(qkv), _ptr(positions), _ptr(inv_freq), float(attention_scaling),
+           B, n_nodes, n_q_heads, n_kv_heads, head_dim, _ptr(kv_len), ctypes.byref(kv), _ptr(q_out), _stream(qkv))
+    return q_out
+
+
+def rmsnorm(x, weight, eps, out=None):
+    out = torch.empty_like(x) if out is None else out
+    N.call("fg_rmsnorm", _ptr(x), _ptr(weight), dtype_code(x), x.numel() // x.shape[-1], x.shape[-1], float(eps),
+           _ptr(out), _stream(x))
+    return out
+
+
+def layernorm(x, weight, bias, eps, out=None):
+    out = torch.empty_like(x) if out is None else out
+    N.call("fg_layernorm", _ptr(x), _ptr(weight), _ptr(bias), dtype_code(x), x.numel() // x.shape[-1], x.shape[-1],
+           float(eps), _ptr(out), _stream(x))
+    return out
+
+
+def silu_mul(gu, out=None):
+    inter = gu.shape[-1] // 2
+    rows = gu.numel() // gu.shape[-1]
+    if out is None:
+        out = torch.empty((*gu.shape[:-1], inter), dtype=gu.dtype, device=gu.device)
+    N.call("fg_silu_mul", _ptr(gu), dtype_code(gu), rows, inter, _ptr(out), _stream(gu))
+    return out
+
+
+def silu_residual(x, y, out=None):
+    out = torch.empty_like(x) if out is None else out
+    N.call("fg_silu_residual", _ptr(x), _ptr(y), dtype_code(x), x.numel(), _ptr(out), _stream(x))
+    return out
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[r] = src[idx[r]] along dim 0 (rows contiguous)."""
+    row_bytes = src[0].numel() * src.element_size()
+    if out is None:
+        out = torch.empty((idx.shape[0], *src.shape[1:]), dtype=src.dtype, device=src.device)
+    N.call("fg_gather_rows", _ptr(src), src.stride(0) * src.element_size(), _ptr(idx), idx.shape[0], row_bytes,
+           _ptr(out), out.stride(0) * out.element_size(), _stream(src))
+    return out

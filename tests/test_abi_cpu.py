@@ -1,0 +1,65 @@
+"""CPU checks of the C ABI: the library loads and exports every declared symbol.
+
+No kernel is launched (this container has no GPU).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO
+
+
+def _declared_functions() -> list[str]:
+    text = (REPO / "include" / "fg_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_hot_path():
+    names = _declared_functions()
+    for must in ("fg_sample_rows", "fg_row_topk", "fg_build_tree", "fg_tree_attention", "fg_accept_extract",
+                 "fg_extract_path", "fg_rope_kv_write", "fg_philox_uniforms"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from flashgrpo_b200 import _native
+
+    lib = _native.load()
+    missing = [n for n in _declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_native.SIGNATURES) == set(_declared_functions())
+
+
+def test_host_only_entry_points():
+    from flashgrpo_b200 import _native
+
+    lib = _native.load()
+    assert lib.fg_version().decode().startswith("fg_b200")
+    assert lib.fg_status_string(_native.FG_ETIMEOUT).decode() == "device wait timed out"
+    # argument validation happens before any CUDA call
+    assert lib.fg_sample_rows(None, 1, 10, 10, 3, None, 1, 1, 1.0, None, None, None) == _native.FG_EINVAL
+    assert lib.fg_row_topk(ctypes.c_void_p(16), 1, 100, 100, 2, 99, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                           ctypes.c_void_p(16), ctypes.c_void_p(16), None) == _native.FG_ECAPACITY
+    assert lib.fg_tree_attention_workspace_size(64, 13, 12, 2, 128, 1, 1024) == 0
+    assert lib.fg_tree_attention_workspace_size(64, 13, 12, 2, 128, 2, 1024) > 0
+
+
+def test_plan_params_tables():
+    from flashgrpo_b200 import ops
+
+    p = ops.plan_params(tree_mode="concurrency_aware", active_batch_size=64, num_medusa_heads=3, cpeak_nodes=1024,
+                        min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16, max_tree_depth=4,
+                        fixed_tree_topk_by_depth=(4, 3, 2), adaptive_depth_weight_decay=0.5)
+    assert p.tree_mode == 1 and p.n_fixed == 3 and list(p.fixed_topk)[:3] == [4, 3, 2]
+    assert p.depth_weight[2] == 0.25
+    import math
+
+    assert p.log_gain[3] == math.log1p(3) - math.log(3)
+    with pytest.raises(ValueError):
+        ops.plan_params(tree_mode="sparse", active_batch_size=1, num_medusa_heads=1, cpeak_nodes=1,
+                        min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=2,
+                        fixed_tree_topk_by_depth=(1,))

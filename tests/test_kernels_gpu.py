@@ -1,0 +1,423 @@
+"""GPU parity of every hot-path kernel, called through the C ABI.
+
+Bit-exact against the CPU oracle: uniforms, sampling, top-k, tree build,
+acceptance walk and KV compaction.  Within stated tolerances against a plain
+PyTorch fp32 reference of the same op: tree attention, RoPE + KV write and
+the elementwise layer pieces.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cuda_available
+from oracle import native as orc
+from oracle import reference_path as rp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")]
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from flashgrpo_b200 import _native, ops as o
+
+    _native.load()
+    yield o
+    assert _native.read_device_error(clear=True) == 0
+
+
+def _to_np(t):
+    return t.detach().float().cpu().numpy()
+
+
+# ------------------------------------------------------------------ sampler
+def test_philox_uniforms_bit_exact(ops):
+    seq = torch.arange(0, 3000, 7, dtype=torch.int32, device=DEV)
+    u = ops.philox_uniforms(0xDEADBEEF12345, seq, 17, 5)
+    ref = orc.philox_uniforms(0xDEADBEEF12345, seq.cpu().numpy(), 17, 5)
+    assert np.array_equal(u.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("V,temp,scale", [(4096, 1.0, 8.0), (151936, 1.0, 2.0), (97, 0.7, 3.0), (128256, 1.3, 1.0)])
+def test_sample_rows_bit_exact(ops, dtype, V, temp, scale):
+    g = torch.Generator().manual_seed(V + int(temp * 10))
+    n = 24
+    logits = (torch.randn(n, V, generator=g) * scale).to(dtype)
+    u = torch.rand(n, generator=g)
+    u[0], u[1] = 0.0, 1.0 - 2 ** -24
+    got = ops.sample_rows(logits.to(DEV), u.to(DEV), temperature=temp).cpu().numpy()
+    ref = orc.sample_rows(logits.float().numpy(), u.numpy(), temperature=temp)
+    assert np.array_equal(got, ref)
+    greedy = ops.sample_rows(logits.to(DEV), u.to(DEV), do_sample=False).cpu().numpy()
+    assert np.array_equal(greedy, logits.float().argmax(-1).numpy())
+
+
+def test_sample_rows_forced_and_strided(ops):
+    logits = torch.randn(6, 3, 512).to(DEV)
+    view = logits[:, 1, :]  # row stride 1536
+    u = torch.rand(6, 4, device=DEV)
+    forced = torch.tensor([-1, 7, -1, -1, 3, -1], dtype=torch.int32, device=DEV)
+    got = ops.sample_rows(view, u, forced=forced).cpu().numpy()
+    ref = orc.sample_rows(_to_np(view), _to_np(u[:, 0]))
+    ref[1], ref[4] = 7, 3
+    assert np.array_equal(got, ref)
+
+
+def test_sampler_distribution_on_gpu(ops):
+    n = 60_000
+    logits = torch.log(torch.tensor([0.6, 0.4])).expand(n, 2).contiguous().to(DEV)
+    u = ops.philox_uniforms(456, torch.arange(n, dtype=torch.int32, device=DEV), 0, 1)
+    s = ops.sample_rows(logits, u).cpu()
+    freq = torch.bincount(s.long(), minlength=2).float() / n
+    assert torch.max(torch.abs(freq - torch.tensor([0.6, 0.4]))) < 0.015
+
+
+# ------------------------------------------------------------------- top-k
+@pytest.mark.parametrize("dtype,V,k", [(torch.bfloat16, 151936, 8), (torch.float32, 4096, 4), (torch.bfloat16, 97, 16),
+                                       (torch.float16, 128256, 3)])
+def test_row_topk_stable_and_lse(ops, dtype, V, k):
+    g = torch.Generator().manual_seed(V)
+    x = (torch.randn(20, V, generator=g) * 2).to(dtype)
+    x[3, :] = 0.5  # every entry tied
+    idx, val, mx, lse = ops.row_topk(x.to(DEV), k)
+    for r in range(x.shape[0]):
+        ri, rv = orc.topk_stable(x[r].float().numpy(), k)
+        assert np.array_equal(idx[r].cpu().numpy(), ri), r
+        assert np.array_equal(val[r].cpu().numpy(), rv), r
+    assert torch.equal(mx.cpu(), x.float().max(-1).values)
+    # fp32 logsumexp rounded to the logits dtype (torch's own fp16 reduction
+    # overflows to inf on a flat 128k row, which the kernel does not copy)
+    ref_lse = torch.logsumexp(x.to(DEV).float(), dim=-1).to(dtype).float().cpu()
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert torch.allclose(lse.cpu(), ref_lse, rtol=tol, atol=tol)
+
+
+# -------------------------------------------------------------- tree build
+def _check_tree(ops, *, tree_mode, B, cpeak, mx, depth, fixed, n_heads, V=300, adaptive=False, amin=(1, 1, 1),
+                metric="top1_prob", seed=0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    kw = dict(tree_mode=tree_mode, active_batch_size=B, num_medusa_heads=n_heads, cpeak_nodes=cpeak,
+              min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=mx, max_tree_depth=depth,
+              fixed_tree_topk_by_depth=list(fixed), adaptive_tree_enabled=adaptive,
+              adaptive_min_topk_by_depth=list(amin))
+    plan = rp.plan_tree(**kw)
+    head_logits = [(torch.randn(B, V, generator=g) * 3).to(dtype) for _ in range(max(plan.active_heads, 1))]
+    head_logits[0][0, :5] = 10.0  # a tie at the top of one row
+    root = torch.randint(0, V, (B,), generator=g, dtype=torch.int32)
+    row_len = torch.randint(5, 300, (B,), generator=g, dtype=torch.int32)
+    kmax = max(plan.topk_by_depth + [1])
+    n_h = plan.active_heads
+    cand = [ops.row_topk(h.to(DEV), kmax) for h in head_logits[:n_h]] if n_h else []
+    cand_idx = torch.stack([c[0] for c in cand]) if n_h else None
+    cand_val = torch.stack([c[1] for c in cand]) if n_h else None
+    hmax = torch.stack([c[2] for c in cand]) if n_h else None
+    hlse = torch.stack([c[3] for c in cand]) if n_h else None
+    params = ops.plan_params(adaptive_confidence_metric=metric, **kw)
+    nmax = 128
+    out = ops.build_tree(params, root.to(DEV), cand_idx, cand_val, hmax, hlse, nmax=nmax, logits_dtype=dtype,
+                         row_len=row_len.to(DEV))
+    torch.cuda.synchronize()
+    # oracle: same plan, same (optionally adapted) branching, stable top-k trees
+    oplan = plan
+    if adaptive and n_h:
+        conf = rp.confidences([h.float() if dtype == torch.float32 else h for h in head_logits[:n_h]], metric, 0.25)
+        adapted = [rp.topk_from_confidence(c, k, d, adaptive=True, min_topk_by_depth=amin, low=0.15, high=0.45)
+                   for d, (k, c) in enumerate(zip(plan.topk_by_depth, conf))]
+        adapted = rp.fit_topk_to_budget(adapted, plan.node_budget_per_seq, min_topk_by_depth=list(amin)[: len(adapted)])
+        oplan = rp.Plan(plan.node_budget_per_seq, len(adapted), adapted, rp.dense_node_count(adapted), plan.mode)
+    trees = rp.build_dense_trees(root.tolist(), [h.float() for h in head_logits[:n_h]], oplan)
+    pl = out["plan"].cpu().tolist()
+    n = trees[0].node_count
+    assert pl[0] == oplan.node_budget_per_seq
+    assert pl[10] == n
+    got_tok = out["tokens"].cpu().numpy()
+    for b, t in enumerate(trees):
+        assert got_tok[b, :n].tolist() == t.tokens, b
+    assert out["parents"][:n].tolist() == trees[0].parents
+    assert out["depths"][:n].tolist() == trees[0].depths
+    pos = out["positions"].cpu().numpy()
+    for b in range(B):
+        assert pos[b, :n].tolist() == [int(row_len[b]) + d - 1 for d in trees[0].depths]
+    _, mask, _, _ = rp.tree_attention_inputs(trees[:1], torch.ones(1, 1, dtype=torch.long), torch.tensor([1]),
+                                             pad_token_id=0, dtype=torch.float32)
+    allowed = (mask[0, 0, :, 1:] == 0).numpy()
+    anc = out["anc"].cpu().numpy().view(np.uint32)
+    for i in range(n):
+        bits = [(int(anc[i, j >> 5]) >> (j & 31)) & 1 for j in range(n)]
+        assert bits == allowed[i, :n].astype(int).tolist(), i
+    _, _, slots = rp.internal_logit_layout(trees)
+    assert np.array_equal(out["slot"].cpu().numpy()[:, :n], np.array(slots))
+    assert pl[11] == sum(1 for i in range(n) if trees[0].children.get(i))
+
+
+@pytest.mark.parametrize("case", [
+    dict(tree_mode="concurrency_aware", B=64, cpeak=1024, mx=16, depth=4, fixed=(4, 3, 2), n_heads=3),
+    dict(tree_mode="fixed", B=4, cpeak=0, mx=16, depth=4, fixed=(4, 2, 2), n_heads=3),
+    dict(tree_mode="concurrency_aware", B=16, cpeak=512, mx=32, depth=5, fixed=(3, 3, 2, 1), n_heads=4),
+    dict(tree_mode="concurrency_aware", B=2, cpeak=4096, mx=128, depth=6, fixed=(2, 2, 2, 2, 2), n_heads=5),
+    dict(tree_mode="concurrency_aware", B=256, cpeak=512, mx=10, depth=4, fixed=(4, 3, 2), n_heads=3),
+    dict(tree_mode="concurrency_aware", B=16, cpeak=512, mx=32, depth=4, fixed=(8, 8, 8), n_heads=3, adaptive=True,
+         amin=(2, 2, 2)),
+    dict(tree_mode="concurrency_aware", B=100, cpeak=3200, mx=32, depth=5, fixed=(8, 8, 8, 8), n_heads=4,
+         adaptive=True, amin=(1, 1, 1, 1), metric="margin"),
+    dict(tree_mode="concurrency_aware", B=8, cpeak=64, mx=16, depth=4, fixed=(4, 3, 2), n_heads=3,
+         dtype=torch.float32),
+])
+def test_build_tree_matches_oracle(ops, case):
+    _check_tree(ops, **case)
+
+
+# ------------------------------------------------ acceptance + compaction
+def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sample, temperature, row_len,
+                max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None):
+    B = tokens.shape[0]
+    outs = {k: torch.full((B, dcap), -9, dtype=torch.int32, device=DEV) for k in ("acc_tokens", "acc_nodes")}
+    for k in ("acc_len", "correction", "pending", "last_node", "finished"):
+        outs[k] = torch.full((B,), -9, dtype=torch.int32, device=DEV)
+    rl = row_len.clone()
+    ops.accept_extract(logits=logits, slot=slots, tokens=tokens, parents=parents, n_nodes=n_nodes,
+                       uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
+                       max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=False,
+                       k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out)
+    torch.cuda.synchronize()
+    return outs, rl
+
+
+def test_accept_matches_reference_fixture(ops, golden_dir):
+    g = np.load(golden_dir / "accept.npz")
+    for c in sorted({k.split("_")[0] for k in g.files}):
+        V, B, nmax, do_sample = g[c + "_meta"].tolist()
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+        outs, _ = _run_accept(ops, t(g[c + "_logits"]), t(g[c + "_slots"]), t(g[c + "_tokens"]),
+                              t(g[c + "_parents"]), t(g[c + "_n_nodes"]), t(g[c + "_uniforms"]),
+                              do_sample=bool(do_sample), temperature=float(g[c + "_temp"][0]),
+                              row_len=torch.zeros(B, dtype=torch.int32, device=DEV), dcap=5)
+        assert np.array_equal(outs["acc_tokens"].cpu().numpy(), g[c + "_acc_tokens"]), c
+        assert np.array_equal(outs["acc_nodes"].cpu().numpy(), g[c + "_acc_nodes"]), c
+        assert np.array_equal(outs["correction"].cpu().numpy(), g[c + "_correction"]), c
+        assert np.array_equal(outs["last_node"].cpu().numpy(), g[c + "_parent"]), c
+
+
+@pytest.mark.parametrize("dtype,V,B,peak", [(torch.bfloat16, 151936, 64, 6.0), (torch.float32, 4096, 12, 8.0),
+                                            (torch.float16, 1000, 33, 5.0)])
+def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak):
+    g = torch.Generator().manual_seed(V + B)
+    plan = rp.Plan(16, 3, [4, 2, 2], 0, "fixed")
+    heads = [(torch.randn(B, V, generator=g) * peak).to(dtype).float() for _ in range(3)]
+    root = torch.randint(0, V, (B,), generator=g)
+    trees = rp.build_dense_trees(root.tolist(), heads, plan)
+    n = trees[0].node_count
+    rows, nodes, slots = rp.internal_logit_layout(trees)
+    packed = torch.stack([heads[min(trees[r].depths[nd] - 1, 2)][r] for r, nd in zip(rows, nodes)])
+    packed = (packed + torch.randn(packed.shape, generator=g) * 0.3).to(dtype)
+    tok = torch.tensor([t.tokens for t in trees], dtype=torch.int32)
+    par = torch.tensor([t.parents for t in trees], dtype=torch.int32)
+    U = torch.rand(B, 6, generator=g)
+    row_len = torch.randint(40, 60, (B,), generator=g, dtype=torch.int32)
+    max_length = 58
+    eos = int(tok[0, 1])
+    # caches: 3 layers, [B, 2, cap, 128]
+    cap = 96
+    kl = [torch.randn(B, 2, cap, 128, generator=g).to(torch.bfloat16).to(DEV) for _ in range(3)]
+    vl = [torch.randn(B, 2, cap, 128, generator=g).to(torch.bfloat16).to(DEV) for _ in range(3)]
+    k_np = [k.view(torch.int16).cpu().numpy().copy() for k in kl]
+    v_np = [v.view(torch.int16).cpu().numpy().copy() for v in vl]
+    hidden = torch.randn(B, n, 64, generator=g).to(DEV)
+    hout = torch.zeros(B, 64, device=DEV)
+    outs, rl = _run_accept(ops, packed.to(DEV), torch.tensor(slots, dtype=torch.int32).to(DEV), tok.to(DEV),
+                           par.to(DEV), torch.full((B,), n, dtype=torch.int32, device=DEV), U.to(DEV),
+                           do_sample=True, temperature=1.0, row_len=row_len.to(DEV), max_length=max_length, eos=eos,
+                           dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout)
+    ref = orc.accept_walk(packed.float().numpy(), np.array(slots), tok.numpy(), par.numpy(), np.full(B, n), U.numpy(),
+                          do_sample=True, temperature=1.0, eos_id=eos, max_length=max_length,
+                          row_len=row_len.numpy(), dcap=8)
+    for k in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):
+        assert np.array_equal(outs[k].cpu().numpy(), ref[k]), k
+    assert np.array_equal(rl.cpu().numpy(), row_len.numpy() + ref["acc_len"])
+    orc.extract_path(k_np, v_np, row_len.numpy(), ref["acc_nodes"], ref["acc_len"])
+    for li in range(3):
+        assert np.array_equal(kl[li].view(torch.int16).cpu().numpy(), k_np[li]), li
+        assert np.array_equal(vl[li].view(torch.int16).cpu().numpy(), v_np[li]), li
+    want_h = hidden[torch.arange(B), torch.from_numpy(ref["last_node"]).long().to(DEV)]
+    assert torch.equal(hout, want_h)
+
+
+def test_extract_path_standalone_matches_reference_fixture(ops, golden_dir):
+    g = np.load(golden_dir / "extract.npz")
+    for c in sorted({k.split("_")[0] for k in g.files}):
+        B, H, old, n, D, is_bf16 = g[c + "_meta"].tolist()
+        paths = g[c + "_paths"]
+        lens = (paths >= 0).sum(1).astype(np.int32)
+        conv = (lambda a: torch.from_numpy(a).view(torch.bfloat16)) if is_bf16 else torch.from_numpy
+        ks = [conv(g[c + f"_k{i}"].copy()).to(DEV) for i in range(2)]
+        vs = [conv(g[c + f"_v{i}"].copy()).to(DEV) for i in range(2)]
+        if (D * ks[0].element_size()) % 16:
+            continue
+        ops.extract_path(ks, vs, torch.full((B,), old, dtype=torch.int32, device=DEV),
+                         torch.from_numpy(np.where(paths < 0, 0, paths).astype(np.int32)).to(DEV),
+                         torch.from_numpy(lens).to(DEV))
+        torch.cuda.synchronize()
+        for i in range(2):
+            rk = conv(g[c + f"_rk{i}"].copy())
+            rv = conv(g[c + f"_rv{i}"].copy())
+            for b in range(B):
+                a = old + lens[b]
+                assert torch.equal(ks[i][b, :, :a].cpu(), rk[b, :, :a]), (c, i, b)
+                assert torch.equal(vs[i][b, :, :a].cpu(), rv[b, :, :a]), (c, i, b)
+
+
+# ---------------------------------------------------------- tree attention
+def _random_tree(n, g):
+    parents = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)]
+    return rp.Tree(list(range(n)), parents, [1] * n)
+
+
+def _anc_bits(tree, n):
+    bits = torch.zeros(n, 4, dtype=torch.int64)
+    for i in range(n):
+        for a in tree.ancestors_including_self(i):
+            bits[i, a >> 5] |= 1 << (a & 31)
+    return (bits & 0xFFFFFFFF).to(torch.int64).numpy().astype(np.uint32).view(np.int32)
+
+
+def _attn_reference(q, k, v, kv_len, tree, scale):
+    """fp32 eager attention with the reference's additive mask, per row."""
+    B, n, hq, D = q.shape
+    hkv = k.shape[1]
+    G = hq // hkv
+    out = torch.zeros(B, n, hq, D, dtype=torch.float32, device=q.device)
+    allowed_tree = torch.zeros(n, n, dtype=torch.bool)
+    for i in range(n):
+        for a in tree.ancestors_including_self(i):
+            allowed_tree[i, a] = True
+    for b in range(B):
+        L = int(kv_len[b])
+        kk = k[b, :, : L + n].float().repeat_interleave(G, 0)  # [hq, T, D]
+        vv = v[b, :, : L + n].float().repeat_interleave(G, 0)
+        qq = q[b].float().transpose(0, 1)  # [hq, n, D]
+        s = torch.matmul(qq, kk.transpose(1, 2)) * scale
+        mask = torch.cat([torch.ones(n, L, dtype=torch.bool), allowed_tree], 1).to(q.device)
+        s = s.masked_fill(~mask, torch.finfo(torch.float32).min)
+        out[b] = torch.matmul(torch.softmax(s, -1), vv).transpose(0, 1)
+    return out
+
+
+@pytest.mark.parametrize("B,n,hq,hkv,L,splits", [
+    (8, 13, 12, 2, 1024, 0), (8, 13, 12, 2, 1024, 1), (4, 13, 12, 2, 700, 3), (6, 32, 28, 4, 517, 0),
+    (2, 64, 32, 8, 300, 2), (3, 128, 32, 8, 129, 0), (1, 16, 32, 8, 4000, 0), (5, 1, 12, 2, 63, 0),
+    (2, 8, 8, 8, 0, 0),
+])
+def test_tree_attention_bf16(ops, B, n, hq, hkv, L, splits):
+    g = torch.Generator().manual_seed(B * 1000 + n)
+    D = 128
+    cap = L + n + 40
+    kv_len = torch.randint(max(L - 60, 0), L + 1, (B,), generator=g, dtype=torch.int32)
+    k = torch.randn(B, hkv, cap, D, generator=g).to(torch.bfloat16).to(DEV)
+    v = torch.randn(B, hkv, cap, D, generator=g).to(torch.bfloat16).to(DEV)
+    q = torch.randn(B, n, hq, D, generator=g).to(torch.bfloat16).to(DEV)
+    tree = _random_tree(n, g)
+    anc = torch.from_numpy(_anc_bits(tree, n)).to(DEV)
+    ws_bytes = ops.attention_workspace_bytes(B, n, hq, hkv, D, num_splits=splits, max_kv_len=int(kv_len.max()))
+    ws = torch.zeros(max(ws_bytes, 16) // 4 + 4, dtype=torch.int32, device=DEV)
+    scale = D ** -0.5
+    out = ops.tree_attention(q, k, v, kv_len.to(DEV), anc, scale=scale, workspace=ws, num_splits=splits,
+                             max_kv_len=int(kv_len.max()))
+    ref = _attn_reference(q, k, v, kv_len, tree, scale)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(ref.abs().max().item(), 1e-3), err
+    # a second call reuses the (self-resetting) workspace
+    out2 = ops.tree_attention(q, k, v, kv_len.to(DEV), anc, scale=scale, workspace=ws, num_splits=splits,
+                              max_kv_len=int(kv_len.max()))
+    assert torch.equal(out, out2)
+
+
+def test_tree_attention_f32(ops):
+    g = torch.Generator().manual_seed(3)
+    B, n, hq, hkv, D, L = 4, 13, 4, 2, 64, 128
+    k = torch.randn(B, hkv, L + n, D, generator=g).to(DEV)
+    v = torch.randn(B, hkv, L + n, D, generator=g).to(DEV)
+    q = torch.randn(B, n, hq, D, generator=g).to(DEV)
+    kv_len = torch.full((B,), L, dtype=torch.int32)
+    tree = _random_tree(n, g)
+    anc = torch.from_numpy(_anc_bits(tree, n)).to(DEV)
+    out = ops.tree_attention(q, k, v, kv_len.to(DEV), anc, scale=D ** -0.5)
+    ref = _attn_reference(q.double(), k.double(), v.double(), kv_len, tree, D ** -0.5)
+    rel = ((out - ref).abs().max() / ref.abs().max()).item()
+    assert rel < 1e-5, rel
+
+
+# ------------------------------------------------------------ layer pieces
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rope_kv_write_matches_hf(ops, dtype):
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+
+    g = torch.Generator().manual_seed(5)
+    B, n, hq, hkv, D, cap = 3, 13, 12, 2, 128, 300
+    qkv = torch.randn(B * n, (hq + 2 * hkv) * D, generator=g).to(dtype).to(DEV)
+    kv_len = torch.tensor([100, 7, 250], dtype=torch.int32, device=DEV)
+    positions = (kv_len[:, None] + torch.randint(0, 4, (1, n), generator=g).to(DEV)).to(torch.int32)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    kc = torch.zeros(B, hkv, cap, D, dtype=dtype, device=DEV)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(B, n, hq, D, dtype=dtype, device=DEV)
+    ops.rope_kv_write(qkv, positions, inv_freq.to(DEV), 1.0, B=B, n_nodes=n, n_q_heads=hq, n_kv_heads=hkv,
+                      head_dim=D, kv_len=kv_len, k_cache=kc, v_cache=vc, q_out=q_out)
+    # HF reference: cos/sin in fp32 -> activation dtype, rotate in that dtype
+    freqs = positions.float()[..., None] * inv_freq.to(DEV)
+    emb = torch.cat([freqs, freqs], -1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)  # [B, n, D]
+    x = qkv.view(B, n, hq + 2 * hkv, D).transpose(1, 2)
+    qr, kr = apply_rotary_pos_emb(x[:, :hq], x[:, hq:hq + hkv], cos, sin)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert torch.allclose(q_out.float(), qr.transpose(1, 2).float(), atol=tol, rtol=tol)
+    for b in range(B):
+        L = int(kv_len[b])
+        assert torch.allclose(kc[b, :, L:L + n].float(), kr[b].float(), atol=tol, rtol=tol)
+        assert torch.equal(vc[b, :, L:L + n], x[b, hq + hkv:])
+        assert torch.count_nonzero(kc[b, :, :L]) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_norms_and_activations(ops, dtype):
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(37, 1536, generator=g).to(dtype).to(DEV)
+    w = (torch.rand(1536, generator=g) + 0.5).to(dtype).to(DEV)
+    bias = torch.randn(1536, generator=g).to(dtype).to(DEV)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    var = x.float().pow(2).mean(-1, keepdim=True)
+    ref = w * (x.float() * torch.rsqrt(var + 1e-6)).to(dtype)
+    assert torch.allclose(ops.rmsnorm(x, w, 1e-6).float(), ref.float(), atol=tol, rtol=tol)
+    ref_ln = torch.nn.functional.layer_norm(x.float(), (1536,), w.float(), bias.float(), 1e-5)
+    assert torch.allclose(ops.layernorm(x, w, bias, 1e-5).float(), ref_ln, atol=tol * 4, rtol=tol)
+    gu = torch.randn(37, 2 * 700, generator=g).to(dtype).to(DEV)
+    ref_sm = torch.nn.functional.silu(gu[:, :700]) * gu[:, 700:]
+    assert torch.allclose(ops.silu_mul(gu).float(), ref_sm.float(), atol=tol, rtol=tol)
+    y = torch.randn_like(x)
+    assert torch.allclose(ops.silu_residual(x, y).float(), (x + torch.nn.functional.silu(y)).float(), atol=tol,
+                          rtol=tol)
+    idx = torch.tensor([3, 0, 36, 3], dtype=torch.int32, device=DEV)
+    assert torch.equal(ops.gather_rows(x, idx), x[idx.long()])
+
+
+def test_bounded_wait_times_out_and_context_survives(ops):
+    from flashgrpo_b200 import _native
+
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    _native.call("fg_wait_flag", flag.data_ptr(), 20_000_000, status.data_ptr(),
+                 torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(status) == _native.FG_ETIMEOUT
+    assert _native.read_device_error(clear=True) == _native.FG_ETIMEOUT
+    flag.fill_(1)
+    _native.call("fg_wait_flag", flag.data_ptr(), 20_000_000, status.data_ptr(),
+                 torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert int(status) == _native.FG_OK
+    assert (torch.ones(4, device=DEV) * 2).sum().item() == 8.0
