@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Accepted tokens/sec of the MEDUSA tree-verify round on B200.
+
+Workload (the benchmark's config 2): Qwen2.5-1.5B-shaped random-init policy
+(bf16, 28 layers, hidden 1536, 12/2 heads, head_dim 128, vocab 151936),
+3 tied MEDUSA heads, 64 rollouts per GPU (8 prompts x 8 samples), 1024-token
+uniform-random prefixes, concurrency-aware trees (cpeak_nodes 1024, at most
+16 nodes -> plan [4, 2], 13 nodes, 2 active heads), temperature 1.0.
+
+A step is one verify round over the rows: proposal GEMM + root sampling +
+candidate top-k, tree build, 28-layer verify forward with tree attention,
+internal-node lm_head, exact_target acceptance + extract_path compaction,
+replayed from a CUDA graph.  `value` = accepted tokens of all ranks / the
+slowest rank's device time (CUDA events) over `--steps` steps.  Inputs are
+larger than L2 (3.1 GB of weights and a 3.7 GB KV cache are read per step).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "ss-grpo_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "accepted tokens/sec per box at 1/2/4/8 B200; tree-attn HBM GB/s vs peak"
+UNIT = "accepted tokens/s"
+WORKLOAD = "config 2: Qwen2.5-1.5B-shaped MEDUSA tree-verify round"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rows", type=int, default=64, help="rollouts per GPU (prompts x 8)")
+    ap.add_argument("--prefix", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
+    ap.add_argument("--e2e-calls", type=int, default=2)
+    ap.add_argument("--e2e-new", type=int, default=32)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-splits", type=int, default=0)
+    return ap.parse_args()
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic() -> float | None:
+    """dram read+write bytes per tree-attention launch from the committed ncu summary."""
+    p = REPO / "profiles" / "tree_attention_config2.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch_full_model"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = REPO / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------- workload
+def config2_decoder(device, layers=None, attn_splits=0):
+    import torch
+
+    from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
+    from flashgrpo_b200.utils import synthetic
+
+    over = {} if layers is None else {"layers": layers}
+    model = synthetic.build_model(2, device=device, attn_implementation="sdpa", **over)
+    heads = synthetic.medusa_head_tensors(2, device=device)
+
+    class Tok:
+        pad_token_id = 0
+        eos_token_id = 1
+
+    cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode="concurrency_aware", cpeak_nodes=1024,
+                            max_tree_nodes_per_seq=16, max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2),
+                            temperature=1.0, top_p=1.0, sampling_seed=1234, attention_splits=attn_splits)
+    torch.cuda.synchronize()
+    return FlashMedusaDecoder(model, heads, Tok(), cfg)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from flashgrpo_b200 import _native
+    from flashgrpo_b200.engine.verify import DecodeState  # noqa: F401
+    from flashgrpo_b200.utils import synthetic
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    torch.manual_seed(0)
+    dec = config2_decoder(device, args.layers, args.attn_splits)
+    eng = dec.engine
+    spec = eng.spec
+    prompts = max(1, args.rows // 8)
+    rows = prompts * 8
+    ids, mask = synthetic.random_prompts(prompts, args.prefix, spec.vocab, seed=100 + rank)
+    W, K = max(args.warmup, 3), max(args.steps, 1)
+    capacity = args.prefix + 3 * (W + K + 8) + 32
+    n_heads = dec.max_heads()
+    rcfg = dec.round_config(max_length=1 << 30)
+    with torch.inference_mode():
+        st = eng.prefill(ids, mask, repeats=8, capacity=capacity, n_heads=n_heads)
+        plan = dec._plan(rows)
+        rb = eng.buffers(rows, plan, plan.active_heads, plan.active_heads + 2)
+        params = dec._params(rows)
+        # warm-up round 1 eagerly (lazy cuBLAS / allocator state), counting our launches
+        before = _native.launches
+        eng.run_round(st, rb, params, rcfg)
+        launches_per_step = _native.launches - before
+        torch.cuda.synchronize()
+        # G graphs in rotation, each with its own per-layer attention events
+        G = min(4, K)
+        events = [[(torch.cuda.Event(enable_timing=True, external=True),
+                    torch.cuda.Event(enable_timing=True, external=True)) for _ in range(spec.n_layers)]
+                  for _ in range(G)]
+        graphs = []
+        pool = None
+        for gi in range(G):
+            g = eng.graph_round(st, rb, params, rcfg, pool=pool, attn_events=events[gi])
+            pool = g.pool()
+            graphs.append(g)
+        for i in range(W - 1):
+            graphs[i % G].replay()
+        torch.cuda.synchronize()
+        acc0 = int(rb.acc_sum.item())
+        len0 = st.row_len.float().mean().item()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            t_start.record()
+            for i in range(K):
+                graphs[i % G].replay()
+            t_end.record()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = t_start.elapsed_time(t_end)
+        accepted = int(rb.acc_sum.item()) - acc0
+        len1 = st.row_len.float().mean().item()
+        # the last G steps' attention launches (one per layer)
+        attn_ms = [events[(K - 1 - j) % G][l][0].elapsed_time(events[(K - 1 - j) % G][l][1])
+                   for j in range(G) for l in range(spec.n_layers)]
+        err = _native.read_device_error(clear=True)
+        if err:
+            raise RuntimeError(f"device error word {err} after the timed region")
+        # the one collective: every rank's per-rollout generated lengths (for
+        # the GRPO group statistics), then totals and the slowest clock
+        rollout_len = (st.row_len - args.prefix).clone()
+        if world > 1:
+            gathered = [torch.empty_like(rollout_len) for _ in range(world)]
+            dist.all_gather(gathered, rollout_len)
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_max = float(t.item())
+            a = torch.tensor([accepted], device=device, dtype=torch.int64)
+            dist.all_reduce(a)
+            accepted_all = int(a.item())
+        else:
+            ms_max, accepted_all = ms, accepted
+        del graphs
+        # ---- roofline of the tree-attention kernel (K3)
+        N_ = rb.N
+        L_avg = 0.5 * (len0 + len1)
+        hq, hkv, D = spec.n_q_heads, spec.n_kv_heads, spec.head_dim
+        attn_bytes = rows * hkv * (L_avg + N_) * D * 2 * 2 + rows * N_ * hq * D * 2 * 2
+        attn_avg_ms = statistics.mean(attn_ms)
+        achieved = attn_bytes / (attn_avg_ms * 1e-3) / 1e9
+        peak, peak_kind = measured_peaks()
+        traffic = profile_traffic()
+        # ---- end-to-end through the public generate() API (prompts H2D, tokens D2H)
+        e2e = None
+        if not args.no_e2e and args.e2e_calls > 0:
+            e_ids = ids.pin_memory()
+            e_mask = mask.pin_memory()
+            dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + 4)  # warm
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            tok, rounds_total = 0, 0
+            for _ in range(args.e2e_calls):
+                res = dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + args.e2e_new)
+                tok += res["total_acc_length"]
+                rounds_total += res["total_verify_rounds"]
+            torch.cuda.synchronize()
+            e_s = time.perf_counter() - t0
+            if world > 1:
+                t = torch.tensor([e_s], device=device, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                e_s = float(t.item())
+                a = torch.tensor([tok], device=device, dtype=torch.int64)
+                dist.all_reduce(a)
+                tok = int(a.item())
+            dcap = plan.active_heads + 2
+            e2e = {"value": tok / e_s, "unit": UNIT,
+                   "h2d_bytes_per_step": int(ids.numel() * 8 + mask.numel() * 8),
+                   "d2h_bytes_per_step": int(rounds_total / args.e2e_calls * rows * (3 + dcap) * 4),
+                   "step": f"one generate() call: {prompts} prompts x {args.prefix} tokens prefilled, x8 samples, "
+                           f"{args.e2e_new} new tokens per row",
+                   "calls": args.e2e_calls}
+    result = {
+        "metric": METRIC, "value": accepted_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids",
+        "config": {"workload": WORKLOAD, "rollouts_per_gpu": rows, "prompts_per_gpu": prompts,
+                   "samples_per_prompt": 8, "prefix_tokens": args.prefix, "tree": plan.topk_by_depth,
+                   "tree_nodes": rb.N, "layers": spec.n_layers, "medusa_heads": 3, "active_heads": plan.active_heads,
+                   "temperature": 1.0, "top_p": 1.0, "parallelism": f"dp{world} (rollouts sharded by prompt group)",
+                   "l2": "inputs larger than L2: 3.1 GB weights + KV cache re-read every step",
+                   "graphs": "each step replays a captured CUDA graph of the round"},
+        "accepted_tokens": accepted_all, "average_accept_length": accepted_all / (K * rows * world),
+        "gpu_launches": launches_per_step * K,
+        "roofline": {"kernel": "fg_tree_attention (tree_attn_bf16_kernel)", "bound": "hbm",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback", "traffic": traffic,
+                     "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": attn_avg_ms,
+                     "launches_timed": len(attn_ms)},
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        result["e2e"] = e2e
+    return result
+
+
+# ------------------------------------------------------------- CPU oracle
+def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 4, prefix: int = 256):
+    """The oracle's restatement of the reference generate loop, on the host
+    cores, on a bounded sample of the config-2 workload (fp32, `rows` rollouts
+    of `prefix`-token prompts)."""
+    import torch
+
+    from oracle import reference_path as rp
+    from flashgrpo_b200.utils import synthetic
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = synthetic.build_model(2, device="cpu", dtype=torch.float32, attn_implementation="eager")
+    st = synthetic.medusa_head_tensors(2, dtype=torch.float32)
+    heads = [{"norm_w": st[f"heads.{i}.norm.weight"], "norm_b": st[f"heads.{i}.norm.bias"],
+              "fc_w": st[f"heads.{i}.fc.weight"], "fc_b": st[f"heads.{i}.fc.bias"]} for i in range(3)]
+    prompts = max(1, rows // 2)
+    ids, mask = synthetic.random_prompts(prompts, prefix, 151936, seed=7)
+    cfg = rp.OracleConfig(tree_mode="concurrency_aware", cpeak_nodes=1024 * rows // 64, max_tree_nodes_per_seq=16,
+                          max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2))
+    res = rp.generate(model, heads, ids, mask, cfg, rp.SeqRoundSampler(1234), repeats=2,
+                      max_length=prefix + warm_rounds + timed_rounds)
+    times = res["round_times"][warm_rounds:warm_rounds + timed_rounds]
+    sec = sum(t for t, _ in times)
+    tok = sum(n for _, n in times)
+    return {"value": tok / sec, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} verify rounds of {rows} rollouts ({prompts} prompts x 2 samples) with "
+                      f"{prefix}-token prefixes, fp32 on the host; oracle/reference_path.py restatement of the "
+                      "reference generate loop with HF eager attention and the dense tree mask",
+            "seconds": sec}
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        W, K = max(args.warmup, 3), max(args.steps, 1)
+        base = cpu_oracle_round_rate(W, K)
+        line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": K, "warmup": W, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids",
+                "config": {"workload": WORKLOAD, "sample": base["sample"]},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
+    try:
+        result = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_oracle_round_rate(1, 4)
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

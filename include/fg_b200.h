@@ -79,10 +79,12 @@ fg_status fg_read_device_error(int32_t *host_out, int32_t clear);
 fg_status fg_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *status_out, void *stream);
 
 /* ------------------------------------------------------------- sampling */
-/* out[r * n_draws + d] = u(seed, seq_ids[r], round_idx, d).  Draw 0 is the
- * root sample of a round, draw 1 + s is acceptance step s. */
+/* out[r * n_draws + d] = u(seed, seq_ids[r], round, d) with
+ * round = round_idx + (round_dev ? *round_dev : 0); round_dev (nullable,
+ * device int32) lets a captured CUDA graph advance the round on the device.
+ * Draw 0 is the root sample of a round, draw 1 + s is acceptance step s. */
 fg_status fg_philox_uniforms(uint64_t seed, const int32_t *seq_ids, int32_t n_rows, int32_t round_idx,
-                             int32_t n_draws, float *out, void *stream);
+                             const int32_t *round_dev, int32_t n_draws, float *out, void *stream);
 
 /* One fg-icdf-v1 token per row of logits [n_rows, row_stride] (dtype
  * FG_DTYPE_*), uniform uniforms[r * u_stride].  forced (nullable): rows with

@@ -439,6 +439,10 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
     ``heads`` is a list of dicts with norm_w, norm_b, fc_w, fc_b tensors.
     ``record`` (a list) receives one RoundRecord per verify round.
     """
+    import time
+
+    t_start = time.perf_counter()
+    round_times = []
     lm_w = model.lm_head.weight
     # prefill (wrapper.py:189-199): positions from the mask, fresh cache
     pos = (attention_mask.long().cumsum(-1) - 1).masked_fill(attention_mask == 0, 0)
@@ -465,7 +469,9 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
     stats = dict(total_acc_length=0, total_decoded_token_num=0, total_verify_rounds=0, total_correction_tokens=0,
                  total_accepted_medusa_tokens=0, total_proposed_medusa_tokens=0)
     round_idx = 0
+    prefill_time = time.perf_counter() - t_start
     while active_ids:
+        t_round = time.perf_counter()
         B = len(active_ids)
         remaining = (max_length - logical).tolist()
         old_lens = logical.tolist()
@@ -583,5 +589,7 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
             logical = logical.index_select(0, kt)
             active_ids = [active_ids[r] for r in keep]
         round_idx += 1
+        round_times.append((time.perf_counter() - t_round, sum(len(t) for t in acc)))
     stats["average_accept_length"] = stats["total_acc_length"] / max(stats["total_decoded_token_num"], 1)
-    return {"generated_token_ids": generated, **stats}
+    return {"generated_token_ids": generated, **stats, "prefill_time": prefill_time,
+            "round_times": round_times}

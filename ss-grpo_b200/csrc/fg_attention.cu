@@ -72,24 +72,34 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Returns false when the phase did not complete within kWaitNs.
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Returns false when the phase did not complete within kWaitNs.  The clock
+// is only read once the barrier has stayed closed for a while, so the
+// common path is a plain try_wait loop.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t addr = smem_u32(bar);
-    uint64_t start = 0;
+    for (int it = 0; it < 4096; ++it)
+        if (mbar_try(addr, parity)) return true;
+    const uint64_t start = now_ns();
     for (uint32_t it = 0;; ++it) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if ((it & 255u) == 0u) {
-            const uint64_t t = now_ns();
-            if (start == 0) start = t;
-            else if ((int64_t)(t - start) > kWaitNs) return false;
-        }
+        if (mbar_try(addr, parity)) return true;
+        if ((it & 1023u) == 0u && (int64_t)(now_ns() - start) > kWaitNs) return false;
     }
+}
+
+// bit j (0..127) of a 4-word ancestor mask held in registers
+__device__ __forceinline__ bool anc_bit(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int j) {
+    const uint32_t w = j < 64 ? (j < 32 ? a0 : a1) : (j < 96 ? a2 : a3);
+    return (w >> (j & 31)) & 1u;
 }
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -260,28 +270,33 @@ __global__ void __launch_bounds__(288, 1) tree_attn_bf16_kernel(const __grid_con
                 mma_bf16(sc[pr * 2 + 1], qa[ks], b2, b3);
             }
         }
-        // mask, scale, online softmax
+        // mask (only chunks reaching past the prefix), scale, online softmax
         const int base = (c_begin + i) * kBlockN;
         float mloc[2] = {-INFINITY, -INFINITY};
+        if (base + kBlockN <= kv_len) {
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
+            for (int t = 0; t < 8; ++t)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int hh = e >> 1;
-                const int pos = base + t * 8 + qc + (e & 1);
-                bool vis;
-                if (pos < kv_len) {
-                    vis = true;
-                } else if (pos < T) {
-                    const int j = pos - kv_len;
-                    vis = (anc[hh][j >> 5] >> (j & 31)) & 1u;
-                } else {
-                    vis = false;
+                for (int e = 0; e < 4; ++e) {
+                    const float v = sc[t][e] * p.scale_log2;
+                    sc[t][e] = v;
+                    mloc[e >> 1] = fmaxf(mloc[e >> 1], v);
                 }
-                const float v = vis ? sc[t][e] * p.scale_log2 : -INFINITY;
-                sc[t][e] = v;
-                mloc[hh] = fmaxf(mloc[hh], v);
-            }
+        } else {
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int hh = e >> 1;
+                    const int pos = base + t * 8 + qc + (e & 1);
+                    const int j = pos - kv_len;
+                    const bool vis = pos < kv_len ||
+                                     (pos < T && anc_bit(anc[hh][0], anc[hh][1], anc[hh][2], anc[hh][3], j));
+                    const float v = vis ? sc[t][e] * p.scale_log2 : -INFINITY;
+                    sc[t][e] = v;
+                    mloc[hh] = fmaxf(mloc[hh], v);
+                }
+        }
         float alpha[2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {

@@ -5,11 +5,13 @@
 namespace fg {
 
 __global__ void philox_uniforms_kernel(uint64_t seed, const int32_t* __restrict__ seq_ids, int32_t n_rows,
-                                       int32_t round_idx, int32_t n_draws, float* __restrict__ out) {
+                                       int32_t round_idx, const int32_t* __restrict__ round_dev, int32_t n_draws,
+                                       float* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)n_rows * n_draws) return;
     const int32_t r = (int32_t)(i / n_draws), d = (int32_t)(i % n_draws);
-    out[i] = philox_uniform(seed, (uint32_t)seq_ids[r], (uint32_t)round_idx, (uint32_t)d);
+    const int32_t round = round_idx + (round_dev != nullptr ? *round_dev : 0);
+    out[i] = philox_uniform(seed, (uint32_t)seq_ids[r], (uint32_t)round, (uint32_t)d);
 }
 
 template <typename T>
@@ -165,12 +167,12 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restr
 using namespace fg;
 
 extern "C" fg_status fg_philox_uniforms(uint64_t seed, const int32_t* seq_ids, int32_t n_rows, int32_t round_idx,
-                                        int32_t n_draws, float* out, void* stream) {
+                                        const int32_t* round_dev, int32_t n_draws, float* out, void* stream) {
     if (n_rows < 0 || n_draws < 0 || (n_rows > 0 && n_draws > 0 && (!seq_ids || !out))) return FG_EINVAL;
     const int64_t n = (int64_t)n_rows * n_draws;
     if (n == 0) return FG_OK;
-    philox_uniforms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(seed, seq_ids, n_rows,
-                                                                                          round_idx, n_draws, out);
+    philox_uniforms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        seed, seq_ids, n_rows, round_idx, round_dev, n_draws, out);
     return launch_status();
 }
 

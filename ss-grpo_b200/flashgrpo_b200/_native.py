@@ -62,7 +62,7 @@ SIGNATURES = {
     "fg_last_cuda_error": (c_i32, []),
     "fg_read_device_error": (c_i32, [ctypes.POINTER(c_i32), c_i32]),
     "fg_wait_flag": (c_i32, [c_vp, c_i64, c_vp, c_vp]),
-    "fg_philox_uniforms": (c_i32, [c_u64, c_vp, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "fg_philox_uniforms": (c_i32, [c_u64, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp]),
     "fg_sample_rows": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_f32, c_vp, c_vp, c_vp]),
     "fg_row_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
@@ -111,10 +111,21 @@ def load():
     return _lib
 
 
+# Entry points that enqueue exactly one kernel; `launches` counts them so a
+# caller can report how many of this library's kernels a step runs.
+LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_build_tree",
+             "fg_tree_attention", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
+             "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows"}
+launches = 0
+
+
 def call(name: str, *args) -> None:
+    global launches
     status = getattr(load(), name)(*args)
     if status != FG_OK:
         raise NativeError(name, status)
+    if name in LAUNCHING:
+        launches += 1
 
 
 def read_device_error(clear: bool = True) -> int:

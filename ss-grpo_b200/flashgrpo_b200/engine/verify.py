@@ -1,0 +1,374 @@
+"""Verify engine: one MEDUSA tree-verify round on a B200, device resident.
+
+A round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1649-2938 of the
+reference, Reflex off) runs as one stream of work with no host sync:
+
+  propose   X = [h ; head_1(h) ; ... ; head_k(h)] -> X @ lm_head^T   (cuBLAS)
+            root token  = fg_sample_rows(rows of h, forced = pending correction)
+            candidates  = fg_row_topk(head rows)                      (K1 top-k)
+  tree      fg_build_tree: plan, dense tree, ancestor bits, slots     (K2)
+  verify    per layer: RMSNorm, QKV GEMM (+bias), fg_rope_kv_write (RoPE +
+            tree K/V written at each row's cache tail), fg_tree_attention
+            (K3), O GEMM + residual, RMSNorm, gate/up GEMM, SwiGLU, down GEMM
+            + residual; final RMSNorm
+  lm_head   internal (has-children) nodes only                        (cuBLAS)
+  accept    fg_accept_extract: exact_target walk, clip/EOS/pending rules,
+            KV compaction in every layer, next hidden state           (K4)
+
+State lives on the device between rounds: the KV cache
+[layers, B, Hkv, capacity, D] with one logical length per row (no holes --
+the reference's padded slots and attention-mask holes disappear), the next
+round's hidden state (rows [0, B) of X), pending correction tokens, the
+round counter feeding the Philox uniforms, and the active-row flags.
+
+Because every tensor of a round has a fixed shape for a given (rows, plan),
+the round is captured once in a CUDA graph and replayed.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native as N
+from .. import ops
+from ..decoding.medusa_tree import TreePlan, dense_topology, internal_nodes
+
+
+# ------------------------------------------------------------------ weights
+@dataclass
+class ModelSpec:
+    n_layers: int
+    hidden: int
+    n_q_heads: int
+    n_kv_heads: int
+    head_dim: int
+    inter: int
+    vocab: int
+    eps: float
+    dtype: torch.dtype
+
+
+def unwrap_causal_lm(causal_lm):
+    if hasattr(causal_lm, "get_base_model"):
+        return causal_lm.get_base_model()
+    if hasattr(causal_lm, "base_model") and hasattr(causal_lm.base_model, "model"):
+        return causal_lm.base_model.model
+    return causal_lm
+
+
+def _fuse_rows(modules_params: list[torch.nn.Parameter]) -> torch.Tensor:
+    """Concatenates parameters along dim 0 and rebinds each one as a view of
+    the fused tensor, so the HF model keeps working without a second copy."""
+    fused = torch.cat([p.data for p in modules_params], 0).contiguous()
+    off = 0
+    for p in modules_params:
+        n = p.shape[0]
+        p.data = fused[off:off + n]
+        off += n
+    return fused
+
+
+class TargetWeights:
+    """The HF causal LM's parameters in the layout the verify forward uses."""
+
+    def __init__(self, causal_lm):
+        base = unwrap_causal_lm(causal_lm)
+        core = base.model
+        cfg = base.config
+        hq = cfg.num_attention_heads
+        self.spec = ModelSpec(
+            n_layers=cfg.num_hidden_layers, hidden=cfg.hidden_size, n_q_heads=hq,
+            n_kv_heads=cfg.num_key_value_heads, head_dim=getattr(cfg, "head_dim", None) or cfg.hidden_size // hq,
+            inter=cfg.intermediate_size, vocab=cfg.vocab_size, eps=float(cfg.rms_norm_eps),
+            dtype=next(base.parameters()).dtype)
+        self.embed = core.embed_tokens.weight
+        self.final_norm = core.norm.weight
+        self.lm_head = base.lm_head.weight
+        rot = core.rotary_emb
+        self.inv_freq = rot.inv_freq.float().contiguous()
+        self.attention_scaling = float(getattr(rot, "attention_scaling", 1.0))
+        self.layers = []
+        for layer in core.layers:
+            at, mlp = layer.self_attn, layer.mlp
+            qkv_b = None
+            if at.q_proj.bias is not None:
+                qkv_b = _fuse_rows([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias])
+            self.layers.append({
+                "in_norm": layer.input_layernorm.weight,
+                "w_qkv": _fuse_rows([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]),
+                "b_qkv": qkv_b,
+                "w_o": at.o_proj.weight,
+                "b_o": at.o_proj.bias,
+                "post_norm": layer.post_attention_layernorm.weight,
+                "w_gu": _fuse_rows([mlp.gate_proj.weight, mlp.up_proj.weight]),
+                "w_down": mlp.down_proj.weight,
+            })
+
+
+class HeadWeights:
+    """MEDUSA head parameters (heads.{i}.norm / heads.{i}.fc of medusa_heads.pt)
+    cast once to the model's compute dtype."""
+
+    def __init__(self, heads, dtype, device):
+        state = heads.state_dict() if hasattr(heads, "state_dict") else dict(heads)
+        self.heads = []
+        i = 0
+        while f"heads.{i}.fc.weight" in state:
+            g = lambda k: state[f"heads.{i}.{k}"].detach().to(device=device, dtype=dtype).contiguous()
+            self.heads.append({"norm_w": g("norm.weight"), "norm_b": g("norm.bias"), "fc_w": g("fc.weight"),
+                               "fc_b": g("fc.bias")})
+            i += 1
+        if any(k.startswith("heads.") and k.endswith("output.weight") for k in state):
+            raise NotImplementedError("untied MEDUSA output heads are not on the B200 path (tie_lm_head=True)")
+
+    def __len__(self):
+        return len(self.heads)
+
+
+# -------------------------------------------------------------- round state
+@dataclass
+class RoundConfig:
+    do_sample: bool = True
+    temperature: float = 1.0
+    eos_id: int = 1
+    max_length: int = 1 << 30
+    seed: int = 0
+    attn_splits: int = 0
+
+
+class DecodeState:
+    """Device state of a batch of rollouts between rounds."""
+
+    def __init__(self, spec: ModelSpec, B: int, capacity: int, device, n_heads: int):
+        self.B, self.capacity = B, capacity
+        L, hkv, D = spec.n_layers, spec.n_kv_heads, spec.head_dim
+        # zero-filled once: every slot the attention kernel can touch is finite
+        self.k = torch.zeros((L, B, hkv, capacity, D), dtype=spec.dtype, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.row_len = torch.zeros(B, dtype=torch.int32, device=device)
+        self.pending = torch.full((B,), -1, dtype=torch.int32, device=device)
+        self.active = torch.ones(B, dtype=torch.int32, device=device)
+        self.seq_ids = torch.arange(B, dtype=torch.int32, device=device)
+        self.round_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self.X = torch.zeros(((n_heads + 1) * B, spec.hidden), dtype=spec.dtype, device=device)
+        self.kv_layers = [ops.kv_layer(self.k[l], self.v[l]) for l in range(L)]
+
+    @property
+    def hidden(self) -> torch.Tensor:
+        return self.X[: self.B]
+
+
+class RoundBuffers:
+    """Every intermediate of one round for a fixed (rows, plan) shape."""
+
+    def __init__(self, spec: ModelSpec, B: int, plan: TreePlan, n_heads: int, device, dcap: int):
+        H, V = spec.hidden, spec.vocab
+        self.n_heads = n_heads
+        parents, depths = dense_topology(plan, n_heads)
+        self.N = len(parents)
+        self.internal = internal_nodes(parents)
+        self.n_int = len(self.internal)
+        self.kmax = max([int(k) for k in plan.topk_by_depth[:n_heads]] + [1])
+        self.n_draws = 1 + max(len(plan.topk_by_depth), 1)
+        N_, f = self.N, dict(device=device)
+        self.logits = torch.empty(((n_heads + 1) * B, V), dtype=spec.dtype, **f)
+        self.ln = torch.empty((B, H), dtype=spec.dtype, **f)
+        self.fc = torch.empty((B, H), dtype=spec.dtype, **f)
+        self.U = torch.empty((B, self.n_draws), dtype=torch.float32, **f)
+        self.root = torch.empty(B, dtype=torch.int32, **f)
+        hb = max(n_heads, 1) * B
+        self.topk = (torch.empty((hb, self.kmax), dtype=torch.int32, **f),
+                     torch.empty((hb, self.kmax), dtype=torch.float32, **f),
+                     torch.empty(hb, dtype=torch.float32, **f), torch.empty(hb, dtype=torch.float32, **f))
+        i32 = dict(dtype=torch.int32, **f)
+        self.tree = {"tokens": torch.empty((B, N_), **i32), "positions": torch.empty((B, N_), **i32),
+                     "slot": torch.empty((B, N_), **i32), "parents": torch.empty(N_, **i32),
+                     "depths": torch.empty(N_, **i32), "anc": torch.empty((N_, 4), **i32),
+                     "internal": torch.empty(N_, **i32), "plan": torch.empty(16, **i32)}
+        T = B * N_
+        qkv_dim = (spec.n_q_heads + 2 * spec.n_kv_heads) * spec.head_dim
+        self.h = torch.empty((T, H), dtype=spec.dtype, **f)
+        self.xn = torch.empty((T, H), dtype=spec.dtype, **f)
+        self.qkv = torch.empty((T, qkv_dim), dtype=spec.dtype, **f)
+        self.q = torch.empty((B, N_, spec.n_q_heads, spec.head_dim), dtype=spec.dtype, **f)
+        self.attn = torch.empty_like(self.q)
+        self.gu = torch.empty((T, 2 * spec.inter), dtype=spec.dtype, **f)
+        self.act = torch.empty((T, spec.inter), dtype=spec.dtype, **f)
+        self.tree_hidden = torch.empty((B, N_, H), dtype=spec.dtype, **f)
+        idx = [b * N_ + i for b in range(B) for i in self.internal]
+        self.int_idx = torch.tensor(idx if idx else [0], dtype=torch.int32, **f)
+        self.hid_int = torch.empty((max(len(idx), 1), H), dtype=spec.dtype, **f)
+        self.tree_logits = torch.empty((max(len(idx), 1), V), dtype=spec.dtype, **f)
+        self.dcap = dcap
+        self.out = {k: torch.empty((B, dcap), **i32) for k in ("acc_tokens", "acc_nodes")}
+        for k in ("acc_len", "correction", "last_node", "finished"):
+            self.out[k] = torch.empty(B, **i32)
+        self.acc_sum = torch.zeros(1, dtype=torch.int64, **f)
+        self.corr_used = torch.zeros(1, dtype=torch.int64, **f)
+        ws = ops.attention_workspace_bytes(B, N_, spec.n_q_heads, spec.n_kv_heads, spec.head_dim, num_splits=0,
+                                           max_kv_len=0)
+        self.ws_bytes = ws
+        self.attn_ws = None
+
+
+# ------------------------------------------------------------------- engine
+class VerifyEngine:
+    def __init__(self, causal_lm, medusa_heads, *, device=None):
+        self.model = causal_lm
+        self.w = TargetWeights(causal_lm)
+        self.spec = self.w.spec
+        self.device = device or self.w.embed.device
+        if self.device.type != "cuda":
+            raise RuntimeError("VerifyEngine runs on a CUDA device (B200); the model is on " + str(self.device))
+        N.load()
+        self.heads = HeadWeights(medusa_heads, self.spec.dtype, self.device)
+        self.scale = self.spec.head_dim ** -0.5
+        self._graphs: dict = {}
+
+    # -------------------------------------------------------------- prefill
+    @torch.no_grad()
+    def prefill(self, input_ids, attention_mask, *, repeats: int = 1, capacity: int, n_heads: int) -> DecodeState:
+        """Runs the HF model over the prompts, then moves the valid (non-pad)
+        prompt K/V into a fresh cache, repeated `repeats` times per prompt
+        (flash_medusa_decoder.py:1325-1346)."""
+        from transformers import DynamicCache
+
+        base = unwrap_causal_lm(self.model)
+        ids = input_ids.to(self.device)
+        mask = attention_mask.to(self.device).long()
+        pos = (mask.cumsum(-1) - 1).masked_fill(mask == 0, 0)
+        out = base.model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=DynamicCache(),
+                         use_cache=True, return_dict=True)
+        hid = out.last_hidden_state
+        n_valid = mask.sum(-1)
+        P, S = ids.shape
+        B = P * repeats
+        if int(n_valid.max()) + 1 > capacity:
+            raise ValueError("KV capacity smaller than the prompt")
+        st = DecodeState(self.spec, B, capacity, self.device, n_heads)
+        layers = [(l.keys, l.values) for l in out.past_key_values.layers]
+        for p in range(P):
+            nv = int(n_valid[p])
+            rows = slice(p * repeats, (p + 1) * repeats)
+            # valid tokens are the mask==1 positions (left padding): positions 0..nv-1
+            sel = mask[p].nonzero().squeeze(-1)
+            for l, (k, v) in enumerate(layers):
+                st.k[l, rows, :, :nv] = k[p][:, sel].unsqueeze(0)
+                st.v[l, rows, :, :nv] = v[p][:, sel].unsqueeze(0)
+            last = int(sel[-1]) if nv > 0 else S - 1
+            st.X[rows] = hid[p, last].unsqueeze(0)
+            st.row_len[rows] = nv
+        del out, layers
+        return st
+
+    # ---------------------------------------------------------------- round
+    def buffers(self, B: int, plan: TreePlan, n_heads: int, dcap: int) -> RoundBuffers:
+        key = ("buf", B, plan.node_budget_per_seq, tuple(plan.topk_by_depth), n_heads, dcap)
+        if key not in self._graphs:
+            self._graphs[key] = RoundBuffers(self.spec, B, plan, n_heads, self.device, dcap)
+        return self._graphs[key]
+
+    def _attn_workspace(self, rb: RoundBuffers, st: DecodeState, splits: int):
+        need = ops.attention_workspace_bytes(st.B, rb.N, self.spec.n_q_heads, self.spec.n_kv_heads,
+                                             self.spec.head_dim, num_splits=splits, max_kv_len=st.capacity)
+        if need and (rb.attn_ws is None or rb.attn_ws.numel() * 4 < need):
+            rb.attn_ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=self.device)
+        return rb.attn_ws
+
+    def propose(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
+        B, nh = st.B, rb.n_heads
+        h = st.hidden
+        for i in range(nh):
+            hw = self.heads.heads[i]
+            ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
+            torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
+            ops.silu_residual(h, rb.fc, out=st.X[(i + 1) * B:(i + 2) * B])
+        torch.mm(st.X[: (nh + 1) * B], self.w.lm_head.t(), out=rb.logits)
+        ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
+        ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
+                        forced=st.pending, out=rb.root)
+        if nh > 0:
+            ops.row_topk(rb.logits[B:(nh + 1) * B], rb.kmax, out=rb.topk)
+
+    def build_tree(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams):
+        nh = rb.n_heads
+        B = st.B
+        if nh > 0:
+            cidx = rb.topk[0].view(nh, B, rb.kmax)
+            cval = rb.topk[1].view(nh, B, rb.kmax)
+            hmax = rb.topk[2].view(nh, B)
+            hlse = rb.topk[3].view(nh, B)
+        else:
+            cidx = cval = hmax = hlse = None
+        ops.build_tree(params, rb.root, cidx, cval, hmax, hlse, nmax=rb.N, logits_dtype=self.spec.dtype,
+                       row_len=st.row_len, out=rb.tree)
+
+    def verify_forward(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig, attn_events=None):
+        """attn_events (optional): per-layer (start, end) CUDA events recorded
+        around the tree-attention launch, for live per-launch timing."""
+        sp, w = self.spec, self.w
+        B, N_ = st.B, rb.N
+        ops.gather_rows(w.embed, rb.tree["tokens"].view(-1), out=rb.h)
+        ws = self._attn_workspace(rb, st, cfg.attn_splits)
+        for l, lw in enumerate(w.layers):
+            ops.rmsnorm(rb.h, lw["in_norm"], sp.eps, out=rb.xn)
+            if lw["b_qkv"] is not None:
+                torch.addmm(lw["b_qkv"], rb.xn, lw["w_qkv"].t(), out=rb.qkv)
+            else:
+                torch.mm(rb.xn, lw["w_qkv"].t(), out=rb.qkv)
+            kv = st.kv_layers[l]
+            ops.rope_kv_write(rb.qkv, rb.tree["positions"], w.inv_freq, w.attention_scaling, B=B, n_nodes=N_,
+                              n_q_heads=sp.n_q_heads, n_kv_heads=sp.n_kv_heads, head_dim=sp.head_dim,
+                              kv_len=st.row_len, k_cache=None, v_cache=None, q_out=rb.q, kv=kv)
+            if attn_events is not None:
+                attn_events[l][0].record()
+            ops.tree_attention(rb.q, st.k[l], st.v[l], st.row_len, rb.tree["anc"], scale=self.scale, out=rb.attn,
+                               workspace=ws, num_splits=cfg.attn_splits, max_kv_len=st.capacity, kv=kv)
+            if attn_events is not None:
+                attn_events[l][1].record()
+            torch.addmm(rb.h, rb.attn.view(B * N_, -1), lw["w_o"].t(), out=rb.h)
+            if lw["b_o"] is not None:
+                rb.h.add_(lw["b_o"])
+            ops.rmsnorm(rb.h, lw["post_norm"], sp.eps, out=rb.xn)
+            torch.mm(rb.xn, lw["w_gu"].t(), out=rb.gu)
+            ops.silu_mul(rb.gu, out=rb.act)
+            torch.addmm(rb.h, rb.act, lw["w_down"].t(), out=rb.h)
+        ops.rmsnorm(rb.h, w.final_norm, sp.eps, out=rb.tree_hidden.view(B * N_, -1))
+
+    def accept(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
+        B = st.B
+        if rb.n_int > 0:
+            ops.gather_rows(rb.tree_hidden.view(B * rb.N, -1), rb.int_idx, out=rb.hid_int)
+            torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
+        rb.corr_used += (st.pending >= 0).sum()
+        outs = dict(rb.out)
+        outs["pending"] = st.pending
+        ops.accept_extract(logits=rb.tree_logits, slot=rb.tree["slot"], tokens=rb.tree["tokens"],
+                           parents=rb.tree["parents"], n_nodes=None, n_nodes_shared=rb.N, uniforms=rb.U[:, 1:],
+                           do_sample=cfg.do_sample, temperature=cfg.temperature, eos_id=cfg.eos_id,
+                           max_length=cfg.max_length, row_len=st.row_len, outputs=outs, dcap=rb.dcap,
+                           update_len=True, active=st.active, k_layers=[st.k[l] for l in range(self.spec.n_layers)],
+                           v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,
+                           hidden_out=st.hidden)
+        rb.acc_sum += rb.out["acc_len"].sum()
+        st.round_dev += 1
+
+    def run_round(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig,
+                  attn_events=None):
+        """All device work of one round, enqueued on the current stream."""
+        self.propose(st, rb, cfg)
+        self.build_tree(st, rb, params)
+        self.verify_forward(st, rb, cfg, attn_events)
+        self.accept(st, rb, cfg)
+
+    # --------------------------------------------------------------- graphs
+    def graph_round(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig,
+                    pool=None, attn_events=None) -> torch.cuda.CUDAGraph:
+        """Captures run_round for this (state, buffers, plan); replay() runs it.
+        attn_events must be created with external=True to be captured."""
+        self._attn_workspace(rb, st, cfg.attn_splits)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=pool):
+            self.run_round(st, rb, params, cfg, attn_events)
+        return g

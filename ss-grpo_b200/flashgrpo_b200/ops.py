@@ -49,13 +49,13 @@ def _rows(t: torch.Tensor, name: str) -> tuple[int, int]:
 
 # ----------------------------------------------------------------- sampling
 def philox_uniforms(seed: int, seq_ids: torch.Tensor, round_idx: int, n_draws: int,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
+                    out: torch.Tensor | None = None, round_dev: torch.Tensor | None = None) -> torch.Tensor:
     _need(seq_ids, "seq_ids", torch.int32)
     n = seq_ids.shape[0]
     if out is None:
         out = torch.empty((n, n_draws), dtype=torch.float32, device=seq_ids.device)
     N.call("fg_philox_uniforms", ctypes.c_uint64(seed & (2 ** 64 - 1)), _ptr(seq_ids), n, int(round_idx),
-           int(n_draws), _ptr(out), _stream(seq_ids))
+           _ptr(round_dev), int(n_draws), _ptr(out), _stream(seq_ids))
     return out
 
 
@@ -207,7 +207,9 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
     stride, vocab = _rows(logits, "logits")
     for name, t in (("slot", slot), ("tokens", tokens), ("parents", parents), ("row_len", row_len)):
         _need(t, name, torch.int32)
-    _need(uniforms, "uniforms", torch.float32)
+    _need(uniforms, "uniforms", torch.float32, contiguous=False)
+    if uniforms.dim() != 2 or uniforms.stride(1) != 1:
+        raise ValueError("uniforms must be [B, draws] with contiguous rows")
     B, nmax = tokens.shape
     a = N.AcceptArgs()
     a.logits, a.logits_dtype, a.logits_row_stride, a.vocab = logits.data_ptr(), dtype_code(logits), stride, vocab

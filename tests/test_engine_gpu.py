@@ -1,0 +1,155 @@
+"""End-to-end parity of the B200 verify engine and the drop-in decoder.
+
+* config 1 (fp32): FlashMedusaDecoder.generate on the GPU against the oracle's
+  restatement of the reference generate loop on the CPU, with the same
+  per-(sequence, round, draw) Philox uniforms -> identical tokens and stats.
+* a Qwen2.5-1.5B-shaped bf16 model with 2 layers: one verify round's tree
+  hidden states against HF eager attention with the reference's dense mask
+  (bf16 tolerance), and the acceptance outputs against the oracle walk fed the
+  GPU's own tree logits (bit-exact).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cuda_available
+from oracle import native as orc
+from oracle import reference_path as rp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")]
+
+
+class _Tok:
+    pad_token_id = 0
+    eos_token_id = 1
+
+
+def _heads_list(st, n):
+    return [{"norm_w": st[f"heads.{i}.norm.weight"], "norm_b": st[f"heads.{i}.norm.bias"],
+             "fc_w": st[f"heads.{i}.fc.weight"], "fc_b": st[f"heads.{i}.fc.bias"]} for i in range(n)]
+
+
+@pytest.mark.parametrize("run", [
+    dict(tree_mode="fixed", fixed=(4, 2, 2), mx=16, depth=4, repeats=1, max_new=24, seed=0),
+    dict(tree_mode="concurrency_aware", cpeak=64, fixed=(4, 3, 2), mx=16, depth=4, repeats=2, max_new=16, seed=3),
+    dict(tree_mode="concurrency_aware", cpeak=2048, fixed=(3, 2, 2), mx=32, depth=4, repeats=1, max_new=20, seed=9,
+         greedy=True),
+])
+def test_generate_config1_matches_oracle(run):
+    from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
+    from flashgrpo_b200.utils import synthetic
+
+    cpu_model = synthetic.build_model(1)
+    gpu_model = synthetic.build_model(1).cuda()
+    st = synthetic.medusa_head_tensors(1)
+    ids, mask = synthetic.random_prompts(4, 128, 4096, seed=0)
+    if run["repeats"] > 1:
+        ids, mask = ids[:2], mask[:2]
+    greedy = run.get("greedy", False)
+    ocfg = rp.OracleConfig(tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
+                           max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
+                           fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy)
+    ref = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(run["seed"]),
+                      repeats=run["repeats"], max_length=128 + run["max_new"])
+    cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
+                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
+                            fixed_tree_topk_by_depth=run["fixed"], top_p=1.0, do_sample=not greedy,
+                            sampling_seed=run["seed"])
+    dec = FlashMedusaDecoder(gpu_model, {k: v.cuda() for k, v in st.items()}, _Tok(), cfg)
+    res = dec.generate(ids, mask, repeated_generate_nums=run["repeats"], max_length=128 + run["max_new"])
+    assert res["generated_token_ids"] == ref["generated_token_ids"]
+    for k in ("total_acc_length", "total_decoded_token_num", "total_verify_rounds", "total_correction_tokens",
+              "total_accepted_medusa_tokens", "total_proposed_medusa_tokens"):
+        assert res[k] == ref[k], k
+    from flashgrpo_b200 import _native
+
+    assert _native.read_device_error(clear=True) == 0
+
+
+def test_verify_round_bf16_against_hf_eager():
+    from flashgrpo_b200 import ops
+    from flashgrpo_b200.decoding.medusa_tree import plan_tree
+    from flashgrpo_b200.engine.verify import RoundConfig, VerifyEngine
+    from flashgrpo_b200.utils import synthetic
+
+    torch.manual_seed(0)
+    model = synthetic.build_model(2, layers=2, device="cpu").cuda()
+    st_heads = {k: v.cuda() for k, v in synthetic.medusa_head_tensors(2).items()}
+    ids, mask = synthetic.random_prompts(2, 200, 151936, seed=4)
+    eng = VerifyEngine(model, st_heads)
+    plan = plan_tree(active_batch_size=8, num_medusa_heads=3, tree_mode="concurrency_aware", cpeak_nodes=128,
+                     min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16, max_tree_depth=4,
+                     fixed_tree_topk_by_depth=[4, 3, 2])
+    assert (plan.topk_by_depth, plan.actual_nodes) == ([4, 2], 13)
+    state = eng.prefill(ids, mask, repeats=4, capacity=260, n_heads=2)
+    old_len = state.row_len.clone()
+    k_before = state.k.clone()
+    v_before = state.v.clone()
+    rb = eng.buffers(8, plan, 2, 4)
+    params = ops.plan_params(tree_mode="concurrency_aware", active_batch_size=8, num_medusa_heads=3,
+                             cpeak_nodes=128, min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16,
+                             max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2))
+    cfg = RoundConfig(seed=5)
+    with torch.inference_mode():
+        hidden0 = state.hidden.clone()
+        pending0 = state.pending.clone()
+        eng.propose(state, rb, cfg)
+        eng.build_tree(state, rb, params)
+        eng.verify_forward(state, rb, cfg)
+        tree_hidden = rb.tree_hidden.clone()
+        k_tree = state.k.clone()
+        v_tree = state.v.clone()
+        eng.accept(state, rb, cfg)
+    torch.cuda.synchronize()
+    assert int(rb.tree["plan"][10]) == 13
+    # --- tree hidden vs HF eager with the dense 4D mask over the prefill cache
+    from transformers import DynamicCache
+
+    tok = rb.tree["tokens"].long()
+    pos = rb.tree["positions"].long()
+    trees = [rp.Tree(tok[b].tolist(), rb.tree["parents"].tolist(), rb.tree["depths"].tolist()) for b in range(8)]
+    L = int(old_len[0])
+    full = torch.ones(8, L, dtype=torch.long, device="cuda")
+    _, mask4d, _, _ = rp.tree_attention_inputs(trees, full.cpu(), old_len.cpu().long(), pad_token_id=0,
+                                               dtype=torch.bfloat16)
+    cache = DynamicCache()
+    for l in range(2):
+        cache.update(k_before[l, :, :, :L].clone(), v_before[l, :, :, :L].clone(), l)
+    model.config._attn_implementation = "eager"
+    with torch.inference_mode():
+        ref = model.model(input_ids=tok, attention_mask=mask4d.cuda(), position_ids=pos, past_key_values=cache,
+                          use_cache=True, return_dict=True).last_hidden_state
+    err = (tree_hidden.float() - ref.float()).abs().max().item()
+    scale = ref.float().abs().max().item()
+    assert err <= 2e-2 * scale, (err, scale)
+    # --- the tree K/V landed at each row's tail like DynamicCache.update appends them
+    for l in range(2):
+        ref_k = cache.layers[l].keys
+        assert (k_tree[l, :, :, L:L + 13].float() - ref_k[:, :, L:L + 13].float()).abs().max() <= 2e-2 * \
+            ref_k.float().abs().max()
+    # --- acceptance on the GPU's own tree logits equals the oracle walk
+    U = rb.U.cpu().numpy()
+    walk = orc.accept_walk(rb.tree_logits.float().cpu().numpy(), rb.tree["slot"].cpu().numpy(),
+                           rb.tree["tokens"].cpu().numpy(),
+                           np.tile(rb.tree["parents"].cpu().numpy(), (8, 1)), np.full(8, 13), U[:, 1:].copy(),
+                           do_sample=True, temperature=1.0, eos_id=1, max_length=1 << 30,
+                           row_len=old_len.cpu().numpy(), dcap=4)
+    for k in ("acc_tokens", "acc_nodes", "acc_len", "correction", "last_node", "finished"):
+        assert np.array_equal(rb.out[k].cpu().numpy(), walk[k]), k
+    assert np.array_equal(state.pending.cpu().numpy(), walk["pending"])
+    assert torch.equal(state.row_len.cpu(), old_len.cpu() + torch.from_numpy(walk["acc_len"]))
+    # root tokens: fg-icdf-v1 draws on the GPU's root logits with the same uniforms
+    root_ref = orc.sample_rows(rb.logits[:8].float().cpu().numpy(), U[:, 0].copy())
+    root_ref = np.where(pending0.cpu().numpy() >= 0, pending0.cpu().numpy(), root_ref)
+    assert np.array_equal(rb.root.cpu().numpy(), root_ref)
+    # KV compaction: valid slots hold the accepted path's tree K/V
+    for b in range(8):
+        a = int(walk["acc_len"][b])
+        for j in range(a):
+            src = L + int(walk["acc_nodes"][b, j])
+            assert torch.equal(state.k[:, b, :, L + j], k_tree[:, b, :, src])
+            assert torch.equal(state.v[:, b, :, L + j], v_tree[:, b, :, src])
+        assert torch.equal(state.hidden[b], tree_hidden[b, int(walk["last_node"][b])])
+    assert not torch.equal(state.hidden, hidden0)
