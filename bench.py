@@ -297,7 +297,7 @@ def run_ours(args, rank, world, local_rank):
 
 
 # ------------------------------------------------------------- CPU oracle
-def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 4, prefix: int = 256):
+def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 8, prefix: int = 256):
     """The oracle's restatement of the reference generate loop, on the host
     cores, on a bounded sample of the config-2 workload (fp32, `rows` rollouts
     of `prefix`-token prompts)."""
@@ -316,7 +316,7 @@ def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 4, pr
     cfg = rp.OracleConfig(tree_mode="concurrency_aware", cpeak_nodes=1024 * rows // 64, max_tree_nodes_per_seq=16,
                           max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2))
     res = rp.generate(model, heads, ids, mask, cfg, rp.SeqRoundSampler(1234), repeats=2,
-                      max_length=prefix + warm_rounds + timed_rounds)
+                      max_length=prefix + warm_rounds + timed_rounds + 2)
     times = res["round_times"][warm_rounds:warm_rounds + timed_rounds]
     sec = sum(t for t, _ in times)
     tok = sum(n for _, n in times)
@@ -359,7 +359,7 @@ def main():
             dist.barrier()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_oracle_round_rate(1, 4)
+            result["cpu_baseline"] = cpu_oracle_round_rate(2, 30)
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()

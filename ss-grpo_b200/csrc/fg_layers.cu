@@ -40,6 +40,7 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
                                int32_t Hkv, int32_t D, const int32_t* __restrict__ kv_len, T* __restrict__ kc,
                                T* __restrict__ vc, int64_t sb, int64_t sh, int64_t ss, int32_t cap,
                                T* __restrict__ q_out) {
+    __shared__ float cs[2][128];  // cos / sin per frequency, once per token
     const int32_t tokn = blockIdx.x;  // b * n_nodes + node
     const int32_t b = tokn / n_nodes, node = tokn % n_nodes;
     const float pos = (float)positions[tokn];
@@ -47,16 +48,20 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
     const T* src = qkv + (int64_t)tokn * (Hq + 2 * Hkv) * D;
     const int32_t slotpos = kv_len[b] + node;
     const bool in_cap = slotpos < cap;
-    for (int32_t e = threadIdx.x; e < (Hq + Hkv) * half; e += blockDim.x) {
-        const int32_t h = e / half, i = e % half;
+    for (int32_t i = threadIdx.x; i < half; i += blockDim.x) {
         const float f = __fmul_rn(pos, inv_freq[i]);
         float c = cosf(f), s = sinf(f);
         if (attn_scaling != 1.0f) {
             c = c * attn_scaling;
             s = s * attn_scaling;
         }
-        c = rnd<T>(c);
-        s = rnd<T>(s);
+        cs[0][i] = rnd<T>(c);
+        cs[1][i] = rnd<T>(s);
+    }
+    __syncthreads();
+    for (int32_t e = threadIdx.x; e < (Hq + Hkv) * half; e += blockDim.x) {
+        const int32_t h = e / half, i = e % half;
+        const float c = cs[0][i], s = cs[1][i];
         const T* x = src + (int64_t)h * D;
         const float x1 = tf<T>(x[i]), x2 = tf<T>(x[i + half]);
         // out[i] = x1*c - x2*s ; out[i+half] = x2*c + x1*s  (each product rounded)
@@ -92,6 +97,46 @@ __device__ float block_sum(float v, float* red) {
     for (int i = 0; i < nw; ++i) t += red[i];
     __syncthreads();
     return t;
+}
+
+// Vectorized RMSNorm: 128 threads, rows of up to 128 * 4 vectors kept in
+// registers between the sum of squares and the scaling.
+template <typename T>
+__global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                          int32_t dim, float eps, T* __restrict__ y) {
+    constexpr int NV = 16 / sizeof(T);
+    __shared__ float red[32];
+    const int32_t nvec = dim / NV;
+    const T* xr = x + (int64_t)blockIdx.x * dim;
+    uint4 u[4];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int32_t vi = threadIdx.x + k * 128;
+        u[k] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * NV) : make_uint4(0, 0, 0, 0);
+        const T* e = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const float v = tf<T>(e[j]);
+            ss += v * v;
+        }
+    }
+    ss = block_sum<T>(ss, red);
+    const float r = rsqrtf(ss / (float)dim + eps);
+    T* yr = y + (int64_t)blockIdx.x * dim;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int32_t vi = threadIdx.x + k * 128;
+        if (vi >= nvec) break;
+        const uint4 uw = *reinterpret_cast<const uint4*>(w + vi * NV);
+        const T* e = reinterpret_cast<const T*>(&u[k]);
+        const T* we = reinterpret_cast<const T*>(&uw);
+        uint4 res;
+        T* o = reinterpret_cast<T*>(&res);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) o[j] = from_f<T>(tf<T>(we[j]) * rnd<T>(tf<T>(e[j]) * r));
+        *reinterpret_cast<uint4*>(yr + vi * NV) = res;
+    }
 }
 
 template <typename T>
@@ -135,6 +180,25 @@ __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gu, int32_t inter, int64_t total, T* __restrict__ out) {
+    constexpr int NV = 16 / sizeof(T);
+    if (inter % NV == 0 && (reinterpret_cast<uintptr_t>(gu) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+        const int64_t nvec = total / NV;
+        const int32_t vrow = inter / NV;
+        for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nvec;
+             e += (int64_t)gridDim.x * blockDim.x) {
+            const int64_t r = e / vrow, i = (e % vrow) * NV;
+            const uint4 ug = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + i);
+            const uint4 uu = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + i);
+            const T* g = reinterpret_cast<const T*>(&ug);
+            const T* u = reinterpret_cast<const T*>(&uu);
+            uint4 res;
+            T* o = reinterpret_cast<T*>(&res);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) o[k] = from_f<T>(rnd<T>(silu(tf<T>(g[k]))) * tf<T>(u[k]));
+            *reinterpret_cast<uint4*>(out + e * NV) = res;
+        }
+        return;
+    }
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = e / inter, i = e % inter;
         const float g = tf<T>(gu[r * 2 * inter + i]), u = tf<T>(gu[r * 2 * inter + inter + i]);
@@ -181,6 +245,7 @@ extern "C" fg_status fg_rope_kv_write(const void* qkv, int32_t dtype, const int3
                                       const fg_kv_layer* kv, void* q_out, void* stream) {
     if (B * n_nodes == 0) return FG_OK;
     if (!qkv || !positions || !inv_freq || !kv_len || !kv || !kv->k || !kv->v || !q_out || head_dim % 2) return FG_EINVAL;
+    if (head_dim > 256) return FG_ECAPACITY;
     cudaStream_t st = (cudaStream_t)stream;
     FG_DISPATCH(dtype, (rope_kv_kernel<T><<<B * n_nodes, 128, 0, st>>>(
                             (const T*)qkv, positions, inv_freq, attention_scaling, n_nodes, n_q_heads, n_kv_heads,
@@ -194,7 +259,16 @@ extern "C" fg_status fg_rmsnorm(const void* x, const void* weight, int32_t dtype
     if (n_rows == 0) return FG_OK;
     if (!x || !weight || !y || dim <= 0) return FG_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
-    FG_DISPATCH(dtype, (rmsnorm_kernel<T><<<n_rows, 256, 0, st>>>((const T*)x, (const T*)weight, dim, eps, (T*)y)));
+    const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
+    const bool vec = (dim * esz) % 16 == 0 && dim * esz <= 128 * 4 * 16 && ((uintptr_t)x % 16) == 0 &&
+                     ((uintptr_t)y % 16) == 0 && ((uintptr_t)weight % 16) == 0;
+    if (vec) {
+        FG_DISPATCH(dtype, (rmsnorm_vec_kernel<T><<<n_rows, 128, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
+                                                                         (T*)y)));
+    } else {
+        FG_DISPATCH(dtype, (rmsnorm_kernel<T><<<n_rows, 256, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
+                                                                      (T*)y)));
+    }
     return launch_status();
 }
 

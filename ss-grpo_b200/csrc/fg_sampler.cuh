@@ -3,10 +3,13 @@
 // One CTA of FG_SAMPLE_LANES threads draws one token from one logits row.
 // Thread t owns vocabulary chunk t (C = roundup8(ceil(V / 512)) contiguous
 // entries); the chunk totals are prefix-summed sequentially by thread 0 so
-// the cumulative values are exactly those of the CPU checker.
+// the cumulative values are exactly those of the CPU checker.  Rows that
+// allow it are read with 16-byte vectors, several in flight per thread; the
+// order of every floating-point addition stays the specified one.
 #pragma once
 
 #include "fg_common.cuh"
+#include "fg_vec.cuh"
 
 namespace fg {
 
@@ -26,26 +29,13 @@ __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return _
 template <>
 __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 
-template <typename T>
-__device__ __forceinline__ float scaled_t(const T* row, int32_t i, float temperature) {
-    float v = to_f<T>(row[i]);
-    if (temperature > 0.0f) v = __fdiv_rn(v, temperature);
-    return v;
+__device__ __forceinline__ float scale_t(float v, float temperature) {
+    return temperature > 0.0f ? __fdiv_rn(v, temperature) : v;
 }
 
-// First index of the maximum (torch.argmax); ties -> lower index.
-template <typename T>
-__device__ int32_t block_argmax(const T* row, int32_t V, SampleSmem& sm) {
+// Block-wide (max value, lowest index) reduction; returns the index.
+__device__ __forceinline__ int32_t block_best(float bv, int32_t bi, SampleSmem& sm) {
     const int tid = threadIdx.x;
-    float bv = -INFINITY;
-    int32_t bi = 0x7fffffff;
-    for (int32_t i = tid; i < V; i += FG_SAMPLE_LANES) {
-        const float v = to_f<T>(row[i]);
-        if (v > bv) {
-            bv = v;
-            bi = i;
-        }
-    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -69,9 +59,102 @@ __device__ int32_t block_argmax(const T* row, int32_t V, SampleSmem& sm) {
                 i = sm.redi[w];
             }
         sm.result = (i == 0x7fffffff) ? 0 : i;
+        sm.red[0] = v;
     }
     __syncthreads();
     const int32_t r = sm.result;
+    return r;
+}
+
+// Row maximum (raw values) and its first index.
+template <typename T>
+__device__ __forceinline__ void row_max(const T* row, int32_t V, float& bv, int32_t& bi) {
+    bv = -INFINITY;
+    bi = 0x7fffffff;
+    const int tid = threadIdx.x;
+    if (row_vectorizable<T>(row, V)) {
+        constexpr int NV = Vec<T>::N;
+        const int32_t nvec = V / NV;
+        for (int32_t v0 = tid; v0 < nvec; v0 += 4 * FG_SAMPLE_LANES) {
+            uint4 u[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int32_t v = v0 + k * FG_SAMPLE_LANES;
+                u[k] = v < nvec ? ldg16(row + (int64_t)v * NV) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int32_t v = v0 + k * FG_SAMPLE_LANES;
+                if (v >= nvec) break;
+                float f[NV];
+                unpack<T>(u[k], f);
+#pragma unroll
+                for (int e = 0; e < NV; ++e)
+                    if (f[e] > bv) {
+                        bv = f[e];
+                        bi = v * NV + e;
+                    }
+            }
+        }
+    } else {
+        for (int32_t i = tid; i < V; i += FG_SAMPLE_LANES) {
+            const float x = to_f<T>(row[i]);
+            if (x > bv) {
+                bv = x;
+                bi = i;
+            }
+        }
+    }
+}
+
+// Left-to-right fp32 sum of e_i over [lo, hi).  With `target` >= 0 it
+// instead returns the first i where base + running sum > target (or -1).
+template <typename T, bool kFind>
+__device__ __forceinline__ float chunk_scan(const T* row, int32_t lo, int32_t hi, float m, float temperature,
+                                            bool vec, float base, float target, int32_t* found) {
+    float c = 0.0f;
+    if (vec) {
+        constexpr int NV = Vec<T>::N;
+        constexpr int NB = 4;
+        for (int32_t i0 = lo; i0 < hi; i0 += NB * NV) {
+            uint4 u[NB];
+#pragma unroll
+            for (int k = 0; k < NB; ++k)
+                u[k] = (i0 + k * NV < hi) ? ldg16(row + i0 + k * NV) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int k = 0; k < NB; ++k) {
+                if (i0 + k * NV >= hi) break;
+                float f[NV];
+                unpack<T>(u[k], f);
+#pragma unroll
+                for (int e = 0; e < NV; ++e) {
+                    c = __fadd_rn(c, fg_exp(__fsub_rn(scale_t(f[e], temperature), m)));
+                    if (kFind && __fadd_rn(base, c) > target) {
+                        *found = i0 + k * NV + e;
+                        return c;
+                    }
+                }
+            }
+        }
+    } else {
+        for (int32_t i = lo; i < hi; ++i) {
+            c = __fadd_rn(c, fg_exp(__fsub_rn(scale_t(to_f<T>(row[i]), temperature), m)));
+            if (kFind && __fadd_rn(base, c) > target) {
+                *found = i;
+                return c;
+            }
+        }
+    }
+    return c;
+}
+
+// First index of the maximum (torch.argmax); ties -> lower index.
+template <typename T>
+__device__ int32_t block_argmax(const T* row, int32_t V, SampleSmem& sm) {
+    float bv;
+    int32_t bi;
+    row_max<T>(row, V, bv, bi);
+    const int32_t r = block_best(bv, bi, sm);
     __syncthreads();
     return r;
 }
@@ -81,25 +164,20 @@ template <typename T>
 __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool do_sample, float u, SampleSmem& sm) {
     if (!do_sample || temperature == 0.0f) return block_argmax<T>(row, V, sm);
     const int tid = threadIdx.x;
-    // pass 1: row maximum (order independent, coalesced)
-    float m = -INFINITY;
-    for (int32_t i = tid; i < V; i += FG_SAMPLE_LANES) m = fmaxf(m, scaled_t<T>(row, i, temperature));
-    m = warp_max(m);
-    if ((tid & 31) == 0) sm.red[tid >> 5] = m;
+    // pass 1: maximum of the scaled logits.  x -> x / T is monotone for T > 0,
+    // so the maximum of the raw values, divided once, is that maximum.
+    float bv;
+    int32_t bi;
+    row_max<T>(row, V, bv, bi);
+    block_best(bv, bi, sm);
+    const float m = scale_t(sm.red[0], temperature);
     __syncthreads();
-    if (tid < 32) {
-        float v = tid < FG_SAMPLE_LANES / 32 ? sm.red[tid] : -INFINITY;
-        v = warp_max(v);
-        if (tid == 0) sm.red[0] = v;
-    }
-    __syncthreads();
-    m = sm.red[0];
     // pass 2: left-to-right sum of this thread's chunk
+    const bool vec = row_vectorizable<T>(row, V);
     const int32_t C = sample_chunk_len(V);
-    const int32_t lo = tid * C;
+    const int32_t lo = min(tid * C, V);
     const int32_t hi = min(lo + C, V);
-    float c = 0.0f;
-    for (int32_t i = lo; i < hi; ++i) c = __fadd_rn(c, fg_exp(__fsub_rn(scaled_t<T>(row, i, temperature), m)));
+    const float c = chunk_scan<T, false>(row, lo, hi, m, temperature, vec, 0.0f, 0.0f, nullptr);
     sm.P[tid + 1] = c;
     if (tid == 0) sm.result = -1;
     __syncthreads();
@@ -115,14 +193,9 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
     const float target = __fmul_rn(u, sm.P[FG_SAMPLE_LANES]);
     const float P0 = sm.P[tid];
     if (P0 <= target && target < sm.P[tid + 1]) {
-        float cc = 0.0f;
-        for (int32_t i = lo; i < hi; ++i) {
-            cc = __fadd_rn(cc, fg_exp(__fsub_rn(scaled_t<T>(row, i, temperature), m)));
-            if (__fadd_rn(P0, cc) > target) {
-                sm.result = i;
-                break;
-            }
-        }
+        int32_t found = -1;
+        chunk_scan<T, true>(row, lo, hi, m, temperature, vec, P0, target, &found);
+        sm.result = found;
     }
     __syncthreads();
     const int32_t r = sm.result;

@@ -31,49 +31,50 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) sample_rows_kernel(
 }
 
 // ----------------------------------------------------------------- top-k
-constexpr int kTopkThreads = 256;
-
 __device__ __forceinline__ bool better(float av, int32_t ai, float bv, int32_t bi) {
     return av > bv || (av == bv && ai < bi);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restrict__ logits, int64_t row_stride,
-                                                                int32_t V, int32_t k, int32_t* __restrict__ out_idx,
-                                                                float* __restrict__ out_val,
-                                                                float* __restrict__ out_max,
-                                                                float* __restrict__ out_lse, int32_t round_lse) {
-    __shared__ float sv[kTopkThreads][FG_MAX_TOPK + 1];
-    __shared__ int32_t si[kTopkThreads][FG_MAX_TOPK + 1];
-    __shared__ float redv[kTopkThreads / 32];
-    __shared__ int32_t redi[kTopkThreads / 32];
-    __shared__ float reds[kTopkThreads / 32];
+// Per-row top-K (value descending, index ascending), row maximum and
+// optional logsumexp.  Each thread keeps a sorted K-list of the entries it
+// visits (vector loads, four in flight); the lists are merged by K rounds of
+// a block-wide "best head" reduction.
+template <typename T, int K, int NT, bool LSE>
+__global__ void __launch_bounds__(NT) row_topk_kernel(const T* __restrict__ logits, int64_t row_stride, int32_t V,
+                                                      int32_t k, int32_t* __restrict__ out_idx,
+                                                      float* __restrict__ out_val, float* __restrict__ out_max,
+                                                      float* __restrict__ out_lse, int32_t round_lse) {
+    __shared__ float sv[NT * K];
+    __shared__ int32_t si[NT * K];
+    __shared__ float redv[NT / 32];
+    __shared__ int32_t redi[NT / 32];
+    __shared__ int32_t redt[NT / 32];
+    __shared__ float reds[NT / 32];
     __shared__ int32_t winner;
     const int tid = threadIdx.x;
     const T* row = logits + (int64_t)blockIdx.x * row_stride;
-    float v[FG_MAX_TOPK];
-    int32_t id[FG_MAX_TOPK];
+    float v[K];
+    int32_t id[K];
 #pragma unroll
-    for (int j = 0; j < FG_MAX_TOPK; ++j) {
+    for (int j = 0; j < K; ++j) {
         v[j] = -INFINITY;
         id[j] = 0x7fffffff;
     }
     float m = -INFINITY, s = 0.0f;
-    for (int32_t i = tid; i < V; i += kTopkThreads) {
-        const float x = to_f<T>(row[i]);
-        // online max / sum of exp for the logsumexp
-        if (x > m) {
-            s = (m == -INFINITY) ? 0.0f : s * expf(m - x);
-            m = x;
+    auto visit = [&](float x, int32_t i) {
+        if (LSE) {
+            if (x > m) {
+                s = (m == -INFINITY) ? 0.0f : s * expf(m - x);
+                m = x;
+            }
+            if (x != -INFINITY) s += expf(x - m);
         }
-        if (x != -INFINITY) s += expf(x - m);
-        // insertion into the sorted local list; indices arrive increasing, so
-        // an equal value stays behind the earlier index
-        if (better(x, i, v[FG_MAX_TOPK - 1], id[FG_MAX_TOPK - 1])) {
+        // indices arrive increasing per thread: an equal value stays behind
+        if (better(x, i, v[K - 1], id[K - 1])) {
             float cv = x;
             int32_t ci = i;
 #pragma unroll
-            for (int j = 0; j < FG_MAX_TOPK; ++j) {
+            for (int j = 0; j < K; ++j) {
                 if (better(cv, ci, v[j], id[j])) {
                     const float tv = v[j];
                     const int32_t ti = id[j];
@@ -84,44 +85,66 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restr
                 }
             }
         }
-    }
-    // logsumexp across the block
-    float gm = warp_max(m);
-    if ((tid & 31) == 0) redv[tid >> 5] = gm;
-    __syncthreads();
-    if (tid == 0) {
-        float t = redv[0];
-        for (int w = 1; w < kTopkThreads / 32; ++w) t = fmaxf(t, redv[w]);
-        redv[0] = t;
-    }
-    __syncthreads();
-    gm = redv[0];
-    float ls = (m == -INFINITY) ? 0.0f : s * expf(m - gm);
+    };
+    if (row_vectorizable<T>(row, V)) {
+        constexpr int NV = Vec<T>::N;
+        const int32_t nvec = V / NV;
+        for (int32_t v0 = tid; v0 < nvec; v0 += 4 * NT) {
+            uint4 u[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
-    if ((tid & 31) == 0) reds[tid >> 5] = ls;
+            for (int k2 = 0; k2 < 4; ++k2) {
+                const int32_t vi = v0 + k2 * NT;
+                u[k2] = vi < nvec ? ldg16(row + (int64_t)vi * NV) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
-    for (int j = 0; j < FG_MAX_TOPK; ++j) {
-        sv[tid][j] = v[j];
-        si[tid][j] = id[j];
+            for (int k2 = 0; k2 < 4; ++k2) {
+                const int32_t vi = v0 + k2 * NT;
+                if (vi >= nvec) break;
+                float f[NV];
+                unpack<T>(u[k2], f);
+#pragma unroll
+                for (int e = 0; e < NV; ++e) visit(f[e], vi * NV + e);
+            }
+        }
+    } else {
+        for (int32_t i = tid; i < V; i += NT) visit(to_f<T>(row[i]), i);
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        sv[tid * K + j] = v[j];
+        si[tid * K + j] = id[j];
+    }
+    if (LSE) {
+        float gm = warp_max(m);
+        if ((tid & 31) == 0) redv[tid >> 5] = gm;
+        __syncthreads();
+        if (tid < 32) {
+            float t = tid < NT / 32 ? redv[tid] : -INFINITY;
+            t = warp_max(t);
+            if (tid == 0) redv[0] = t;
+        }
+        __syncthreads();
+        gm = redv[0];
+        float ls = (m == -INFINITY) ? 0.0f : s * expf(m - gm);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+        if ((tid & 31) == 0) reds[tid >> 5] = ls;
+        __syncthreads();
+        if (tid == 0) {
+            float tot = 0.0f;
+            for (int w = 0; w < NT / 32; ++w) tot += reds[w];
+            float lse = gm + logf(tot);
+            if (round_lse == FG_DTYPE_BF16) lse = __bfloat162float(__float2bfloat16_rn(lse));
+            if (round_lse == FG_DTYPE_F16) lse = __half2float(__float2half_rn(lse));
+            out_lse[blockIdx.x] = lse;
+        }
     }
     __syncthreads();
-    if (tid == 0) {
-        float tot = 0.0f;
-        for (int w = 0; w < kTopkThreads / 32; ++w) tot += reds[w];
-        float lse = gm + logf(tot);
-        if (round_lse == FG_DTYPE_BF16) lse = __bfloat162float(__float2bfloat16_rn(lse));
-        if (round_lse == FG_DTYPE_F16) lse = __half2float(__float2half_rn(lse));
-        out_lse[blockIdx.x] = lse;
-        out_max[blockIdx.x] = gm;
-    }
     // k rounds of "best head among all thread lists"
     int head = 0;
     for (int r = 0; r < k; ++r) {
-        float hv = head < k ? sv[tid][head] : -INFINITY;
-        int32_t hi = head < k ? si[tid][head] : 0x7fffffff;
-        float bv = hv;
-        int32_t bi = hi;
+        float bv = head < K ? sv[tid * K + head] : -INFINITY;
+        int32_t bi = head < K ? si[tid * K + head] : 0x7fffffff;
         int bt = tid;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -137,29 +160,58 @@ __global__ void __launch_bounds__(kTopkThreads) row_topk_kernel(const T* __restr
         if ((tid & 31) == 0) {
             redv[tid >> 5] = bv;
             redi[tid >> 5] = bi;
-            reds[tid >> 5] = __int_as_float(bt);
+            redt[tid >> 5] = bt;
         }
         __syncthreads();
-        if (tid == 0) {
-            float wv = redv[0];
-            int32_t wi = redi[0];
-            int wt = __float_as_int(reds[0]);
-            for (int w = 1; w < kTopkThreads / 32; ++w) {
-                const int t2 = __float_as_int(reds[w]);
-                if (better(redv[w], redi[w], wv, wi) || (redv[w] == wv && redi[w] == wi && t2 < wt)) {
-                    wv = redv[w];
-                    wi = redi[w];
-                    wt = t2;
+        if (tid < 32) {
+            float wv = tid < NT / 32 ? redv[tid] : -INFINITY;
+            int32_t wi = tid < NT / 32 ? redi[tid] : 0x7fffffff;
+            int wt = tid < NT / 32 ? redt[tid] : 0x7fffffff;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+                const int32_t oi = __shfl_xor_sync(0xffffffffu, wi, o);
+                const int ot = __shfl_xor_sync(0xffffffffu, wt, o);
+                if (better(ov, oi, wv, wi) || (ov == wv && oi == wi && ot < wt)) {
+                    wv = ov;
+                    wi = oi;
+                    wt = ot;
                 }
             }
-            winner = wt;
-            out_idx[(int64_t)blockIdx.x * k + r] = (wi == 0x7fffffff) ? 0 : wi;
-            out_val[(int64_t)blockIdx.x * k + r] = wv;
+            if (tid == 0) {
+                winner = wt;
+                out_idx[(int64_t)blockIdx.x * k + r] = (wi == 0x7fffffff) ? 0 : wi;
+                out_val[(int64_t)blockIdx.x * k + r] = wv;
+                if (r == 0) out_max[blockIdx.x] = wv;
+            }
         }
         __syncthreads();
         if (tid == winner) ++head;
-        __syncthreads();
     }
+}
+
+template <typename T, bool LSE>
+static void launch_topk(const T* logits, int64_t row_stride, int32_t V, int32_t n_rows, int32_t k, int32_t* idx,
+                        float* val, float* mx, float* lse, int32_t dtype, cudaStream_t st) {
+    if (k <= 1)
+        row_topk_kernel<T, 1, 1024, LSE><<<n_rows, 1024, 0, st>>>(logits, row_stride, V, k, idx, val, mx, lse, dtype);
+    else if (k <= 2)
+        row_topk_kernel<T, 2, 1024, LSE><<<n_rows, 1024, 0, st>>>(logits, row_stride, V, k, idx, val, mx, lse, dtype);
+    else if (k <= 4)
+        row_topk_kernel<T, 4, 1024, LSE><<<n_rows, 1024, 0, st>>>(logits, row_stride, V, k, idx, val, mx, lse, dtype);
+    else if (k <= 8)
+        row_topk_kernel<T, 8, 512, LSE><<<n_rows, 512, 0, st>>>(logits, row_stride, V, k, idx, val, mx, lse, dtype);
+    else
+        row_topk_kernel<T, 16, 256, LSE><<<n_rows, 256, 0, st>>>(logits, row_stride, V, k, idx, val, mx, lse, dtype);
+}
+
+template <typename T>
+static void dispatch_topk(const void* logits, int64_t row_stride, int32_t V, int32_t n_rows, int32_t k, int32_t* idx,
+                          float* val, float* mx, float* lse, int32_t dtype, cudaStream_t st) {
+    if (lse)
+        launch_topk<T, true>((const T*)logits, row_stride, V, n_rows, k, idx, val, mx, lse, dtype, st);
+    else
+        launch_topk<T, false>((const T*)logits, row_stride, V, n_rows, k, idx, val, mx, lse, dtype, st);
 }
 
 }  // namespace fg
@@ -208,21 +260,19 @@ extern "C" fg_status fg_row_topk(const void* logits, int32_t dtype, int64_t row_
                                  int32_t n_rows, int32_t k, int32_t* out_idx, float* out_val, float* out_max,
                                  float* out_lse, void* stream) {
     if (n_rows == 0) return FG_OK;
-    if (!logits || !out_idx || !out_val || !out_max || !out_lse || vocab <= 0 || row_stride < vocab) return FG_EINVAL;
+    if (!logits || !out_idx || !out_val || !out_max || vocab <= 0 || row_stride < vocab) return FG_EINVAL;
     if (k <= 0 || k > FG_MAX_TOPK || k > vocab) return FG_ECAPACITY;
     cudaStream_t st = (cudaStream_t)stream;
     switch (dtype) {
         case FG_DTYPE_F32:
-            row_topk_kernel<float><<<n_rows, kTopkThreads, 0, st>>>((const float*)logits, row_stride, vocab, k,
-                                                                   out_idx, out_val, out_max, out_lse, dtype);
+            dispatch_topk<float>(logits, row_stride, vocab, n_rows, k, out_idx, out_val, out_max, out_lse, dtype, st);
             break;
         case FG_DTYPE_BF16:
-            row_topk_kernel<__nv_bfloat16><<<n_rows, kTopkThreads, 0, st>>>(
-                (const __nv_bfloat16*)logits, row_stride, vocab, k, out_idx, out_val, out_max, out_lse, dtype);
+            dispatch_topk<__nv_bfloat16>(logits, row_stride, vocab, n_rows, k, out_idx, out_val, out_max, out_lse,
+                                         dtype, st);
             break;
         case FG_DTYPE_F16:
-            row_topk_kernel<__half><<<n_rows, kTopkThreads, 0, st>>>((const __half*)logits, row_stride, vocab, k,
-                                                                    out_idx, out_val, out_max, out_lse, dtype);
+            dispatch_topk<__half>(logits, row_stride, vocab, n_rows, k, out_idx, out_val, out_max, out_lse, dtype, st);
             break;
         default:
             return FG_EINVAL;

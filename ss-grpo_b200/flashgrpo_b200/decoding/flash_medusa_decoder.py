@@ -88,6 +88,10 @@ class FlashMedusaDecoder:
         if config.top_k is not None:
             raise NotImplementedError("top_k sampling is not on the B200 path yet")
         self._engine: VerifyEngine | None = None
+        # captured round graphs, keyed by (state, round shape, round config);
+        # a shape is run eagerly once before it is captured
+        self._graphs: dict = {}
+        self._seen: set = set()
 
     # ------------------------------------------------------------- helpers
     @property
@@ -160,8 +164,7 @@ class FlashMedusaDecoder:
         tree_node_sum = 0.0
         tree_plan_last = {}
         pending_host = [-1] * B
-        graphs: dict = {}
-        seen: set = set()
+        graphs, seen = self._graphs, self._seen
         pinned = None
         verify_time = 0.0
         while any(active_host):
@@ -178,9 +181,8 @@ class FlashMedusaDecoder:
             params = self._params(n_active) if nh > 0 else ops.plan_params(
                 tree_mode="explicit", active_batch_size=n_active, num_medusa_heads=0, cpeak_nodes=0,
                 min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=1, fixed_tree_topk_by_depth=())
-            if nh > 0 and plan.node_budget_per_seq != rb.N and dense_node_count(plan.topk_by_depth) != rb.N:
-                pass  # truncated dense tree: the buffers were sized from the truncated topology
-            key = (B, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, n_active)
+            key = (id(st), B, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, n_active,
+                   rcfg.do_sample, rcfg.temperature, rcfg.eos_id, rcfg.max_length, rcfg.seed, rcfg.attn_splits)
             tv = time.time()
             if cfg.use_cuda_graphs and key in seen:
                 if key not in graphs:
@@ -226,7 +228,6 @@ class FlashMedusaDecoder:
                 if fin[r]:
                     active_host[r] = False
             pending_host = pend
-        graphs.clear()
         total_time = time.time() - total_start
         rounds = max(stats["total_verify_rounds"], 1)
         decoded = max(stats["total_decoded_token_num"], 1)

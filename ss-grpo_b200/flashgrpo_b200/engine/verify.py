@@ -162,7 +162,8 @@ class DecodeState:
 class RoundBuffers:
     """Every intermediate of one round for a fixed (rows, plan) shape."""
 
-    def __init__(self, spec: ModelSpec, B: int, plan: TreePlan, n_heads: int, device, dcap: int):
+    def __init__(self, spec: ModelSpec, B: int, plan: TreePlan, n_heads: int, device, dcap: int,
+                 adaptive: bool = False):
         H, V = spec.hidden, spec.vocab
         self.n_heads = n_heads
         parents, depths = dense_topology(plan, n_heads)
@@ -178,9 +179,11 @@ class RoundBuffers:
         self.U = torch.empty((B, self.n_draws), dtype=torch.float32, **f)
         self.root = torch.empty(B, dtype=torch.int32, **f)
         hb = max(n_heads, 1) * B
+        # the logsumexp is only consumed by adaptive trees
         self.topk = (torch.empty((hb, self.kmax), dtype=torch.int32, **f),
                      torch.empty((hb, self.kmax), dtype=torch.float32, **f),
-                     torch.empty(hb, dtype=torch.float32, **f), torch.empty(hb, dtype=torch.float32, **f))
+                     torch.empty(hb, dtype=torch.float32, **f),
+                     torch.empty(hb, dtype=torch.float32, **f) if adaptive else None)
         i32 = dict(dtype=torch.int32, **f)
         self.tree = {"tokens": torch.empty((B, N_), **i32), "positions": torch.empty((B, N_), **i32),
                      "slot": torch.empty((B, N_), **i32), "parents": torch.empty(N_, **i32),
@@ -227,16 +230,31 @@ class VerifyEngine:
         self._graphs: dict = {}
 
     # -------------------------------------------------------------- prefill
+    def state(self, B: int, capacity: int, n_heads: int) -> DecodeState:
+        """A decode state of this shape, reused across calls (so captured
+        round graphs stay valid) and reset for a new batch."""
+        key = ("state", B, capacity, n_heads)
+        st = self._graphs.get(key)
+        if st is None:
+            st = DecodeState(self.spec, B, capacity, self.device, n_heads)
+            self._graphs[key] = st
+        st.row_len.zero_()
+        st.pending.fill_(-1)
+        st.active.fill_(1)
+        st.seq_ids.copy_(torch.arange(B, dtype=torch.int32, device=self.device))
+        st.round_dev.zero_()
+        return st
+
     @torch.no_grad()
     def prefill(self, input_ids, attention_mask, *, repeats: int = 1, capacity: int, n_heads: int) -> DecodeState:
         """Runs the HF model over the prompts, then moves the valid (non-pad)
-        prompt K/V into a fresh cache, repeated `repeats` times per prompt
+        prompt K/V into the cache, repeated `repeats` times per prompt
         (flash_medusa_decoder.py:1325-1346)."""
         from transformers import DynamicCache
 
         base = unwrap_causal_lm(self.model)
-        ids = input_ids.to(self.device)
-        mask = attention_mask.to(self.device).long()
+        ids = input_ids.to(self.device, non_blocking=True)
+        mask = attention_mask.to(self.device, non_blocking=True).long()
         pos = (mask.cumsum(-1) - 1).masked_fill(mask == 0, 0)
         out = base.model(input_ids=ids, attention_mask=mask, position_ids=pos, past_key_values=DynamicCache(),
                          use_cache=True, return_dict=True)
@@ -246,7 +264,7 @@ class VerifyEngine:
         B = P * repeats
         if int(n_valid.max()) + 1 > capacity:
             raise ValueError("KV capacity smaller than the prompt")
-        st = DecodeState(self.spec, B, capacity, self.device, n_heads)
+        st = self.state(B, capacity, n_heads)
         layers = [(l.keys, l.values) for l in out.past_key_values.layers]
         for p in range(P):
             nv = int(n_valid[p])
@@ -263,10 +281,10 @@ class VerifyEngine:
         return st
 
     # ---------------------------------------------------------------- round
-    def buffers(self, B: int, plan: TreePlan, n_heads: int, dcap: int) -> RoundBuffers:
-        key = ("buf", B, plan.node_budget_per_seq, tuple(plan.topk_by_depth), n_heads, dcap)
+    def buffers(self, B: int, plan: TreePlan, n_heads: int, dcap: int, adaptive: bool = False) -> RoundBuffers:
+        key = ("buf", B, plan.node_budget_per_seq, tuple(plan.topk_by_depth), n_heads, dcap, adaptive)
         if key not in self._graphs:
-            self._graphs[key] = RoundBuffers(self.spec, B, plan, n_heads, self.device, dcap)
+            self._graphs[key] = RoundBuffers(self.spec, B, plan, n_heads, self.device, dcap, adaptive)
         return self._graphs[key]
 
     def _attn_workspace(self, rb: RoundBuffers, st: DecodeState, splits: int):
@@ -298,7 +316,7 @@ class VerifyEngine:
             cidx = rb.topk[0].view(nh, B, rb.kmax)
             cval = rb.topk[1].view(nh, B, rb.kmax)
             hmax = rb.topk[2].view(nh, B)
-            hlse = rb.topk[3].view(nh, B)
+            hlse = rb.topk[3].view(nh, B) if rb.topk[3] is not None else None
         else:
             cidx = cval = hmax = hlse = None
         ops.build_tree(params, rb.root, cidx, cval, hmax, hlse, nmax=rb.N, logits_dtype=self.spec.dtype,

@@ -76,15 +76,16 @@ def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool
     return out
 
 
-def row_topk(logits: torch.Tensor, k: int, out=None):
-    """(idx int32 [n,k], val f32 [n,k], row max f32 [n], logsumexp f32 [n])."""
+def row_topk(logits: torch.Tensor, k: int, out=None, *, with_lse: bool = True):
+    """(idx int32 [n,k], val f32 [n,k], row max f32 [n], logsumexp f32 [n] or None)."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     n = logits.shape[0]
     dev = logits.device
     if out is None:
         out = (torch.empty((n, k), dtype=torch.int32, device=dev), torch.empty((n, k), dtype=torch.float32, device=dev),
-               torch.empty(n, dtype=torch.float32, device=dev), torch.empty(n, dtype=torch.float32, device=dev))
+               torch.empty(n, dtype=torch.float32, device=dev),
+               torch.empty(n, dtype=torch.float32, device=dev) if with_lse else None)
     idx, val, mx, lse = out
     N.call("fg_row_topk", _ptr(logits), dtype_code(logits), stride, vocab, n, int(k), _ptr(idx), _ptr(val), _ptr(mx),
            _ptr(lse), _stream(logits))
