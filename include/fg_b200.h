@@ -181,6 +181,22 @@ fg_status fg_tree_attention(const void *q, int32_t dtype, const fg_kv_layer *kv,
                             int32_t n_kv_heads, int32_t head_dim, float scale, void *out, void *workspace,
                             size_t workspace_bytes, int32_t num_splits, int32_t max_kv_len, void *stream);
 
+/* Same attention, for callers that cannot allocate device memory: a caller
+ * binding this ABI from another language without a device allocator, or
+ * living under a memory manager that owns the GPU, where cudaMalloc would
+ * fail or synchronize the device mid-round.  No counterpart in the
+ * reference.  The split-K scratch comes from one fixed array inside the
+ * library (FG_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the
+ * library until exit); needs beyond it return FG_ECAPACITY.  The first call
+ * on a device looks the array up (make it before any stream capture); calls
+ * share the array, so calls that overlap on the GPU race.  Allocates
+ * nothing. */
+#define FG_NOALLOC_SCRATCH_BYTES (32u << 20)
+fg_status fg_tree_attention_noalloc(const void *q, int32_t dtype, const fg_kv_layer *kv, const int32_t *kv_len,
+                                    const uint32_t *anc_bits, int32_t B, int32_t n_nodes, int32_t n_q_heads,
+                                    int32_t n_kv_heads, int32_t head_dim, float scale, void *out,
+                                    int32_t num_splits, int32_t max_kv_len, void *stream);
+
 /* ------------------------------------------------ acceptance + extraction */
 typedef struct fg_accept_args {
     const void *logits;        /* tree logits rows (packed internal nodes) */

@@ -8,3 +8,4 @@
 #include "fg_accept.cu"
 #include "fg_layers.cu"
 #include "fg_attention.cu"
+#include "fg_attention_noalloc.cu"

@@ -19,6 +19,7 @@ FG_MAX_DEPTHS = 8
 FG_MAX_TOPK = 16
 FG_MAX_PATH = 16
 FG_MAX_LAYERS = 128
+FG_NOALLOC_SCRATCH_BYTES = 32 << 20
 
 c_i32, c_i64, c_f32, c_f64, c_u64, c_vp = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_double,
                                           ctypes.c_uint64, ctypes.c_void_p)
@@ -70,6 +71,8 @@ SIGNATURES = {
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
     "fg_tree_attention": (c_i32, [c_vp, c_i32, ctypes.POINTER(KvLayer), c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                                   c_i32, c_f32, c_vp, c_vp, ctypes.c_size_t, c_i32, c_i32, c_vp]),
+    "fg_tree_attention_noalloc": (c_i32, [c_vp, c_i32, ctypes.POINTER(KvLayer), c_vp, c_vp, c_i32, c_i32, c_i32,
+                                          c_i32, c_i32, c_f32, c_vp, c_i32, c_i32, c_vp]),
     "fg_accept_extract": (c_i32, [ctypes.POINTER(AcceptArgs), c_vp]),
     "fg_extract_path": (c_i32, [c_i32, ctypes.POINTER(c_u64), ctypes.POINTER(c_u64), c_i32, c_i32, c_i32, c_i32,
                                 c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_i32, c_vp]),
@@ -114,7 +117,7 @@ def load():
 # Entry points that enqueue exactly one kernel; `launches` counts them so a
 # caller can report how many of this library's kernels a step runs.
 LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_build_tree",
-             "fg_tree_attention", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
+             "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
              "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows"}
 launches = 0
 
