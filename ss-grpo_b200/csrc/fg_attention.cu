@@ -508,7 +508,7 @@ static bool make_kv_map(CUtensorMap* map, void* base, int32_t B, int32_t Hkv, in
 
 static int auto_splits(int32_t items, int32_t max_kv_len, int32_t n_nodes) {
     const int chunks = (max_kv_len + n_nodes + kBlockN - 1) / kBlockN;
-    const int slots = 148 * 2;
+    const int slots = 148;  // one tensor-core CTA per SM (~194 KB of shared memory each)
     int s = slots / max(1, items);
     s = max(1, min(s, chunks / 2));
     return min(s, 64);
@@ -597,16 +597,31 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tree_attn_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             tc::kSmemBytes);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             return FG_ECUDA;
         }
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    const int wm = (min(kMaxRows, p.rows_total) + 15) / 16;
+    tc::Params tp;
+    tp.q = p.q;
+    tp.out = p.out;
+    tp.kv_len = p.kv_len;
+    tp.anc = p.anc;
+    tp.N = p.N;
+    tp.Hq = p.Hq;
+    tp.Hkv = p.Hkv;
+    tp.G = p.G;
+    tp.groups = p.groups;
+    tp.splits = p.splits;
+    tp.rows_total = p.rows_total;
+    tp.scale_log2 = p.scale_log2;
+    tp.ws_o = p.ws_o;
+    tp.ws_ml = p.ws_ml;
+    tp.ws_cnt = p.ws_cnt;
     dim3 grid(p.splits, n_kv_heads * p.groups, B);
-    tree_attn_bf16_kernel<<<grid, 32 * (wm + 1), kSmemBytes, st>>>(mk, mv, p);
+    tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, tp);
     return launch_status();
 }

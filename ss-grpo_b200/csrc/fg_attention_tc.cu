@@ -1,0 +1,576 @@
+// fg_attention_tc.cu -- K3 on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same contract as the bf16 path of fg_tree_attention (flash-decoding GQA
+// attention of one layer's tree queries over each row's KV slots, tree mask
+// from ancestor bits), organised for sm_100a:
+//
+//   warp 0       TMA producer: K/V tiles of 64 slots x 128 dims (two 64x64
+//                boxes each, 128-byte swizzle) into a 4-stage ring.
+//   warp 1       allocates 512 TMEM columns; one elected thread issues
+//                tcgen05.mma: S = Q K^T (M=128 query rows, N=64 slots,
+//                K=128 dims) and O += P V (M=128, N=128 dims, K=64 slots);
+//                completion is signalled with tcgen05.commit on mbarriers.
+//   warps 4-7    softmax warpgroup 0: even KV tiles,
+//   warps 8-11   softmax warpgroup 1: odd KV tiles.  Each warpgroup is an
+//                independent online softmax with its own TMEM S tile
+//                (64 columns), its own P tile in 128B-swizzled smem and its
+//                own TMEM O accumulator (128 columns): one thread per query
+//                row (TMEM lane = row) loads S with tcgen05.ld, applies the
+//                tree mask, works in the log2 domain with lazy rescaling (O is
+//                rescaled only when the row maximum grows by more than 8, so P
+//                stays below 2^8) and writes P as bf16.  At the end the two
+//                (m, l, O) states are merged through shared memory; each
+//                warpgroup writes half of the head dimension (normalised
+//                output, or fp32 partials merged by the last split).
+//
+// Query rows are (node, head-of-group) pairs, row = node * G + g, up to 128
+// per CTA; the Q tile is loaded once by the softmax warpgroups.  Every
+// mbarrier wait is bounded (about one second); on a timeout the kernel
+// records FG_ETIMEOUT, stops issuing work, drains what it issued and frees
+// TMEM.
+#include "fg_common.cuh"
+
+namespace fg {
+namespace tc {
+
+constexpr int kD = 128;
+constexpr int kBlk = 64;                      // KV slots per stage
+constexpr int kStages = 4;
+constexpr int kRows = 128;                    // query rows per CTA (MMA M)
+constexpr int kThreads = 384;                 // 12 warps
+constexpr int kQBytes = kRows * kD * 2;       // 32 KB, two 16 KB d-halves
+constexpr int kPBytes = kRows * kBlk * 2;     // 16 KB per P buffer
+constexpr int kBox = kBlk * 64 * 2;           // 8 KB: 64 slots x 64 dims
+constexpr int kStageBytes = 4 * kBox;         // K lo/hi + V lo/hi = 32 KB
+constexpr int kOffQ = 0;
+constexpr int kOffP = kQBytes;                              // 32 KB
+constexpr int kOffStage = kOffP + 2 * kPBytes;              // 64 KB
+constexpr int kOffBar = kOffStage + kStages * kStageBytes;  // 192 KB
+constexpr int kOffXchg = kOffBar + 256;                     // m/l exchange, 2 KB
+constexpr int kSmemBytes = kOffXchg + 4 * kRows * 4 + 1024;
+constexpr uint32_t kTmemCols = 512;           // S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
+constexpr uint32_t kColO0 = 128;
+constexpr int64_t kWaitNs = 1000000000LL;
+constexpr float kRescaleLog2 = 8.0f;
+
+struct Params {
+    const __nv_bfloat16* q;
+    __nv_bfloat16* out;
+    const int32_t* kv_len;
+    const uint32_t* anc;
+    int32_t N, Hq, Hkv, G, groups, splits, rows_total;
+    float scale_log2;
+    float* ws_o;
+    float* ws_ml;
+    int32_t* ws_cnt;
+};
+
+// ---------------------------------------------------------------- PTX glue
+__device__ __forceinline__ uint32_t sa(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ uint64_t gtime() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(b)) : "memory");
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false after ~1 s or when another role aborted the CTA.
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    for (int i = 0; i < 2048; ++i)
+        if (bar_try(b, parity)) return true;
+    const uint64_t t0 = gtime();
+    for (uint32_t i = 0;; ++i) {
+        if (bar_try(b, parity)) return true;
+        if ((i & 255u) == 0u) {
+            if (*abort_flag) return false;
+            if ((int64_t)(gtime() - t0) > kWaitNs) {
+                *abort_flag = 1;
+                atomicCAS(&g_fg_error_word, 0, FG_ETIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// Time-bounded wait that ignores the abort flag: used to drain work this
+// thread already issued (TMA loads, MMAs) before TMEM or smem is released.
+__device__ __forceinline__ bool bar_drain(uint64_t* b, uint32_t parity) {
+    const uint64_t t0 = gtime();
+    for (uint32_t i = 0;; ++i) {
+        if (bar_try(b, parity)) return true;
+        if ((i & 255u) == 0u && (int64_t)(gtime() - t0) > kWaitNs) {
+            atomicCAS(&g_fg_error_word, 0, FG_ETIMEOUT);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(sa(b))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2, version 1).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, M = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool b_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(kRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(b))
+                 : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tst32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ bool anc_has(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int j) {
+    const uint32_t w = j < 64 ? (j < 32 ? a0 : a1) : (j < 96 ? a2 : a3);
+    return (w >> (j & 31)) & 1u;
+}
+
+// Byte offset of 16-byte column c of row r in a 128B-swizzled tile of 128-byte rows.
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+struct Bars {
+    uint64_t kv_full[kStages];
+    uint64_t kv_empty[kStages];
+    uint64_t s_full[2];
+    uint64_t s_free[2];
+    uint64_t p_full[2];
+    uint64_t o_done[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+    int last_flag;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                              const __grid_constant__ CUtensorMap tmV, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    float* xchg = reinterpret_cast<float*>(smem + kOffXchg);  // [m0 | l0 | m1 | l1] x 128 rows
+    volatile int* abort_flag = &bars->abort_flag;
+
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / p.groups, grp = blockIdx.y % p.groups;
+    const int b = blockIdx.z;
+    const int row0 = grp * kRows;
+    const int R = min(kRows, p.rows_total - row0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kv_len = p.kv_len[b];
+    const int T = kv_len + p.N;
+    const int nblk = (T + kBlk - 1) / kBlk;
+    const int per = (nblk + p.splits - 1) / p.splits;
+    const int c0 = min(nblk, split * per);
+    const int nmine = min(nblk, c0 + per) - c0;
+    const int item = (b * p.Hkv + kvh) * p.groups + grp;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            bar_init(&bars->kv_full[s], 1);
+            bar_init(&bars->kv_empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            bar_init(&bars->s_full[i], 1);
+            bar_init(&bars->s_free[i], 4);
+            bar_init(&bars->p_full[i], 4);
+            bar_init(&bars->o_done[i], 1);
+        }
+        bar_init(&bars->drain, 1);
+        bars->abort_flag = 0;
+        bars->last_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&bars->tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    const int wg = warp >= 4 ? (warp - 4) >> 2 : -1;  // softmax warpgroup
+    const int r = (warp & 3) * 32 + lane;              // query row = TMEM lane
+    // Q tile (rows beyond R zero) -> swizzled smem; warpgroup w loads dims [64w, 64w + 64)
+    if (wg >= 0) {
+        uint8_t* qs = smem + kOffQ + wg * (kRows * 128);
+        const bool valid = r < R;
+        const int rr = row0 + (valid ? r : 0);
+        const __nv_bfloat16* qrow = p.q + (((int64_t)b * p.N + rr / p.G) * p.Hq + kvh * p.G + rr % p.G) * kD + wg * 64;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 v = valid ? *reinterpret_cast<const uint4*>(qrow + c * 8) : make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(qs + sw128(r, c)) = v;
+        }
+        fence_async_smem();
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nmine; ++i) {
+                const int s = i % kStages;
+                if (i >= kStages && !bar_wait(&bars->kv_empty[s], ((i / kStages) - 1) & 1, abort_flag)) break;
+                uint8_t* st = smem + kOffStage + s * kStageBytes;
+                const int slot = (c0 + i) * kBlk;
+                bar_expect(&bars->kv_full[s], kStageBytes);
+                tma_4d(st, &tmK, 0, slot, kvh, b, &bars->kv_full[s]);
+                tma_4d(st + kBox, &tmK, 64, slot, kvh, b, &bars->kv_full[s]);
+                tma_4d(st + 2 * kBox, &tmV, 0, slot, kvh, b, &bars->kv_full[s]);
+                tma_4d(st + 3 * kBox, &tmV, 64, slot, kvh, b, &bars->kv_full[s]);
+                issued = i + 1;
+            }
+            // the last loads of each stage have landed before this CTA's smem goes away
+            for (int j = max(0, issued - kStages); j < issued; ++j)
+                bar_drain(&bars->kv_full[j % kStages], (j / kStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        // tile i belongs to warpgroup i & 1: S tile (i & 1), P tile (i & 1), O (i & 1)
+        if (lane == 0) {
+            constexpr uint32_t id_qk = idesc_bf16(kBlk, false);
+            constexpr uint32_t id_pv = idesc_bf16(kD, true);
+            const uint32_t q_addr = sa(smem + kOffQ);
+            auto issue_qk = [&](int i) -> bool {
+                const int s = i % kStages;
+                if (!bar_wait(&bars->kv_full[s], (i / kStages) & 1, abort_flag)) return false;
+                if (i >= 2 && !bar_wait(&bars->s_free[i & 1], ((i >> 1) - 1) & 1, abort_flag)) return false;
+                fence_after();
+                const uint32_t k_addr = sa(smem + kOffStage + s * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    const uint64_t da = sdesc(q_addr + (kk >> 2) * (kRows * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t db = sdesc(k_addr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
+                    umma(tmem + (uint32_t)((i & 1) * kBlk), da, db, id_qk, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&bars->s_full[i & 1]);
+                return true;
+            };
+            bool ok = true;
+            for (int i = 0; i < min(2, nmine) && ok; ++i) ok = issue_qk(i);
+            for (int i = 0; i < nmine && ok; ++i) {
+                const int s = i % kStages;
+                if (!bar_wait(&bars->p_full[i & 1], (i >> 1) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                fence_after();
+                const uint32_t p_addr = sa(smem + kOffP + (i & 1) * kPBytes);
+                const uint32_t v_addr = sa(smem + kOffStage + s * kStageBytes + 2 * kBox);
+                const uint32_t o_col = kColO0 + (uint32_t)(i & 1) * kD;
+#pragma unroll
+                for (int kk = 0; kk < kBlk / 16; ++kk) {
+                    const uint64_t da = sdesc(p_addr + kk * 32, 16, 1024);
+                    const uint64_t db = sdesc(v_addr + kk * 2048, kBox, 1024);
+                    umma(tmem + o_col, da, db, id_pv, (i >= 2 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&bars->o_done[i & 1]);
+                umma_commit(&bars->kv_empty[s]);
+                if (i + 2 < nmine) ok = issue_qk(i + 2);
+            }
+            // everything issued has completed before TMEM is read or freed
+            umma_commit(&bars->drain);
+            bar_drain(&bars->drain, 0);
+        }
+    } else if (wg >= 0) {
+        // ------------------------------------------- softmax warpgroup wg
+        const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t s_col = (uint32_t)(wg * kBlk);
+        const uint32_t o_col = kColO0 + (uint32_t)wg * kD;
+        const bool valid = r < R;
+        const int rr = row0 + (valid ? r : 0);
+        const int node = rr / p.G;
+        uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+        if (valid) {
+            a0 = p.anc[node * 4 + 0];
+            a1 = p.anc[node * 4 + 1];
+            a2 = p.anc[node * 4 + 2];
+            a3 = p.anc[node * 4 + 3];
+        }
+        float m_used = -INFINITY, l = 0.0f;
+        bool ok = true;
+        const int n_own = (nmine - wg + 1) / 2;  // tiles wg, wg + 2, ...
+        // Every tcgen05.ld / tcgen05.st below is a warp-collective
+        // (.sync.aligned) instruction: control flow around them is kept
+        // warp-uniform (__all_sync / __any_sync), per-row choices are selects.
+        constexpr unsigned kFull = 0xffffffffu;
+        for (int j = 0; j < n_own; ++j) {
+            const int i = 2 * j + wg;
+            if (!__all_sync(kFull, bar_wait(&bars->s_full[wg], j & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            fence_after();
+            float sv[kBlk];
+            tld32(tmem + lane_addr + s_col, sv);
+            tld32(tmem + lane_addr + s_col + 32, sv + 32);
+            fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive(&bars->s_free[wg]);
+            // mask + scale; maximum by a tree of independent fmaxf
+            const int base = (c0 + i) * kBlk;
+            if (base + kBlk <= kv_len) {
+#pragma unroll
+                for (int c = 0; c < kBlk; ++c) sv[c] *= p.scale_log2;
+            } else {
+#pragma unroll
+                for (int c = 0; c < kBlk; ++c) {
+                    const int pos = base + c;
+                    const bool vis = pos < kv_len || (pos < T && anc_has(a0, a1, a2, a3, pos - kv_len));
+                    sv[c] = vis ? sv[c] * p.scale_log2 : -INFINITY;
+                }
+            }
+            float mq[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                mq[q] = fmaxf(fmaxf(fmaxf(sv[q], sv[q + 8]), fmaxf(sv[q + 16], sv[q + 24])),
+                              fmaxf(fmaxf(sv[q + 32], sv[q + 40]), fmaxf(sv[q + 48], sv[q + 56])));
+            }
+            const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
+                                   fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7])));
+            // previous PV of this warpgroup done: P tile free and O stable
+            if (j >= 1 && !__all_sync(kFull, bar_wait(&bars->o_done[wg], (j - 1) & 1, abort_flag))) {
+                ok = false;
+                break;
+            }
+            const bool grow = mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx != -INFINITY);
+            const float alpha = grow ? ((m_used == -INFINITY) ? 0.0f : ex2(m_used - mx)) : 1.0f;
+            if (j >= 1 && __any_sync(kFull, grow)) {
+                // O holds this warpgroup's PV up to its previous tile: rescale in TMEM
+                fence_after();
+#pragma unroll 1
+                for (int cch = 0; cch < kD; cch += 32) {
+                    float ov[32];
+                    tld32(tmem + lane_addr + o_col + cch, ov);
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) ov[c] *= alpha;
+                    tst32(tmem + lane_addr + o_col + cch, ov);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            if (grow) {
+                l *= alpha;
+                m_used = mx;
+            }
+            // P = exp2(s - m_used) -> bf16, swizzled rows of 128 bytes
+            uint8_t* pbuf = smem + kOffP + wg * kPBytes;
+            const float mneg = m_used == -INFINITY ? 0.0f : -m_used;
+            float rsq[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float e[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) e[q] = ex2(sv[c * 8 + q] + mneg);  // ex2(-inf) = 0
+                rsq[c] = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+                uint4 w;
+                w.x = pack2(e[0], e[1]);
+                w.y = pack2(e[2], e[3]);
+                w.z = pack2(e[4], e[5]);
+                w.w = pack2(e[6], e[7]);
+                *reinterpret_cast<uint4*>(pbuf + sw128(r, c)) = w;
+            }
+            l += ((rsq[0] + rsq[1]) + (rsq[2] + rsq[3])) + ((rsq[4] + rsq[5]) + (rsq[6] + rsq[7]));
+            fence_async_smem();
+            fence_before();
+            __syncwarp();
+            if (lane == 0) bar_arrive(&bars->p_full[wg]);
+        }
+        // ---- epilogue: last PV of this warpgroup, then merge the two states
+        if (ok && n_own > 0) ok = __all_sync(kFull, bar_wait(&bars->o_done[wg], (n_own - 1) & 1, abort_flag));
+        fence_after();
+        xchg[(2 * wg) * kRows + r] = ok ? m_used : -INFINITY;
+        xchg[(2 * wg + 1) * kRows + r] = ok ? l : 0.0f;
+        // both O accumulators are final once both warpgroups pass this barrier
+        fence_before();
+        asm volatile("bar.sync 2, 256;" ::: "memory");
+        fence_after();
+        const float m0 = xchg[r], l0 = xchg[kRows + r], m1 = xchg[2 * kRows + r], l1 = xchg[3 * kRows + r];
+        const float mt = fmaxf(m0, m1);
+        // tile counts are CTA-uniform: a warpgroup without tiles left its O
+        // uninitialised and it is never read
+        const int n0 = (nmine + 1) / 2, n1 = nmine / 2;
+        const float w0 = (m0 != -INFINITY) ? ex2(m0 - mt) : 0.0f;
+        const float w1 = (m1 != -INFINITY) ? ex2(m1 - mt) : 0.0f;
+        const float lt = l0 * w0 + l1 * w1;
+        const int aborted = *abort_flag;
+        if (__all_sync(kFull, ok) && !__any_sync(kFull, aborted != 0)) {
+            // this warpgroup writes dims [64 wg, 64 wg + 64) of the merged row
+            const int d0 = wg * 64;
+            float* wo = nullptr;
+            if (p.splits > 1) {
+                wo = p.ws_o + ((int64_t)item * p.splits + split) * (kRows * kD) + (int64_t)r * kD;
+                if (wg == 0) {
+                    float* wml = p.ws_ml + ((int64_t)item * p.splits + split) * (2 * kRows);
+                    wml[r] = (w0 > 0.0f || w1 > 0.0f) ? mt : -INFINITY;
+                    wml[kRows + r] = lt;
+                }
+            }
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+            __nv_bfloat16* orow = p.out + (((int64_t)b * p.N + rr / p.G) * p.Hq + kvh * p.G + rr % p.G) * kD;
+#pragma unroll 1
+            for (int cch = 0; cch < 64; cch += 32) {
+                float oa[32], ob[32];
+                if (n0 > 0) {
+                    tld32(tmem + lane_addr + kColO0 + d0 + cch, oa);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) oa[c] = 0.0f;
+                }
+                if (n1 > 0) {
+                    tld32(tmem + lane_addr + kColO0 + kD + d0 + cch, ob);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) ob[c] = 0.0f;
+                }
+#pragma unroll
+                for (int c = 0; c < 32; ++c) oa[c] = (w0 > 0.0f ? oa[c] * w0 : 0.0f) + (w1 > 0.0f ? ob[c] * w1 : 0.0f);
+                if (p.splits == 1) {
+                    if (valid) {
+#pragma unroll
+                        for (int c = 0; c < 32; c += 8) {
+                            uint4 w;
+                            w.x = pack2(oa[c] * inv, oa[c + 1] * inv);
+                            w.y = pack2(oa[c + 2] * inv, oa[c + 3] * inv);
+                            w.z = pack2(oa[c + 4] * inv, oa[c + 5] * inv);
+                            w.w = pack2(oa[c + 6] * inv, oa[c + 7] * inv);
+                            *reinterpret_cast<uint4*>(orow + d0 + cch + c) = w;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 4)
+                        *reinterpret_cast<float4*>(wo + d0 + cch + c) = make_float4(oa[c], oa[c + 1], oa[c + 2], oa[c + 3]);
+                }
+            }
+        }
+        fence_before();
+    }
+    // ---- all roles done with TMEM: free it; splits merge below
+    __syncthreads();
+    fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    if (p.splits == 1 || *abort_flag) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&p.ws_cnt[item], 1);
+        bars->last_flag = (prev == p.splits - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!bars->last_flag) return;
+    __threadfence();
+    const float* wo_all = p.ws_o + (int64_t)item * p.splits * (kRows * kD);
+    const float* wml_all = p.ws_ml + (int64_t)item * p.splits * (2 * kRows);
+    for (int e = threadIdx.x; e < R * (kD / 2); e += blockDim.x) {
+        const int rw = e / (kD / 2), d = (e % (kD / 2)) * 2;
+        float mt = -INFINITY;
+        for (int s2 = 0; s2 < p.splits; ++s2) mt = fmaxf(mt, __ldcg(wml_all + s2 * 2 * kRows + rw));
+        float lt = 0.0f, o0 = 0.0f, o1 = 0.0f;
+        if (mt != -INFINITY) {
+            for (int s2 = 0; s2 < p.splits; ++s2) {
+                const float ms = __ldcg(wml_all + s2 * 2 * kRows + rw);
+                if (ms == -INFINITY) continue;
+                const float w = ex2(ms - mt);
+                lt += w * __ldcg(wml_all + s2 * 2 * kRows + kRows + rw);
+                const float2 ov =
+                    __ldcg(reinterpret_cast<const float2*>(wo_all + (int64_t)s2 * kRows * kD + rw * kD + d));
+                o0 += w * ov.x;
+                o1 += w * ov.y;
+            }
+        }
+        const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+        const int rr = row0 + rw;
+        __nv_bfloat16* orow = p.out + (((int64_t)b * p.N + rr / p.G) * p.Hq + kvh * p.G + rr % p.G) * kD;
+        *reinterpret_cast<__nv_bfloat162*>(orow + d) = __floats2bfloat162_rn(o0 * inv, o1 * inv);
+    }
+    if (threadIdx.x == 0) p.ws_cnt[item] = 0;
+}
+
+}  // namespace tc
+}  // namespace fg

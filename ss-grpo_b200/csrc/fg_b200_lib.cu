@@ -7,5 +7,6 @@
 #include "fg_tree.cu"
 #include "fg_accept.cu"
 #include "fg_layers.cu"
+#include "fg_attention_tc.cu"
 #include "fg_attention.cu"
 #include "fg_attention_noalloc.cu"
