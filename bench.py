@@ -283,7 +283,7 @@ def run_ours(args, rank, world, local_rank):
                    "graphs": "each step replays a captured CUDA graph of the round"},
         "accepted_tokens": accepted_all, "average_accept_length": accepted_all / (K * rows * world),
         "gpu_launches": launches_per_step * K,
-        "roofline": {"kernel": "fg_tree_attention (tree_attn_bf16_kernel)", "bound": "hbm",
+        "roofline": {"kernel": "fg_tree_attention (fg::tc::attn_tc_kernel, tcgen05)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback", "traffic": traffic,

@@ -169,7 +169,10 @@ typedef struct fg_kv_layer {
  *   tree_attention.py:6-67 as bits).
  * Replaces HF eager/SDPA attention with the dense 4D mask inside
  * forward_tree (flashgrpo_b200/models/qwen_flashgrpo_wrapper.py:220-239).
- * dtype FG_DTYPE_BF16 (tensor cores, D = 128) or FG_DTYPE_F32 (D <= 128).
+ * dtype FG_DTYPE_BF16 (tensor cores, D = 128, scale > 0) or FG_DTYPE_F32
+ * (D <= 128).  The bf16 path reads whole 128-slot tiles: slots from
+ * kv_len[b] + n_nodes up to the next multiple of 128 (within capacity) are
+ * read with weight 0 and must hold finite values (a zero-filled cache does).
  * num_splits 0 = automatic (from max_kv_len, the longest prefix of the
  * batch).  workspace: fg_tree_attention_workspace_size bytes for the same
  * arguments (0 when one split suffices), zero-filled before first use (the

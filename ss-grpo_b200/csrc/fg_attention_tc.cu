@@ -4,16 +4,18 @@
 // attention of one layer's tree queries over each row's KV slots, tree mask
 // from ancestor bits), organised for sm_100a:
 //
-//   warp 0       TMA producer: K/V tiles of 64 slots x 128 dims (two 64x64
-//                boxes each, 128-byte swizzle) into a 4-stage ring.
+//   warp 0       TMA producer: K and V tiles of 128 slots x 128 dims (two
+//                128x64 boxes each, 128-byte swizzle) into a 2-stage ring
+//                whose K and V halves are released separately (K(i) after
+//                QK(i), V(i) after PV(i)).
 //   warp 1       allocates 512 TMEM columns; one elected thread issues
-//                tcgen05.mma: S = Q K^T (M=128 query rows, N=64 slots,
-//                K=128 dims) and O += P V (M=128, N=128 dims, K=64 slots);
+//                tcgen05.mma: S = Q K^T (M=128 query rows, N=128 slots,
+//                K=128 dims) and O += P V (M=128, N=128 dims, K=128 slots);
 //                completion is signalled with tcgen05.commit on mbarriers.
 //   warps 4-7    softmax warpgroup 0: even KV tiles,
 //   warps 8-11   softmax warpgroup 1: odd KV tiles.  Each warpgroup is an
 //                independent online softmax with its own TMEM S tile
-//                (64 columns), its own P tile in 128B-swizzled smem and its
+//                (128 columns), its own P tile in 128B-swizzled smem and its
 //                own TMEM O accumulator (128 columns): one thread per query
 //                row (TMEM lane = row) loads S with tcgen05.ld, applies the
 //                tree mask, works in the log2 domain with lazy rescaling (O is
@@ -24,7 +26,11 @@
 //                output, or fp32 partials merged by the last split).
 //
 // Query rows are (node, head-of-group) pairs, row = node * G + g, up to 128
-// per CTA; the Q tile is loaded once by the softmax warpgroups.  Every
+// per CTA; the Q tile is loaded once by the softmax warpgroups.  The last
+// tile of a row reads KV slots past the row's tree tail (up to the next
+// multiple of 128, zero-filled beyond capacity): they are masked out of the
+// softmax but pass through P V with weight 0, so they must hold finite
+// values (a zero-initialised cache does).  Every
 // mbarrier wait is bounded (about one second); on a timeout the kernel
 // records FG_ETIMEOUT, stops issuing work, drains what it issued and frees
 // TMEM.
@@ -34,22 +40,25 @@ namespace fg {
 namespace tc {
 
 constexpr int kD = 128;
-constexpr int kBlk = 64;                      // KV slots per stage
-constexpr int kStages = 4;
+constexpr int kBlk = 128;                     // KV slots per tile / stage
+constexpr int kStages = 2;
 constexpr int kRows = 128;                    // query rows per CTA (MMA M)
 constexpr int kThreads = 384;                 // 12 warps
 constexpr int kQBytes = kRows * kD * 2;       // 32 KB, two 16 KB d-halves
-constexpr int kPBytes = kRows * kBlk * 2;     // 16 KB per P buffer
-constexpr int kBox = kBlk * 64 * 2;           // 8 KB: 64 slots x 64 dims
-constexpr int kStageBytes = 4 * kBox;         // K lo/hi + V lo/hi = 32 KB
+constexpr int kPBytes = kRows * kBlk * 2;     // 32 KB per P buffer, two 16 KB slot-halves
+constexpr int kBox = kBlk * 64 * 2;           // 16 KB: 128 slots x 64 dims
+constexpr int kStageBytes = 4 * kBox;         // K lo/hi + V lo/hi = 64 KB
 constexpr int kOffQ = 0;
 constexpr int kOffP = kQBytes;                              // 32 KB
-constexpr int kOffStage = kOffP + 2 * kPBytes;              // 64 KB
-constexpr int kOffBar = kOffStage + kStages * kStageBytes;  // 192 KB
-constexpr int kOffXchg = kOffBar + 256;                     // m/l exchange, 2 KB
-constexpr int kSmemBytes = kOffXchg + 4 * kRows * 4 + 1024;
-constexpr uint32_t kTmemCols = 512;           // S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
-constexpr uint32_t kColO0 = 128;
+constexpr int kOffStage = kOffP + 2 * kPBytes;              // 96 KB
+constexpr int kOffBar = kOffStage + kStages * kStageBytes;  // 224 KB
+// The epilogue's m/l exchange of warpgroup w lives in its own P buffer,
+// which no MMA reads once w's last PV has completed.  (The Q tile is not
+// free at that point: the issuer may still have a QK of the other
+// warpgroup's last tile outstanding.)
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512)
+constexpr uint32_t kColO0 = 256;
 constexpr int64_t kWaitNs = 1000000000LL;
 constexpr float kRescaleLog2 = 8.0f;
 
@@ -92,6 +101,18 @@ __device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking probe of a phase (never suspends the thread): the MMA issuer
+// polls several barriers in turn with it.
+__device__ __forceinline__ bool bar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(sa(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: false after ~1 s or when another role aborted the CTA.
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
     for (int i = 0; i < 2048; ++i)
@@ -174,6 +195,35 @@ __device__ __forceinline__ void tld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 128 consecutive fp32 columns of this thread's TMEM lane; the wait sits in
+// the same asm statement so no use of the registers can precede it.
+__device__ __forceinline__ void tld128(uint32_t taddr, float* v) {
+    uint32_t r[128];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+          "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+          "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+          "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+          "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+          "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+          "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+          "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+          "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tst32(uint32_t taddr, const float* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -197,9 +247,27 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-__device__ __forceinline__ bool anc_has(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int j) {
-    const uint32_t w = j < 64 ? (j < 32 ? a0 : a1) : (j < 96 ? a2 : a3);
-    return (w >> (j & 31)) & 1u;
+// Visibility of the 32 KV slots p0 .. p0 + 31 for one query row: bit t set
+// when slot p0 + t is a prefix slot (< kv_len) or a tree slot (< T) whose
+// tree index p0 + t - kv_len is an ancestor-or-self bit of (a0, a1, a2, a3).
+// Branch-free: funnel shifts over the 128-bit ancestor mask.
+__device__ __forceinline__ uint32_t visible_bits(int p0, int kv_len, int T, uint32_t a0, uint32_t a1, uint32_t a2,
+                                                 uint32_t a3) {
+    const int np = min(max(kv_len - p0, 0), 32);
+    const uint32_t prefix = np >= 32 ? 0xffffffffu : ((1u << np) - 1u);
+    const int nt = min(max(T - p0, 0), 32);
+    const uint32_t live = nt >= 32 ? 0xffffffffu : ((1u << nt) - 1u);
+    const int j0 = p0 - kv_len;  // tree index of bit 0, may be negative
+    uint32_t tree;
+    if (j0 < 0) {
+        tree = j0 > -32 ? (a0 << (-j0)) : 0u;
+    } else {
+        const int q = j0 >> 5, sh = j0 & 31;
+        const uint32_t lo = q == 0 ? a0 : q == 1 ? a1 : q == 2 ? a2 : q == 3 ? a3 : 0u;
+        const uint32_t hi = q == 0 ? a1 : q == 1 ? a2 : q == 2 ? a3 : 0u;
+        tree = __funnelshift_r(lo, hi, sh);
+    }
+    return (prefix | tree) & live;
 }
 
 // Byte offset of 16-byte column c of row r in a 128B-swizzled tile of 128-byte rows.
@@ -213,8 +281,10 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 struct Bars {
-    uint64_t kv_full[kStages];
-    uint64_t kv_empty[kStages];
+    uint64_t k_full[kStages];
+    uint64_t k_empty[kStages];
+    uint64_t v_full[kStages];
+    uint64_t v_empty[kStages];
     uint64_t s_full[2];
     uint64_t s_free[2];
     uint64_t p_full[2];
@@ -230,7 +300,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-    float* xchg = reinterpret_cast<float*>(smem + kOffXchg);  // [m0 | l0 | m1 | l1] x 128 rows
     volatile int* abort_flag = &bars->abort_flag;
 
     const int split = blockIdx.x;
@@ -247,10 +316,29 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const int nmine = min(nblk, c0 + per) - c0;
     const int item = (b * p.Hkv + kvh) * p.groups + grp;
 
+    // K(i) and V(i) go to stage i % kStages; K and V halves have their own barriers
+    auto load_k = [&](int i) {
+        const int s = i % kStages;
+        uint8_t* st = smem + kOffStage + s * kStageBytes;
+        const int slot = (c0 + i) * kBlk;
+        bar_expect(&bars->k_full[s], 2 * kBox);
+        tma_4d(st, &tmK, 0, slot, kvh, b, &bars->k_full[s]);
+        tma_4d(st + kBox, &tmK, 64, slot, kvh, b, &bars->k_full[s]);
+    };
+    auto load_v = [&](int i) {
+        const int s = i % kStages;
+        uint8_t* st = smem + kOffStage + s * kStageBytes + 2 * kBox;
+        const int slot = (c0 + i) * kBlk;
+        bar_expect(&bars->v_full[s], 2 * kBox);
+        tma_4d(st, &tmV, 0, slot, kvh, b, &bars->v_full[s]);
+        tma_4d(st + kBox, &tmV, 64, slot, kvh, b, &bars->v_full[s]);
+    };
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            bar_init(&bars->kv_full[s], 1);
-            bar_init(&bars->kv_empty[s], 1);
+            bar_init(&bars->k_full[s], 1);
+            bar_init(&bars->k_empty[s], 1);
+            bar_init(&bars->v_full[s], 1);
+            bar_init(&bars->v_empty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             bar_init(&bars->s_full[i], 1);
@@ -262,6 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         bars->abort_flag = 0;
         bars->last_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // the first tiles of the ring load while Q is staged and TMEM allocated
+        for (int i = 0; i < min(kStages, nmine); ++i) load_k(i);
+        for (int i = 0; i < min(kStages, nmine); ++i) load_v(i);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&bars->tmem_base)),
@@ -289,70 +380,92 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     fence_after();
     const uint32_t tmem = bars->tmem_base;
 
-    if (warp == 0) {
-        // ------------------------------------------------------ TMA producer
+    if (warp == 0 || warp == 2) {
+        // ------------------------------------- TMA producers: K (warp 0), V (warp 2)
+        // K(i) reuses the stage of K(i - 2) once QK(i - 2) has completed, V(i)
+        // that of V(i - 2) once PV(i - 2) has: the two streams never wait on
+        // each other, so a K load is not held up behind a PV.
         if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nmine; ++i) {
+            const bool is_k = warp == 0;
+            uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+            uint64_t* full = is_k ? bars->k_full : bars->v_full;
+            int issued = min(kStages, nmine);
+            for (int i = kStages; i < nmine; ++i) {
                 const int s = i % kStages;
-                if (i >= kStages && !bar_wait(&bars->kv_empty[s], ((i / kStages) - 1) & 1, abort_flag)) break;
-                uint8_t* st = smem + kOffStage + s * kStageBytes;
-                const int slot = (c0 + i) * kBlk;
-                bar_expect(&bars->kv_full[s], kStageBytes);
-                tma_4d(st, &tmK, 0, slot, kvh, b, &bars->kv_full[s]);
-                tma_4d(st + kBox, &tmK, 64, slot, kvh, b, &bars->kv_full[s]);
-                tma_4d(st + 2 * kBox, &tmV, 0, slot, kvh, b, &bars->kv_full[s]);
-                tma_4d(st + 3 * kBox, &tmV, 64, slot, kvh, b, &bars->kv_full[s]);
+                if (!bar_wait(&empty[s], ((i / kStages) - 1) & 1, abort_flag)) break;
+                if (is_k) load_k(i); else load_v(i);
                 issued = i + 1;
             }
             // the last loads of each stage have landed before this CTA's smem goes away
-            for (int j = max(0, issued - kStages); j < issued; ++j)
-                bar_drain(&bars->kv_full[j % kStages], (j / kStages) & 1);
+            for (int j = max(0, issued - kStages); j < issued; ++j) bar_drain(&full[j % kStages], (j / kStages) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
-        // tile i belongs to warpgroup i & 1: S tile (i & 1), P tile (i & 1), O (i & 1)
+        // tile i belongs to warpgroup i & 1: S tile (i & 1), P tile (i & 1), O
+        // (i & 1).  QK(i) needs K(i) and S(i - 2) read; PV(i) needs V(i) and
+        // P(i).  The two streams are polled without blocking and issued as
+        // soon as their operands are ready, each in tile order.
         if (lane == 0) {
             constexpr uint32_t id_qk = idesc_bf16(kBlk, false);
             constexpr uint32_t id_pv = idesc_bf16(kD, true);
             const uint32_t q_addr = sa(smem + kOffQ);
-            auto issue_qk = [&](int i) -> bool {
-                const int s = i % kStages;
-                if (!bar_wait(&bars->kv_full[s], (i / kStages) & 1, abort_flag)) return false;
-                if (i >= 2 && !bar_wait(&bars->s_free[i & 1], ((i >> 1) - 1) & 1, abort_flag)) return false;
-                fence_after();
-                const uint32_t k_addr = sa(smem + kOffStage + s * kStageBytes);
-#pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                    const uint64_t da = sdesc(q_addr + (kk >> 2) * (kRows * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t db = sdesc(k_addr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
-                    umma(tmem + (uint32_t)((i & 1) * kBlk), da, db, id_qk, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(&bars->s_full[i & 1]);
-                return true;
-            };
+            int nq = 0, npv = 0;
             bool ok = true;
-            for (int i = 0; i < min(2, nmine) && ok; ++i) ok = issue_qk(i);
-            for (int i = 0; i < nmine && ok; ++i) {
-                const int s = i % kStages;
-                if (!bar_wait(&bars->p_full[i & 1], (i >> 1) & 1, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                fence_after();
-                const uint32_t p_addr = sa(smem + kOffP + (i & 1) * kPBytes);
-                const uint32_t v_addr = sa(smem + kOffStage + s * kStageBytes + 2 * kBox);
-                const uint32_t o_col = kColO0 + (uint32_t)(i & 1) * kD;
+            uint64_t t_idle = 0;
+            for (uint32_t spin = 0; npv < nmine; ++spin) {
+                bool progress = false;
+                if (nq < nmine && bar_test(&bars->k_full[nq % kStages], (nq / kStages) & 1) &&
+                    (nq < 2 || bar_test(&bars->s_free[nq & 1], ((nq >> 1) - 1) & 1))) {
+                    fence_after();
+                    const uint32_t k_addr = sa(smem + kOffStage + (nq % kStages) * kStageBytes);
 #pragma unroll
-                for (int kk = 0; kk < kBlk / 16; ++kk) {
-                    const uint64_t da = sdesc(p_addr + kk * 32, 16, 1024);
-                    const uint64_t db = sdesc(v_addr + kk * 2048, kBox, 1024);
-                    umma(tmem + o_col, da, db, id_pv, (i >= 2 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kD / 16; ++kk) {
+                        const uint64_t da = sdesc(q_addr + (kk >> 2) * (kRows * 128) + (kk & 3) * 32, 16, 1024);
+                        const uint64_t db = sdesc(k_addr + (kk >> 2) * kBox + (kk & 3) * 32, 16, 1024);
+                        umma(tmem + (uint32_t)((nq & 1) * kBlk), da, db, id_qk, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&bars->s_full[nq & 1]);
+                    umma_commit(&bars->k_empty[nq % kStages]);
+                    ++nq;
+                    progress = true;
                 }
-                umma_commit(&bars->o_done[i & 1]);
-                umma_commit(&bars->kv_empty[s]);
-                if (i + 2 < nmine) ok = issue_qk(i + 2);
+                if (npv < nq && bar_test(&bars->v_full[npv % kStages], (npv / kStages) & 1) &&
+                    bar_test(&bars->p_full[npv & 1], (npv >> 1) & 1)) {
+                    fence_after();
+                    const uint32_t p_addr = sa(smem + kOffP + (npv & 1) * kPBytes);
+                    const uint32_t v_addr = sa(smem + kOffStage + (npv % kStages) * kStageBytes + 2 * kBox);
+                    const uint32_t o_col = kColO0 + (uint32_t)(npv & 1) * kD;
+#pragma unroll
+                    for (int kk = 0; kk < kBlk / 16; ++kk) {
+                        const uint64_t da = sdesc(p_addr + (kk >> 2) * (kRows * 128) + (kk & 3) * 32, 16, 1024);
+                        const uint64_t db = sdesc(v_addr + kk * 2048, kBox, 1024);
+                        umma(tmem + o_col, da, db, id_pv, (npv >= 2 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&bars->o_done[npv & 1]);
+                    umma_commit(&bars->v_empty[npv % kStages]);
+                    ++npv;
+                    progress = true;
+                }
+                if (progress) {
+                    t_idle = 0;
+                } else if ((spin & 255u) == 0u) {
+                    // bounded like every other wait: ~1 s without progress aborts the CTA
+                    if (*abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t now = gtime();
+                    if (t_idle == 0) {
+                        t_idle = now;
+                    } else if ((int64_t)(now - t_idle) > kWaitNs) {
+                        *abort_flag = 1;
+                        atomicCAS(&g_fg_error_word, 0, FG_ETIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                }
             }
+            (void)ok;
             // everything issued has completed before TMEM is read or freed
             umma_commit(&bars->drain);
             bar_drain(&bars->drain, 0);
@@ -387,32 +500,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             }
             fence_after();
             float sv[kBlk];
-            tld32(tmem + lane_addr + s_col, sv);
-            tld32(tmem + lane_addr + s_col + 32, sv + 32);
+            static_assert(kBlk == 128, "S tile is read with one 128-column TMEM load");
+            tld128(tmem + lane_addr + s_col, sv);
             fence_before();
             __syncwarp();
             if (lane == 0) bar_arrive(&bars->s_free[wg]);
-            // mask + scale; maximum by a tree of independent fmaxf
+            // tree mask (last tiles only), then the raw row maximum; the
+            // scale (> 0) is applied inside the exponent
             const int base = (c0 + i) * kBlk;
-            if (base + kBlk <= kv_len) {
+            if (base + kBlk > kv_len) {
+                uint32_t vis[kBlk / 32];
 #pragma unroll
-                for (int c = 0; c < kBlk; ++c) sv[c] *= p.scale_log2;
-            } else {
+                for (int w = 0; w < kBlk / 32; ++w) vis[w] = visible_bits(base + 32 * w, kv_len, T, a0, a1, a2, a3);
 #pragma unroll
-                for (int c = 0; c < kBlk; ++c) {
-                    const int pos = base + c;
-                    const bool vis = pos < kv_len || (pos < T && anc_has(a0, a1, a2, a3, pos - kv_len));
-                    sv[c] = vis ? sv[c] * p.scale_log2 : -INFINITY;
-                }
+                for (int c = 0; c < kBlk; ++c) sv[c] = ((vis[c >> 5] >> (c & 31)) & 1u) ? sv[c] : -INFINITY;
             }
-            float mq[8];
+            float mq0 = sv[0], mq1 = sv[1], mq2 = sv[2], mq3 = sv[3];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                mq[q] = fmaxf(fmaxf(fmaxf(sv[q], sv[q + 8]), fmaxf(sv[q + 16], sv[q + 24])),
-                              fmaxf(fmaxf(sv[q + 32], sv[q + 40]), fmaxf(sv[q + 48], sv[q + 56])));
+            for (int c = 4; c < kBlk; c += 4) {
+                mq0 = fmaxf(mq0, sv[c]);
+                mq1 = fmaxf(mq1, sv[c + 1]);
+                mq2 = fmaxf(mq2, sv[c + 2]);
+                mq3 = fmaxf(mq3, sv[c + 3]);
             }
-            const float mx = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])),
-                                   fmaxf(fmaxf(mq[4], mq[5]), fmaxf(mq[6], mq[7])));
+            const float mx = fmaxf(fmaxf(mq0, mq1), fmaxf(mq2, mq3)) * p.scale_log2;  // -inf stays -inf
             // previous PV of this warpgroup done: P tile free and O stable
             if (j >= 1 && !__all_sync(kFull, bar_wait(&bars->o_done[wg], (j - 1) & 1, abort_flag))) {
                 ok = false;
@@ -420,8 +531,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             }
             const bool grow = mx > m_used + kRescaleLog2 || (m_used == -INFINITY && mx != -INFINITY);
             const float alpha = grow ? ((m_used == -INFINITY) ? 0.0f : ex2(m_used - mx)) : 1.0f;
-            if (j >= 1 && __any_sync(kFull, grow)) {
-                // O holds this warpgroup's PV up to its previous tile: rescale in TMEM
+            const bool rescale_o = j >= 1 && __any_sync(kFull, grow);
+            if (grow) {
+                l *= alpha;
+                m_used = mx;
+            }
+            // P = exp2(s - m_used) -> bf16, swizzled rows of 128 bytes
+            uint8_t* pbuf = smem + kOffP + wg * kPBytes;
+            const float mneg = m_used == -INFINITY ? 0.0f : -m_used;
+            float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kBlk / 8; ++c) {
+                float e[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) e[q] = ex2(fmaf(sv[c * 8 + q], p.scale_log2, mneg));  // ex2(-inf) = 0
+                const float part = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+                if (c & 1) rs1 += part; else rs0 += part;
+                uint4 w;
+                w.x = pack2(e[0], e[1]);
+                w.y = pack2(e[2], e[3]);
+                w.z = pack2(e[4], e[5]);
+                w.w = pack2(e[6], e[7]);
+                // slot-halves of 64 slots, each a 128B-swizzled 128 x 128-byte tile
+                *reinterpret_cast<uint4*>(pbuf + (c >> 3) * (kRows * 128) + sw128(r, c & 7)) = w;
+            }
+            l += rs0 + rs1;
+            if (rescale_o) {
+                // O holds this warpgroup's PV up to its previous tile: rescale
+                // in TMEM (after the S values are dead, to keep them in registers)
                 fence_after();
 #pragma unroll 1
                 for (int cch = 0; cch < kD; cch += 32) {
@@ -433,28 +570,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                 }
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
-            if (grow) {
-                l *= alpha;
-                m_used = mx;
-            }
-            // P = exp2(s - m_used) -> bf16, swizzled rows of 128 bytes
-            uint8_t* pbuf = smem + kOffP + wg * kPBytes;
-            const float mneg = m_used == -INFINITY ? 0.0f : -m_used;
-            float rsq[8];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                float e[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) e[q] = ex2(sv[c * 8 + q] + mneg);  // ex2(-inf) = 0
-                rsq[c] = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
-                uint4 w;
-                w.x = pack2(e[0], e[1]);
-                w.y = pack2(e[2], e[3]);
-                w.z = pack2(e[4], e[5]);
-                w.w = pack2(e[6], e[7]);
-                *reinterpret_cast<uint4*>(pbuf + sw128(r, c)) = w;
-            }
-            l += ((rsq[0] + rsq[1]) + (rsq[2] + rsq[3])) + ((rsq[4] + rsq[5]) + (rsq[6] + rsq[7]));
             fence_async_smem();
             fence_before();
             __syncwarp();
@@ -463,17 +578,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // ---- epilogue: last PV of this warpgroup, then merge the two states
         if (ok && n_own > 0) ok = __all_sync(kFull, bar_wait(&bars->o_done[wg], (n_own - 1) & 1, abort_flag));
         fence_after();
-        xchg[(2 * wg) * kRows + r] = ok ? m_used : -INFINITY;
-        xchg[(2 * wg + 1) * kRows + r] = ok ? l : 0.0f;
+        // Each warpgroup publishes (m, l) in its own P buffer, dead once its
+        // last PV has completed.  A warpgroup without tiles writes nothing:
+        // its state (m = -inf, l = 0) is implied by the CTA-uniform tile
+        // counts.  (After an abort a PV may still read the buffer; the CTA
+        // then writes no output.)
+        const int n0 = (nmine + 1) / 2, n1 = nmine / 2;
+        if (n_own > 0) {
+            float* mine = reinterpret_cast<float*>(smem + kOffP + wg * kPBytes);  // [m | l] x 128 rows
+            mine[r] = ok ? m_used : -INFINITY;
+            mine[kRows + r] = ok ? l : 0.0f;
+        }
         // both O accumulators are final once both warpgroups pass this barrier
         fence_before();
         asm volatile("bar.sync 2, 256;" ::: "memory");
         fence_after();
-        const float m0 = xchg[r], l0 = xchg[kRows + r], m1 = xchg[2 * kRows + r], l1 = xchg[3 * kRows + r];
+        const float* x0 = reinterpret_cast<const float*>(smem + kOffP);
+        const float* x1 = reinterpret_cast<const float*>(smem + kOffP + kPBytes);
+        const float m0 = n0 > 0 ? x0[r] : -INFINITY, l0 = n0 > 0 ? x0[kRows + r] : 0.0f;
+        const float m1 = n1 > 0 ? x1[r] : -INFINITY, l1 = n1 > 0 ? x1[kRows + r] : 0.0f;
         const float mt = fmaxf(m0, m1);
-        // tile counts are CTA-uniform: a warpgroup without tiles left its O
-        // uninitialised and it is never read
-        const int n0 = (nmine + 1) / 2, n1 = nmine / 2;
+        // a warpgroup without tiles left its O uninitialised and it is never read
         const float w0 = (m0 != -INFINITY) ? ex2(m0 - mt) : 0.0f;
         const float w1 = (m1 != -INFINITY) ? ex2(m1 - mt) : 0.0f;
         const float lt = l0 * w0 + l1 * w1;
