@@ -152,6 +152,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from flashgrpo_b200 import _native
+    from flashgrpo_b200.engine import shard
     from flashgrpo_b200.engine.verify import DecodeState  # noqa: F401
     from flashgrpo_b200.utils import synthetic
 
@@ -161,9 +162,13 @@ def run_ours(args, rank, world, local_rank):
     dec = config2_decoder(device, args.layers, args.attn_splits)
     eng = dec.engine
     spec = eng.spec
+    # the global batch is world x prompts prompt groups; this rank owns a
+    # contiguous range of whole groups (8 samples of a prompt stay together)
     prompts = max(1, args.rows // 8)
-    rows = prompts * 8
-    ids, mask = synthetic.random_prompts(prompts, args.prefix, spec.vocab, seed=100 + rank)
+    my_prompts = shard.prompt_shard(prompts * world, world, rank)
+    ids_all, mask_all = synthetic.random_prompts(prompts * world, args.prefix, spec.vocab, seed=100)
+    ids, mask = ids_all[my_prompts.start:my_prompts.stop], mask_all[my_prompts.start:my_prompts.stop]
+    rows = len(my_prompts) * 8
     W, K = max(args.warmup, 3), max(args.steps, 1)
     capacity = args.prefix + 3 * (W + K + 8) + 32
     n_heads = dec.max_heads()
@@ -219,17 +224,9 @@ def run_ours(args, rank, world, local_rank):
         # the one collective: every rank's per-rollout generated lengths (for
         # the GRPO group statistics), then totals and the slowest clock
         rollout_len = (st.row_len - args.prefix).clone()
-        if world > 1:
-            gathered = [torch.empty_like(rollout_len) for _ in range(world)]
-            dist.all_gather(gathered, rollout_len)
-            t = torch.tensor([ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms_max = float(t.item())
-            a = torch.tensor([accepted], device=device, dtype=torch.int64)
-            dist.all_reduce(a)
-            accepted_all = int(a.item())
-        else:
-            ms_max, accepted_all = ms, accepted
+        lengths_all = shard.gather_rollout_values(rollout_len)
+        ms_max = shard.reduce_scalar(ms, "max", device)
+        accepted_all = int(shard.reduce_scalar(accepted, "sum", device))
         del graphs
         # ---- roofline of the tree-attention kernel (K3)
         N_ = rb.N
@@ -256,14 +253,8 @@ def run_ours(args, rank, world, local_rank):
                 tok += res["total_acc_length"]
                 rounds_total += res["total_verify_rounds"]
             torch.cuda.synchronize()
-            e_s = time.perf_counter() - t0
-            if world > 1:
-                t = torch.tensor([e_s], device=device, dtype=torch.float64)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                e_s = float(t.item())
-                a = torch.tensor([tok], device=device, dtype=torch.int64)
-                dist.all_reduce(a)
-                tok = int(a.item())
+            e_s = shard.reduce_scalar(time.perf_counter() - t0, "max", device)
+            tok = int(shard.reduce_scalar(tok, "sum", device))
             dcap = plan.active_heads + 2
             e2e = {"value": tok / e_s, "unit": UNIT,
                    "h2d_bytes_per_step": int(ids.numel() * 8 + mask.numel() * 8),
@@ -282,6 +273,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "inputs larger than L2: 3.1 GB weights + KV cache re-read every step",
                    "graphs": "each step replays a captured CUDA graph of the round"},
         "accepted_tokens": accepted_all, "average_accept_length": accepted_all / (K * rows * world),
+        "rollouts_gathered": int(lengths_all.numel()),
         "gpu_launches": launches_per_step * K,
         "roofline": {"kernel": "fg_tree_attention (fg::tc::attn_tc_kernel, tcgen05)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -351,7 +343,7 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
     try:
         result = run_ours(args, rank, world, local_rank)
     finally:
