@@ -73,15 +73,18 @@ def profile_traffic() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 20 ms from before
+    the warm-up until after the timed region; `summary` keeps the samples
+    whose timestamps fall inside the timed window (marked with `mark`)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.window = None
         self.path = REPO / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
 
     def __enter__(self):
@@ -89,14 +92,19 @@ class ClockSampler:
             self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                                          "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
+    def mark(self, t0: float, t1: float):
+        """Wall-clock bounds (time.time()) of the timed region."""
+        self.window = (t0, t1)
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -107,22 +115,31 @@ class ClockSampler:
     def summary(self) -> dict:
         if self.proc is None or not self.path.exists():
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], None, set()
+        from datetime import datetime
+
+        samples = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, float(parts[2]), float(parts[3]),
+                                {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = samples
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [x for x in samples if t0 <= x[0] <= t1]
+            if not inside and samples:  # region shorter than the sampling period: nearest sample
+                mid = 0.5 * (t0 + t1)
+                inside = [min(samples, key=lambda x: abs(x[0] - mid))]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": inside[-1][2],
+                "reasons": sorted(set().union(*(x[3] for x in inside))), "samples": len(inside)}
 
 
 # --------------------------------------------------------------- workload
@@ -194,6 +211,7 @@ def run_ours(args, rank, world, local_rank):
             g = eng.graph_round(st, rb, params, rcfg, pool=pool, attn_events=events[gi])
             pool = g.pool()
             graphs.append(g)
+        clocks = ClockSampler(local_rank).__enter__()
         for i in range(W - 1):
             graphs[i % G].replay()
         torch.cuda.synchronize()
@@ -204,12 +222,14 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local_rank) as clocks:
-            t_start.record()
-            for i in range(K):
-                graphs[i % G].replay()
-            t_end.record()
-            torch.cuda.synchronize()
+        w0 = time.time()
+        t_start.record()
+        for i in range(K):
+            graphs[i % G].replay()
+        t_end.record()
+        torch.cuda.synchronize()
+        clocks.mark(w0, time.time())
+        clocks.__exit__(None, None, None)
         if world > 1:
             dist.barrier()
         ms = t_start.elapsed_time(t_end)
