@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-splits", type=int, default=0)
+    ap.add_argument("--lm-head", choices=["fused", "separate"], default="fused",
+                    help="proposal lm_head: tcgen05 GEMM with fused top-k, or cuBLAS + row top-k")
     return ap.parse_args()
 
 
@@ -143,7 +145,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- workload
-def config2_decoder(device, layers=None, attn_splits=0):
+def config2_decoder(device, layers=None, attn_splits=0, lm_head="fused"):
     import torch
 
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -159,7 +161,8 @@ def config2_decoder(device, layers=None, attn_splits=0):
 
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode="concurrency_aware", cpeak_nodes=1024,
                             max_tree_nodes_per_seq=16, max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2),
-                            temperature=1.0, top_p=1.0, sampling_seed=1234, attention_splits=attn_splits)
+                            temperature=1.0, top_p=1.0, sampling_seed=1234, attention_splits=attn_splits,
+                            lm_head_kernel=lm_head)
     torch.cuda.synchronize()
     return FlashMedusaDecoder(model, heads, Tok(), cfg)
 
@@ -176,7 +179,7 @@ def run_ours(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     torch.manual_seed(0)
-    dec = config2_decoder(device, args.layers, args.attn_splits)
+    dec = config2_decoder(device, args.layers, args.attn_splits, args.lm_head)
     eng = dec.engine
     spec = eng.spec
     # the global batch is world x prompts prompt groups; this rank owns a
@@ -289,7 +292,8 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": WORKLOAD, "rollouts_per_gpu": rows, "prompts_per_gpu": prompts,
                    "samples_per_prompt": 8, "prefix_tokens": args.prefix, "tree": plan.topk_by_depth,
                    "tree_nodes": rb.N, "layers": spec.n_layers, "medusa_heads": 3, "active_heads": plan.active_heads,
-                   "temperature": 1.0, "top_p": 1.0, "parallelism": f"dp{world} (rollouts sharded by prompt group)",
+                   "temperature": 1.0, "top_p": 1.0, "lm_head": args.lm_head,
+                   "parallelism": f"dp{world} (rollouts sharded by prompt group)",
                    "l2": "inputs larger than L2: 3.1 GB weights + KV cache re-read every step",
                    "graphs": "each step replays a captured CUDA graph of the round"},
         "accepted_tokens": accepted_all, "average_accept_length": accepted_all / (K * rows * world),

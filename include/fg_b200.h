@@ -105,6 +105,25 @@ fg_status fg_sample_rows(const void *logits, int32_t dtype, int64_t row_stride, 
 fg_status fg_row_topk(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
                       int32_t k, int32_t *out_idx, float *out_val, float *out_max, float *out_lse, void *stream);
 
+/* The tied lm_head of the proposal rows on the tensor cores with the top-k
+ * fused: logits[r, v] = bf16(x[r, :] . w[v, :]) for x [M, H] (M <= 256,
+ * H a multiple of 64), w [V, H] (bf16, row strides x_ld / w_ld elements).
+ * Rows [0, n_logit_rows) write their logits to `logits` (row stride
+ * logits_ld); rows [topk_row0, M) produce, in row order from topk_row0, what
+ * fg_row_topk returns on those logits (k best by value desc / index asc,
+ * maximum, logsumexp rounded to bf16 when out_lse != NULL) without writing
+ * them.  topk_row0 == M skips the top-k.  workspace:
+ * fg_lm_head_topk_workspace_size bytes (no zero-fill needed).  Replaces the
+ * concat-heads lm_head of _medusa_logits_for_last_hidden
+ * (flashgrpo_b200/decoding/flash_medusa_decoder.py:906-1005) followed by the
+ * torch.topk of build_batch_trees (medusa_tree.py:767) and the confidence
+ * reductions (flash_medusa_decoder.py:1034-1040).  dtype FG_DTYPE_BF16 only. */
+size_t fg_lm_head_topk_workspace_size(int32_t M, int32_t V, int32_t topk_row0, int32_t k);
+fg_status fg_lm_head_topk(const void *x, int32_t dtype, int64_t x_ld, int32_t M, int32_t H, const void *w,
+                          int64_t w_ld, int32_t V, int32_t n_logit_rows, void *logits, int64_t logits_ld,
+                          int32_t topk_row0, int32_t k, int32_t *out_idx, float *out_val, float *out_max,
+                          float *out_lse, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------ tree build */
 typedef struct fg_plan_params {
     int32_t tree_mode;          /* 0 = "fixed", 1 = "concurrency_aware", 2 = explicit

@@ -10,3 +10,4 @@
 #include "fg_attention_tc.cu"
 #include "fg_attention.cu"
 #include "fg_attention_noalloc.cu"
+#include "fg_lmhead_tc.cu"

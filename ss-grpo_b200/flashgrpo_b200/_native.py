@@ -66,6 +66,9 @@ SIGNATURES = {
     "fg_philox_uniforms": (c_i32, [c_u64, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp]),
     "fg_sample_rows": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_f32, c_vp, c_vp, c_vp]),
     "fg_row_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "fg_lm_head_topk_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32]),
+    "fg_lm_head_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32,
+                                c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                               c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
@@ -116,7 +119,7 @@ def load():
 
 # Entry points that enqueue exactly one kernel; `launches` counts them so a
 # caller can report how many of this library's kernels a step runs.
-LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_build_tree",
+LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
              "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows"}
 launches = 0

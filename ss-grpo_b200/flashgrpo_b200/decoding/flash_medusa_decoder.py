@@ -63,6 +63,7 @@ class FlashMedusaConfig:
     sampling_seed: int = 0
     use_cuda_graphs: bool = True
     attention_splits: int = 0
+    lm_head_kernel: str = "fused"  # "fused" (tcgen05 + top-k epilogue) or "separate" (cuBLAS + fg_row_topk)
 
 
 class FlashMedusaDecoder:
@@ -87,6 +88,8 @@ class FlashMedusaDecoder:
             raise NotImplementedError("nucleus sampling (top_p < 1) is not on the B200 path yet; use top_p=1.0")
         if config.top_k is not None:
             raise NotImplementedError("top_k sampling is not on the B200 path yet")
+        if config.lm_head_kernel not in {"fused", "separate"}:
+            raise ValueError(f"Unsupported lm_head_kernel={config.lm_head_kernel}")
         self._engine: VerifyEngine | None = None
         # captured round graphs, keyed by (state, round shape, round config);
         # a shape is run eagerly once before it is captured
@@ -126,7 +129,7 @@ class FlashMedusaDecoder:
         eos = eos if eos is not None else (pad if pad is not None else 0)
         return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), eos_id=int(eos),
                            max_length=int(max_length), seed=int(cfg.sampling_seed),
-                           attn_splits=int(cfg.attention_splits))
+                           attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel))
 
     def max_heads(self) -> int:
         cfg = self.config

@@ -135,6 +135,10 @@ class RoundConfig:
     max_length: int = 1 << 30
     seed: int = 0
     attn_splits: int = 0
+    # proposal lm_head: "fused" = tcgen05 GEMM with the top-k in its epilogue
+    # (bf16, hidden a multiple of 64, <= 256 rows), "separate" = cuBLAS GEMM
+    # then fg_row_topk
+    lm_head: str = "fused"
 
 
 class DecodeState:
@@ -287,6 +291,19 @@ class VerifyEngine:
             self._graphs[key] = RoundBuffers(self.spec, B, plan, n_heads, self.device, dcap, adaptive)
         return self._graphs[key]
 
+    def _fused_lm_head(self, cfg: RoundConfig, M: int) -> bool:
+        sp = self.spec
+        return (cfg.lm_head == "fused" and sp.dtype == torch.bfloat16 and sp.hidden % 64 == 0 and M <= 256
+                and self.w.lm_head.stride(1) == 1)
+
+    def _lm_head_ws(self, M: int, topk_row0: int, k: int) -> torch.Tensor:
+        need = ops.lm_head_topk_workspace_bytes(M, self.spec.vocab, topk_row0, k)
+        ws = getattr(self, "_lmh_ws", None)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.empty(max(need, 16) // 4 + 64, dtype=torch.int32, device=self.device)
+            self._lmh_ws = ws
+        return ws
+
     def _attn_workspace(self, rb: RoundBuffers, st: DecodeState, splits: int):
         need = ops.attention_workspace_bytes(st.B, rb.N, self.spec.n_q_heads, self.spec.n_kv_heads,
                                              self.spec.head_dim, num_splits=splits, max_kv_len=st.capacity)
@@ -302,12 +319,20 @@ class VerifyEngine:
             ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
             torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
             ops.silu_residual(h, rb.fc, out=st.X[(i + 1) * B:(i + 2) * B])
-        torch.mm(st.X[: (nh + 1) * B], self.w.lm_head.t(), out=rb.logits)
+        M = (nh + 1) * B
+        if self._fused_lm_head(cfg, M):
+            # root rows keep their logits (the sampler reads them); head rows
+            # only produce their top-k (fg_row_topk semantics)
+            ws = self._lm_head_ws(M, B, rb.kmax)
+            ops.lm_head_topk(st.X[:M], self.w.lm_head, n_logit_rows=B, logits=rb.logits, topk_row0=B, k=rb.kmax,
+                             topk_out=rb.topk if nh > 0 else None, workspace=ws)
+        else:
+            torch.mm(st.X[:M], self.w.lm_head.t(), out=rb.logits[:M])
+            if nh > 0:
+                ops.row_topk(rb.logits[B:M], rb.kmax, out=rb.topk)
         ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
                         forced=st.pending, out=rb.root)
-        if nh > 0:
-            ops.row_topk(rb.logits[B:(nh + 1) * B], rb.kmax, out=rb.topk)
 
     def build_tree(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams):
         nh = rb.n_heads
@@ -386,6 +411,9 @@ class VerifyEngine:
         """Captures run_round for this (state, buffers, plan); replay() runs it.
         attn_events must be created with external=True to be captured."""
         self._attn_workspace(rb, st, cfg.attn_splits)
+        M = (rb.n_heads + 1) * st.B
+        if self._fused_lm_head(cfg, M):
+            self._lm_head_ws(M, st.B, rb.kmax)  # allocated outside the capture
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=pool):
             self.run_round(st, rb, params, cfg, attn_events)

@@ -92,6 +92,31 @@ def row_topk(logits: torch.Tensor, k: int, out=None, *, with_lse: bool = True):
     return out
 
 
+def lm_head_topk_workspace_bytes(M: int, V: int, topk_row0: int, k: int) -> int:
+    return int(N.load().fg_lm_head_topk_workspace_size(int(M), int(V), int(topk_row0), int(k)))
+
+
+def lm_head_topk(x: torch.Tensor, weight: torch.Tensor, *, n_logit_rows: int, logits: torch.Tensor | None,
+                 topk_row0: int, k: int, topk_out, workspace: torch.Tensor):
+    """Fused lm_head + top-k (bf16): logits of rows [0, n_logit_rows) into
+    `logits`, and for rows [topk_row0, M) the fg_row_topk outputs
+    (idx, val, max, lse-or-None) in `topk_out`."""
+    _need(x, "x", contiguous=False)
+    _need(weight, "weight", contiguous=False)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise ValueError("lm_head_topk is the bf16 path")
+    M, H = x.shape
+    V = weight.shape[0]
+    if x.stride(1) != 1 or weight.stride(1) != 1 or (logits is not None and logits.stride(1) != 1):
+        raise ValueError("rows must be contiguous")
+    idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
+    N.call("fg_lm_head_topk", _ptr(x), N.FG_DTYPE_BF16, x.stride(0), M, H, _ptr(weight), weight.stride(0), V,
+           int(n_logit_rows), _ptr(logits), logits.stride(0) if logits is not None else 0, int(topk_row0), int(k),
+           _ptr(idx), _ptr(val), _ptr(mx), _ptr(lse), _ptr(workspace),
+           workspace.numel() * workspace.element_size() if workspace is not None else 0, _stream(x))
+    return topk_out
+
+
 # ---------------------------------------------------------------- planning
 def plan_params(*, tree_mode: str, active_batch_size: int, num_medusa_heads: int, cpeak_nodes: int,
                 min_tree_nodes_per_seq: int, max_tree_nodes_per_seq: int, max_tree_depth: int,

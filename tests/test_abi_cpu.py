@@ -46,6 +46,15 @@ def test_host_only_entry_points():
                            ctypes.c_void_p(16), ctypes.c_void_p(16), None) == _native.FG_ECAPACITY
     assert lib.fg_tree_attention_workspace_size(64, 13, 12, 2, 128, 1, 1024) == 0
     assert lib.fg_tree_attention_workspace_size(64, 13, 12, 2, 128, 2, 1024) > 0
+    # fused lm_head + top-k: shape limits are checked before any CUDA call
+    p = ctypes.c_void_p(256)
+    lmh = lambda dtype, M, H, k: lib.fg_lm_head_topk(p, dtype, H, M, H, p, H, 1000, 0, None, 0, 0, k, p, p, p, None,
+                                                      p, 1 << 20, None)
+    assert lmh(_native.FG_DTYPE_F32, 64, 128, 4) == _native.FG_EUNSUPPORTED
+    assert lmh(_native.FG_DTYPE_BF16, 257, 128, 4) == _native.FG_ECAPACITY
+    assert lmh(_native.FG_DTYPE_BF16, 64, 100, 4) == _native.FG_ECAPACITY
+    assert lib.fg_lm_head_topk_workspace_size(192, 151936, 64, 4) > 0
+    assert lib.fg_lm_head_topk_workspace_size(192, 151936, 192, 4) == 0
 
 
 def test_plan_params_tables():

@@ -98,6 +98,57 @@ def test_row_topk_stable_and_lse(ops, dtype, V, k):
     assert torch.allclose(lse.cpu(), ref_lse, rtol=tol, atol=tol)
 
 
+# ---------------------------------------------------- fused lm_head + top-k
+@pytest.mark.parametrize("M,H,V,n_write,row0,k,lse", [
+    (192, 1536, 151936, 64, 64, 4, False),   # config 2: 64 root rows + 2 heads x 64 rows
+    (192, 1536, 151936, 64, 64, 4, True),
+    (130, 256, 5000, 2, 2, 8, True),         # second M block with 2 rows
+    (64, 512, 1000, 0, 0, 16, True),         # V not a multiple of 16
+    (256, 128, 32000, 256, 0, 2, False),     # all rows write logits and get top-k
+    (7, 64, 300, 7, 3, 1, False),
+    (40, 192, 2064, 40, 40, 4, False),       # logits only
+])
+def test_lm_head_topk_matches_gemm_then_row_topk(ops, M, H, V, n_write, row0, k, lse):
+    g = torch.Generator().manual_seed(M * 31 + V)
+    x = (torch.randn(M, H, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    x[min(1, M - 1)] = 0  # an all-tied row: every logit is 0
+    ref = (x.float() @ w.float().t())
+    n_top = M - row0
+    ws = torch.empty(max(ops.lm_head_topk_workspace_bytes(M, V, row0, k), 16) // 4 + 4, dtype=torch.int32, device=DEV)
+    mk = lambda: (torch.empty((n_top, k), dtype=torch.int32, device=DEV),
+                  torch.empty((n_top, k), dtype=torch.float32, device=DEV),
+                  torch.empty(n_top, dtype=torch.float32, device=DEV),
+                  torch.empty(n_top, dtype=torch.float32, device=DEV) if lse else None)
+    # pass 1: every row's logits written, so the fused top-k can be checked
+    # against fg_row_topk on exactly the values the kernel produced
+    full = torch.full((M, V), float("nan"), dtype=torch.bfloat16, device=DEV)
+    out1 = mk() if n_top > 0 else None
+    ops.lm_head_topk(x, w, n_logit_rows=M, logits=full, topk_row0=row0, k=k, topk_out=out1, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.isfinite(full.float()).all()
+    err = (full.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+    if n_top > 0:
+        want = ops.row_topk(full[row0:], k, with_lse=lse)
+        assert torch.equal(out1[0], want[0])
+        assert torch.equal(out1[1], want[1])
+        assert torch.equal(out1[2], want[2])
+        if lse:
+            assert torch.allclose(out1[3], want[3], rtol=1e-2, atol=1e-2)
+    # pass 2: only the first n_write rows written; same top-k, same rows
+    part = torch.full((M, V), float("nan"), dtype=torch.bfloat16, device=DEV)
+    out2 = mk() if n_top > 0 else None
+    ops.lm_head_topk(x, w, n_logit_rows=n_write, logits=part, topk_row0=row0, k=k, topk_out=out2, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(part[:n_write], full[:n_write])
+    assert torch.isnan(part[n_write:].float()).all()
+    if n_top > 0:
+        for a, b in zip(out1, out2):
+            if a is not None:
+                assert torch.equal(a, b)
+
+
 # -------------------------------------------------------------- tree build
 def _check_tree(ops, *, tree_mode, B, cpeak, mx, depth, fixed, n_heads, V=300, adaptive=False, amin=(1, 1, 1),
                 metric="top1_prob", seed=0, dtype=torch.bfloat16):
