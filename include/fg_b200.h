@@ -36,6 +36,14 @@
  *   t* = the chunk with P_t <= target < P_{t+1};
  *   token = first i of chunk t* with P_t* + c_i > target.
  *   Greedy (do_sample == 0 or T == 0): first index of the maximum logit.
+ * Nucleus variant "fg-icdf-v1n" (0 < top_p < 1), on exact integer masses:
+ *   q_i = trunc(e_i * 2^40) (uint64), Z = sum q_i,
+ *   P = trunc(double(top_p) * double(Z)); order entries by key descending,
+ *   index ascending, key = order-preserving image of x (-0 as +0); the
+ *   boundary K* is the first position whose cumulative mass exceeds P (mass
+ *   S there); kept = entries before or at K*;
+ *   t = trunc(double(u) * double(S)); token = first index (ascending) among
+ *   kept entries whose running kept mass exceeds t.
  */
 #ifndef FG_B200_H_
 #define FG_B200_H_
@@ -53,7 +61,7 @@ typedef int32_t fg_status;
 #define FG_ECAPACITY 2    /* a size exceeds a compile-time or buffer capacity */
 #define FG_ETIMEOUT 3     /* a device-side wait gave up */
 #define FG_ECUDA 4        /* a CUDA launch/runtime call failed; see fg_last_cuda_error */
-#define FG_EUNSUPPORTED 5 /* configuration not implemented (e.g. top_p < 1) */
+#define FG_EUNSUPPORTED 5 /* configuration not implemented (e.g. a dtype a kernel does not take) */
 
 #define FG_DTYPE_F32 0
 #define FG_DTYPE_BF16 1
@@ -86,15 +94,17 @@ fg_status fg_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *status_
 fg_status fg_philox_uniforms(uint64_t seed, const int32_t *seq_ids, int32_t n_rows, int32_t round_idx,
                              const int32_t *round_dev, int32_t n_draws, float *out, void *stream);
 
-/* One fg-icdf-v1 token per row of logits [n_rows, row_stride] (dtype
- * FG_DTYPE_*), uniform uniforms[r * u_stride].  forced (nullable): rows with
- * forced[r] >= 0 take that token instead (pending correction tokens).
- * Replaces sample_from_logits with top_p = 1, top_k = None
+/* One token per row of logits [n_rows, row_stride] (dtype FG_DTYPE_*),
+ * uniform uniforms[r * u_stride]: fg-icdf-v1 for top_p >= 1 (or <= 0), the
+ * nucleus variant fg-icdf-v1n for 0 < top_p < 1 (the kept set of
+ * logits_to_probs, acceptance.py:7-31, on exact integer masses).  forced
+ * (nullable): rows with forced[r] >= 0 take that token instead (pending
+ * correction tokens).  Replaces sample_from_logits with top_k = None
  * (flashgrpo_b200/decoding/acceptance.py:34-130) for the root token of a
  * round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1717-1743). */
 fg_status fg_sample_rows(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
                          const float *uniforms, int64_t u_stride, int32_t do_sample, float temperature,
-                         const int32_t *forced, int32_t *out_tokens, void *stream);
+                         float top_p, const int32_t *forced, int32_t *out_tokens, void *stream);
 
 /* Per row: the k best entries ordered by (value descending, index
  * ascending), the row maximum and logsumexp (rounded to the logits dtype,
@@ -237,6 +247,7 @@ typedef struct fg_accept_args {
     int32_t B;
     int32_t do_sample;
     float temperature;
+    float top_p;               /* 0 < top_p < 1: nucleus draws (fg-icdf-v1n) */
     int32_t eos_id;
     int32_t max_length;
     int32_t *row_len;          /* [B] logical length before the round; advanced if update_len */

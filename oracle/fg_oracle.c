@@ -38,6 +38,19 @@
  *   greedy (do_sample == 0 or T == 0): first index of the maximum logit,
  *   matching torch.argmax (acceptance.py:43-44).
  *
+ * Nucleus variant "fg-icdf-v1n" (0 < top_p < 1), the kept set of
+ * logits_to_probs / sample_from_logits (acceptance.py:7-31, 63-124) stated on
+ * exact integer masses so that any summation order gives the same result:
+ *   q_i      = trunc(e_i * 2^40)                  (uint64)
+ *   Z        = sum q_i,  P = trunc(double(top_p) * double(Z))
+ *   key_i    = order-preserving 32-bit image of x_i (-0 counted as +0)
+ *   sorted   = key descending, index ascending
+ *   K*       = first sorted position whose running mass exceeds P; S is the
+ *              running mass there; kept = sorted positions <= K*
+ *   t        = trunc(double(u) * double(S))
+ *   token    = first index (ascending) among kept entries whose running kept
+ *              mass exceeds t.
+ *
  * Build: oracle/build_oracle.sh (gcc -O2 -ffp-contract=off, no fast-math).
  */
 #include <math.h>
@@ -188,10 +201,114 @@ int32_t fgo_sample_row(const float *logits, int32_t V, float temperature, int32_
     return -1; /* S == 0: every logit is NaN or -inf */
 }
 
+/* ---------------------------------------------------- nucleus (v1n) draw */
+
+typedef struct {
+    uint32_t key;
+    int32_t idx;
+} fgo_keyed;
+
+static uint32_t fgo_nucleus_key(float x) {
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    if (b == 0x80000000u) b = 0u;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+static int fgo_keyed_cmp(const void *pa, const void *pb) {
+    const fgo_keyed *a = (const fgo_keyed *)pa, *b = (const fgo_keyed *)pb;
+    if (a->key != b->key) return a->key > b->key ? -1 : 1;
+    return a->idx < b->idx ? -1 : (a->idx > b->idx ? 1 : 0);
+}
+
+/* The fg-icdf-v1n boundary of one row by an explicit sort (see the header):
+ * fills q[V] and returns the boundary index (-1 if every entry is NaN/-inf),
+ * with its key in *tau and the running mass there in *S. */
+static int32_t fgo_nucleus_boundary(const float *logits, int32_t V, float temperature, float top_p, uint64_t *q,
+                                    uint32_t *tau_out, uint64_t *S_out) {
+    float m = -INFINITY;
+    for (int32_t i = 0; i < V; ++i) m = fmaxf(m, fgo_scaled(logits, i, temperature));
+    if (!(m > -INFINITY)) return -1;
+    fgo_keyed *ord = (fgo_keyed *)malloc((size_t)V * sizeof(fgo_keyed));
+    if (!ord) return -1;
+    uint64_t Z = 0;
+    for (int32_t i = 0; i < V; ++i) {
+        const float x = fgo_scaled(logits, i, temperature);
+        const float e = fgo_exp(x - m);
+        q[i] = (uint64_t)(e * 1099511627776.0f); /* 2^40, exact scaling; truncation */
+        ord[i].key = fgo_nucleus_key(x);
+        ord[i].idx = i;
+        Z += q[i];
+    }
+    const uint64_t P = (uint64_t)((double)top_p * (double)Z);
+    qsort(ord, (size_t)V, sizeof(fgo_keyed), fgo_keyed_cmp);
+    uint64_t cum = 0;
+    int32_t istar = -1;
+    for (int32_t k = 0; k < V; ++k) {
+        cum += q[ord[k].idx];
+        if (cum > P) {
+            *tau_out = ord[k].key;
+            istar = ord[k].idx;
+            *S_out = cum;
+            break;
+        }
+    }
+    free(ord);
+    return istar;
+}
+
+/* Kept set of the fg-icdf-v1n nucleus (mask[i] = 1 for kept entries). */
+int32_t fgo_nucleus_kept(const float *logits, int32_t V, float temperature, float top_p, uint8_t *mask) {
+    uint64_t *q = (uint64_t *)malloc((size_t)V * sizeof(uint64_t));
+    if (!q) return -1;
+    uint32_t tau = 0;
+    uint64_t S = 0;
+    const int32_t istar = fgo_nucleus_boundary(logits, V, temperature, top_p, q, &tau, &S);
+    for (int32_t i = 0; i < V; ++i) {
+        const uint32_t key = fgo_nucleus_key(fgo_scaled(logits, i, temperature));
+        mask[i] = (istar >= 0 && (key > tau || (key == tau && i <= istar))) ? 1 : 0;
+    }
+    free(q);
+    return istar;
+}
+
+/* fg-icdf-v1n sample of one row (see the header). */
+int32_t fgo_sample_row_nucleus(const float *logits, int32_t V, float temperature, float top_p, float u) {
+    uint64_t *q = (uint64_t *)malloc((size_t)V * sizeof(uint64_t));
+    if (!q) return -1;
+    uint32_t tau = 0;
+    uint64_t S = 0;
+    const int32_t istar = fgo_nucleus_boundary(logits, V, temperature, top_p, q, &tau, &S);
+    int32_t token = -1;
+    if (istar >= 0) {
+        const uint64_t t = (uint64_t)((double)u * (double)S);
+        uint64_t run = 0;
+        for (int32_t i = 0; i < V; ++i) {
+            const uint32_t key = fgo_nucleus_key(fgo_scaled(logits, i, temperature));
+            if (key > tau || (key == tau && i <= istar)) {
+                run += q[i];
+                if (run > t) {
+                    token = i;
+                    break;
+                }
+            }
+        }
+    }
+    free(q);
+    return token;
+}
+
+/* Dispatch: greedy, fg-icdf-v1 (top_p outside (0, 1)) or fg-icdf-v1n. */
+int32_t fgo_sample_row_p(const float *logits, int32_t V, float temperature, int32_t do_sample, float top_p, float u) {
+    if (!do_sample || temperature == 0.0f) return fgo_argmax(logits, V);
+    if (top_p > 0.0f && top_p < 1.0f) return fgo_sample_row_nucleus(logits, V, temperature, top_p, u);
+    return fgo_sample_row(logits, V, temperature, do_sample, u);
+}
+
 void fgo_sample_rows(const float *logits, int64_t row_stride, int32_t V, int32_t n_rows, const float *uniforms,
-                     int32_t do_sample, float temperature, int32_t *out) {
+                     int32_t do_sample, float temperature, float top_p, int32_t *out) {
     for (int32_t r = 0; r < n_rows; ++r)
-        out[r] = fgo_sample_row(logits + (int64_t)r * row_stride, V, temperature, do_sample, uniforms[r]);
+        out[r] = fgo_sample_row_p(logits + (int64_t)r * row_stride, V, temperature, do_sample, top_p, uniforms[r]);
 }
 
 /* ------------------------------------------------------- acceptance walk */
@@ -208,7 +325,7 @@ void fgo_sample_rows(const float *logits, int64_t row_stride, int32_t V, int32_t
 int32_t fgo_accept_walk(const float *logits, int64_t row_stride, int32_t V, const int32_t *slot,
                         const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes, int32_t nmax,
                         const float *uniforms, int32_t u_stride, int32_t B, int32_t do_sample, float temperature,
-                        int32_t eos_id, int32_t max_length, const int32_t *row_len, int32_t dcap,
+                        float top_p, int32_t eos_id, int32_t max_length, const int32_t *row_len, int32_t dcap,
                         int32_t *acc_tokens, int32_t *acc_nodes, int32_t *acc_len, int32_t *raw_len,
                         int32_t *correction, int32_t *pending, int32_t *last_node, int32_t *finished) {
     for (int32_t b = 0; b < B; ++b) {
@@ -231,8 +348,8 @@ int32_t fgo_accept_walk(const float *logits, int64_t row_stride, int32_t V, cons
             if (first_child < 0) break;
             const int32_t s = sl[parent];
             if (s < 0) return -(b + 1);
-            const int32_t sampled = fgo_sample_row(logits + (int64_t)s * row_stride, V, temperature, do_sample,
-                                                   uniforms[(int64_t)b * u_stride + step]);
+            const int32_t sampled = fgo_sample_row_p(logits + (int64_t)s * row_stride, V, temperature, do_sample,
+                                                     top_p, uniforms[(int64_t)b * u_stride + step]);
             ++step;
             int32_t match = -1;
             for (int32_t j = first_child; j < n; ++j)

@@ -282,11 +282,12 @@ class CallOrderSampler:
         self.seed = int(seed)
         self.calls = 0
 
-    def __call__(self, logits_rows: torch.Tensor, seq_ids, round_idx, draw, *, do_sample, temperature):
+    def __call__(self, logits_rows: torch.Tensor, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0):
         u = np.array([native.uniform(self.seed, k, self.calls, 0) for k in range(logits_rows.shape[0])],
                      dtype=np.float32)
         self.calls += 1
-        return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature)
+        return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature,
+                                  top_p=top_p)
 
 
 class SeqRoundSampler:
@@ -298,12 +299,13 @@ class SeqRoundSampler:
     def __init__(self, seed=0):
         self.seed = int(seed)
 
-    def __call__(self, logits_rows, seq_ids, round_idx, draw, *, do_sample, temperature):
+    def __call__(self, logits_rows, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0):
         u = np.array([native.uniform(self.seed, int(s), int(round_idx), int(draw)) for s in seq_ids], dtype=np.float32)
-        return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature)
+        return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature,
+                                  top_p=top_p)
 
 
-def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *, do_sample, temperature):
+def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *, do_sample, temperature, top_p=1.0):
     """Depth-synchronous exact_target walk (acceptance.py:183-267)."""
     B = len(trees)
     acc_tokens = [[int(t.tokens[0])] for t in trees]
@@ -315,7 +317,7 @@ def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *,
     while active:
         rows = torch.stack([tree_logits[slots[b][parent[b]]] for b in active])
         sampled = sampler(rows, [seq_ids[b] for b in active], round_idx, 1 + step,
-                          do_sample=do_sample, temperature=temperature)
+                          do_sample=do_sample, temperature=temperature, **({"top_p": top_p} if top_p != 1.0 else {}))
         step += 1
         still = []
         for b, tok in zip(active, sampled.tolist()):
@@ -480,7 +482,8 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
         root = [0] * B
         if fresh:
             toks = sampler(cur_logits[fresh], [active_ids[r] for r in fresh], round_idx, 0,
-                           do_sample=cfg.do_sample, temperature=cfg.temperature)
+                           do_sample=cfg.do_sample, temperature=cfg.temperature,
+                           **({"top_p": cfg.top_p} if cfg.top_p != 1.0 else {}))
             for r, t in zip(fresh, toks.tolist()):
                 root[r] = int(t)
         for r in range(B):
@@ -526,7 +529,7 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
         else:
             raw_tok, raw_nodes, _, raw_corr = accept_walk_batch(trees, tree_logits, slots, sampler, active_ids,
                                                                 round_idx, do_sample=cfg.do_sample,
-                                                                temperature=cfg.temperature)
+                                                                temperature=cfg.temperature, top_p=cfg.top_p)
         acc, acc_nodes, fin = [], [], []
         for r in range(B):
             tk = raw_tok[r][: max(1, int(remaining[r]))]

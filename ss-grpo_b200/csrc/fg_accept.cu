@@ -16,6 +16,7 @@
 // any, so no ordering between threads is needed.
 #include "fg_common.cuh"
 #include "fg_sampler.cuh"
+#include "fg_nucleus.cuh"
 
 namespace fg {
 
@@ -39,6 +40,7 @@ struct AcceptParams {
     int32_t u_stride;
     int32_t do_sample;
     float temperature;
+    float top_p;
     int32_t eos_id;
     int32_t max_length;
     int32_t* row_len;
@@ -96,6 +98,7 @@ __device__ void compact_row(const KvPtrs& kv, int32_t n_layers, int32_t elem_byt
 template <typename T>
 __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptParams p, KvPtrs kv) {
     __shared__ SampleSmem sm;
+    __shared__ NucleusSmem ns;
     __shared__ int32_t s_child;
     __shared__ int32_t s_match;
     __shared__ int32_t s_path[FG_MAX_PATH];
@@ -151,8 +154,10 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
             break;
         }
         const T* row = static_cast<const T*>(p.logits) + (int64_t)srow * p.logits_row_stride;
-        const int32_t drawn = block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0,
-                                              p.uniforms[(int64_t)b * p.u_stride + step], sm);
+        const float u = p.uniforms[(int64_t)b * p.u_stride + step];
+        const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
+        const int32_t drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
+                                      : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
         if (tid == 0) s_match = 0x7fffffff;
         __syncthreads();
         for (int32_t j = s_child + tid; j < n; j += blockDim.x)
@@ -272,6 +277,7 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     p.u_stride = a->u_stride;
     p.do_sample = a->do_sample;
     p.temperature = a->temperature;
+    p.top_p = a->top_p;
     p.eos_id = a->eos_id;
     p.max_length = a->max_length;
     p.row_len = a->row_len;

@@ -84,8 +84,6 @@ class FlashMedusaDecoder:
             raise NotImplementedError("sparse tree layouts belong to the Reflex/HRDCR subsystem (tree_layout='dense')")
         if config.reflex_enabled:
             raise NotImplementedError("Reflex/HRDCR proposal adaptation is not on the B200 path")
-        if config.do_sample and config.temperature != 0 and config.top_p is not None and 0 < float(config.top_p) < 1:
-            raise NotImplementedError("nucleus sampling (top_p < 1) is not on the B200 path yet; use top_p=1.0")
         if config.top_k is not None:
             raise NotImplementedError("top_k sampling is not on the B200 path yet")
         if config.lm_head_kernel not in {"fused", "separate"}:
@@ -127,7 +125,9 @@ class FlashMedusaDecoder:
         eos = getattr(self.tokenizer, "eos_token_id", None)
         pad = getattr(self.tokenizer, "pad_token_id", None)
         eos = eos if eos is not None else (pad if pad is not None else 0)
-        return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), eos_id=int(eos),
+        top_p = 1.0 if cfg.top_p is None else float(cfg.top_p)
+        return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), top_p=top_p,
+                           eos_id=int(eos),
                            max_length=int(max_length), seed=int(cfg.sampling_seed),
                            attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel))
 

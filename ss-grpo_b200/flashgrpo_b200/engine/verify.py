@@ -131,6 +131,7 @@ class HeadWeights:
 class RoundConfig:
     do_sample: bool = True
     temperature: float = 1.0
+    top_p: float = 1.0  # 0 < top_p < 1: nucleus draws (fg-icdf-v1n)
     eos_id: int = 1
     max_length: int = 1 << 30
     seed: int = 0
@@ -332,7 +333,7 @@ class VerifyEngine:
                 ops.row_topk(rb.logits[B:M], rb.kmax, out=rb.topk)
         ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
-                        forced=st.pending, out=rb.root)
+                        top_p=cfg.top_p, forced=st.pending, out=rb.root)
 
     def build_tree(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams):
         nh = rb.n_heads
@@ -389,7 +390,7 @@ class VerifyEngine:
         outs["pending"] = st.pending
         ops.accept_extract(logits=rb.tree_logits, slot=rb.tree["slot"], tokens=rb.tree["tokens"],
                            parents=rb.tree["parents"], n_nodes=None, n_nodes_shared=rb.N, uniforms=rb.U[:, 1:],
-                           do_sample=cfg.do_sample, temperature=cfg.temperature, eos_id=cfg.eos_id,
+                           do_sample=cfg.do_sample, temperature=cfg.temperature, top_p=cfg.top_p, eos_id=cfg.eos_id,
                            max_length=cfg.max_length, row_len=st.row_len, outputs=outs, dcap=rb.dcap,
                            update_len=True, active=st.active, k_layers=[st.k[l] for l in range(self.spec.n_layers)],
                            v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,

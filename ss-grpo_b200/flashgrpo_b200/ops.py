@@ -60,8 +60,10 @@ def philox_uniforms(seed: int, seq_ids: torch.Tensor, round_idx: int, n_draws: i
 
 
 def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool = True, temperature: float = 1.0,
-                forced: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """fg-icdf-v1 draw per row; uniforms [n] or [n, k] (column 0 is used)."""
+                top_p: float = 1.0, forced: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """fg-icdf-v1 draw per row (fg-icdf-v1n when 0 < top_p < 1); uniforms
+    [n] or [n, k] (column 0 is used)."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     _need(uniforms, "uniforms", torch.float32, contiguous=False)
@@ -72,7 +74,7 @@ def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool
     if out is None:
         out = torch.empty(n, dtype=torch.int32, device=logits.device)
     N.call("fg_sample_rows", _ptr(logits), dtype_code(logits), stride, vocab, n, _ptr(uniforms), u_stride,
-           int(bool(do_sample)), float(temperature), _ptr(forced), _ptr(out), _stream(logits))
+           int(bool(do_sample)), float(temperature), float(top_p), _ptr(forced), _ptr(out), _stream(logits))
     return out
 
 
@@ -226,7 +228,8 @@ def layer_pointer_arrays(k_layers, v_layers):
 
 def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
                    row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
-                   tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0):
+                   tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0,
+                   top_p: float = 1.0):
     """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
     acc_len/correction/pending/last_node/finished [B]."""
     _need(logits, "logits", contiguous=False)
@@ -245,7 +248,7 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
     a.n_nodes_shared = int(n_nodes_shared)
     a.nmax = nmax
     a.uniforms, a.u_stride = uniforms.data_ptr(), uniforms.stride(0)
-    a.B, a.do_sample, a.temperature = B, int(bool(do_sample)), float(temperature)
+    a.B, a.do_sample, a.temperature, a.top_p = B, int(bool(do_sample)), float(temperature), float(top_p)
     a.eos_id, a.max_length = int(eos_id), int(max_length)
     a.row_len, a.update_len, a.active, a.dcap = row_len.data_ptr(), int(bool(update_len)), _ptr(active), int(dcap)
     for key in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):

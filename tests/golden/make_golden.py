@@ -316,12 +316,44 @@ def gen_generate():
     (HERE / "generate_cfg1.json").write_text(json.dumps(results))
 
 
+# ------------------------------------------------------------------ nucleus
+def gen_nucleus():
+    """Kept sets of the reference's nucleus rule (logits_to_probs,
+    acceptance.py:7-31: sort descending, keep through the first cumulative
+    probability above top_p) on seeded rows with distinct logits, plus each
+    row's distance between top_p and the reference's fp32 cumulative sums on
+    either side of the boundary (rows where that distance is at the level of
+    fp32 rounding may legitimately differ in the last kept entry)."""
+    g = torch.Generator().manual_seed(2024)
+    rows, temps, tops, kept, margin = [], [], [], [], []
+    for r in range(48):
+        V = [97, 512, 1000, 4096][r % 4]
+        scale = [0.5, 1.0, 3.0, 8.0][(r // 4) % 4]
+        logits = torch.randn(V, generator=g) * scale
+        T = [1.0, 0.7, 1.3][r % 3]
+        top_p = [0.5, 0.8, 0.9, 0.95, 0.99][r % 5]
+        probs = ref_acc.logits_to_probs(logits[None], temperature=T, top_p=top_p)[0]
+        sp = torch.softmax(logits.float() / T, dim=-1).sort(descending=True).values
+        cum = torch.cumsum(sp, dim=-1)
+        k = int((cum > top_p).nonzero()[0]) if bool((cum > top_p).any()) else V - 1
+        lo = float(cum[k - 1]) if k > 0 else 0.0
+        rows.append(np.pad(logits.numpy().astype(np.float32), (0, 4096 - V), constant_values=np.nan))
+        temps.append(T)
+        tops.append(top_p)
+        kept.append(np.pad((probs > 0).numpy(), (0, 4096 - V)))
+        margin.append(min(abs(float(cum[k]) - top_p), abs(lo - top_p)))
+    np.savez_compressed(HERE / "nucleus.npz", logits=np.stack(rows), vocab=np.array([[97, 512, 1000, 4096][r % 4]
+                        for r in range(48)], dtype=np.int32), temperature=np.array(temps, dtype=np.float32),
+                        top_p=np.array(tops, dtype=np.float32), kept=np.stack(kept), margin=np.array(margin))
+
+
+GENERATORS = {"planner": lambda: gen_planner(), "trees": lambda: gen_trees(), "accept": lambda: gen_accept(),
+              "extract": lambda: gen_extract(), "generate": lambda: gen_generate(), "nucleus": lambda: gen_nucleus()}
+
 if __name__ == "__main__":
+    # python tests/golden/make_golden.py [name ...]  (default: every fixture)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     native.build()
-    gen_planner()
-    gen_trees()
-    gen_accept()
-    gen_extract()
-    gen_generate()
+    for name in (sys.argv[1:] or list(GENERATORS)):
+        GENERATORS[name]()
     print("golden fixtures written to", HERE)

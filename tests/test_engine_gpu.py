@@ -36,6 +36,8 @@ def _heads_list(st, n):
     dict(tree_mode="concurrency_aware", cpeak=64, fixed=(4, 3, 2), mx=16, depth=4, repeats=2, max_new=16, seed=3),
     dict(tree_mode="concurrency_aware", cpeak=2048, fixed=(3, 2, 2), mx=32, depth=4, repeats=1, max_new=20, seed=9,
          greedy=True),
+    # nucleus sampling, the reference's default top_p
+    dict(tree_mode="fixed", fixed=(4, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=5, top_p=0.95),
 ])
 def test_generate_config1_matches_oracle(run):
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -50,12 +52,13 @@ def test_generate_config1_matches_oracle(run):
     greedy = run.get("greedy", False)
     ocfg = rp.OracleConfig(tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
-                           fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy)
+                           fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy,
+                           top_p=run.get("top_p", 1.0))
     ref = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(run["seed"]),
                       repeats=run["repeats"], max_length=128 + run["max_new"])
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                             max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
-                            fixed_tree_topk_by_depth=run["fixed"], top_p=1.0, do_sample=not greedy,
+                            fixed_tree_topk_by_depth=run["fixed"], top_p=run.get("top_p", 1.0), do_sample=not greedy,
                             sampling_seed=run["seed"])
     dec = FlashMedusaDecoder(gpu_model, {k: v.cuda() for k, v in st.items()}, _Tok(), cfg)
     res = dec.generate(ids, mask, repeated_generate_nums=run["repeats"], max_length=128 + run["max_new"])

@@ -58,6 +58,25 @@ def test_sample_rows_bit_exact(ops, dtype, V, temp, scale):
     assert np.array_equal(greedy, logits.float().argmax(-1).numpy())
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("V,temp,scale,top_p", [(4096, 1.0, 8.0, 0.9), (151936, 1.0, 2.0, 0.95), (97, 0.7, 3.0, 0.5),
+                                                (128256, 1.3, 1.0, 0.99), (1000, 1.0, 0.05, 0.8)])
+def test_sample_rows_nucleus_bit_exact(ops, dtype, V, temp, scale, top_p):
+    # fg-icdf-v1n: radix-select boundary on the GPU vs an explicit sort on the
+    # CPU; bf16 rows have many tied values, so boundaries cut tie groups
+    g = torch.Generator().manual_seed(V + int(temp * 10) + int(top_p * 100))
+    n = 16
+    logits = (torch.randn(n, V, generator=g) * scale).to(dtype)
+    logits[2] = logits[2].round()  # heavy ties
+    u = torch.rand(n, generator=g)
+    u[0], u[1] = 0.0, 1.0 - 2 ** -24
+    got = ops.sample_rows(logits.to(DEV), u.to(DEV), temperature=temp, top_p=top_p).cpu().numpy()
+    ref = orc.sample_rows(logits.float().numpy(), u.numpy(), temperature=temp, top_p=top_p)
+    assert np.array_equal(got, ref)
+    for r in range(4):  # every draw lies in the kept set
+        assert orc.nucleus_kept(logits[r].float().numpy(), temp, top_p)[got[r]]
+
+
 def test_sample_rows_forced_and_strided(ops):
     logits = torch.randn(6, 3, 512).to(DEV)
     view = logits[:, 1, :]  # row stride 1536
@@ -226,7 +245,8 @@ def test_build_tree_matches_oracle(ops, case):
 
 # ------------------------------------------------ acceptance + compaction
 def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sample, temperature, row_len,
-                max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None):
+                max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None,
+                top_p=1.0):
     B = tokens.shape[0]
     outs = {k: torch.full((B, dcap), -9, dtype=torch.int32, device=DEV) for k in ("acc_tokens", "acc_nodes")}
     for k in ("acc_len", "correction", "pending", "last_node", "finished"):
@@ -235,7 +255,8 @@ def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sa
     ops.accept_extract(logits=logits, slot=slots, tokens=tokens, parents=parents, n_nodes=n_nodes,
                        uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
                        max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=False,
-                       k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out)
+                       k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out,
+                       top_p=top_p)
     torch.cuda.synchronize()
     return outs, rl
 
@@ -255,9 +276,10 @@ def test_accept_matches_reference_fixture(ops, golden_dir):
         assert np.array_equal(outs["last_node"].cpu().numpy(), g[c + "_parent"]), c
 
 
-@pytest.mark.parametrize("dtype,V,B,peak", [(torch.bfloat16, 151936, 64, 6.0), (torch.float32, 4096, 12, 8.0),
-                                            (torch.float16, 1000, 33, 5.0)])
-def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak):
+@pytest.mark.parametrize("dtype,V,B,peak,top_p", [(torch.bfloat16, 151936, 64, 6.0, 1.0), (torch.float32, 4096, 12, 8.0, 1.0),
+                                                  (torch.float16, 1000, 33, 5.0, 1.0), (torch.bfloat16, 151936, 64, 6.0, 0.9),
+                                                  (torch.float32, 4096, 12, 2.0, 0.5)])
+def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p):
     g = torch.Generator().manual_seed(V + B)
     plan = rp.Plan(16, 3, [4, 2, 2], 0, "fixed")
     heads = [(torch.randn(B, V, generator=g) * peak).to(dtype).float() for _ in range(3)]
@@ -284,10 +306,10 @@ def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak):
     outs, rl = _run_accept(ops, packed.to(DEV), torch.tensor(slots, dtype=torch.int32).to(DEV), tok.to(DEV),
                            par.to(DEV), torch.full((B,), n, dtype=torch.int32, device=DEV), U.to(DEV),
                            do_sample=True, temperature=1.0, row_len=row_len.to(DEV), max_length=max_length, eos=eos,
-                           dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout)
+                           dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout, top_p=top_p)
     ref = orc.accept_walk(packed.float().numpy(), np.array(slots), tok.numpy(), par.numpy(), np.full(B, n), U.numpy(),
                           do_sample=True, temperature=1.0, eos_id=eos, max_length=max_length,
-                          row_len=row_len.numpy(), dcap=8)
+                          row_len=row_len.numpy(), dcap=8, top_p=top_p)
     for k in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):
         assert np.array_equal(outs[k].cpu().numpy(), ref[k]), k
     assert np.array_equal(rl.cpu().numpy(), row_len.numpy() + ref["acc_len"])

@@ -76,6 +76,62 @@ def test_sampler_never_picks_zero_probability_and_greedy_is_first_max():
     assert native.sample_rows(x, [1.0 - 2 ** -24])[0] in (399, 650)
 
 
+# ------------------------------------------------------- nucleus (top-p)
+def test_nucleus_kept_set_matches_reference(golden_dir):
+    # logits_to_probs (acceptance.py:7-31) on 48 seeded rows, 4 vocab sizes,
+    # 3 temperatures, top_p in {0.5, 0.8, 0.9, 0.95, 0.99}
+    d = np.load(golden_dir / "nucleus.npz")
+    compared = 0
+    for r in range(d["logits"].shape[0]):
+        V = int(d["vocab"][r])
+        if d["margin"][r] < 1e-5:  # boundary within fp32 rounding of the reference's cumsum
+            continue
+        mine = native.nucleus_kept(d["logits"][r, :V], float(d["temperature"][r]), float(d["top_p"][r]))
+        assert np.array_equal(mine, d["kept"][r, :V]), r
+        compared += 1
+    assert compared >= 40
+
+
+def test_nucleus_sampler_matches_renormalised_kept_distribution():
+    rng = np.random.default_rng(11)
+    logits = (rng.standard_normal(300) * 2).astype(np.float32)
+    for temp, top_p in ((1.0, 0.9), (0.7, 0.5)):
+        p = np.exp((logits.astype(np.float64) - logits.max()) / temp)
+        p /= p.sum()
+        keep = native.nucleus_kept(logits, temp, top_p)
+        # the reference rule: sorted prefix through the first cumulative > top_p
+        order = np.argsort(-logits, kind="stable")
+        k = int(np.argmax(np.cumsum(p[order]) > top_p))
+        want = np.zeros(300, dtype=bool)
+        want[order[: k + 1]] = True
+        assert np.array_equal(keep, want)
+        q = np.where(keep, p, 0.0)
+        q /= q.sum()
+        u = native.philox_uniforms(21, np.arange(60_000), 3, 1)[:, 0]
+        s = native.sample_rows(np.broadcast_to(logits, (60_000, 300)).copy(), u, temperature=temp, top_p=top_p)
+        assert keep[s].all()
+        freq = np.bincount(s, minlength=300) / s.size
+        assert np.max(np.abs(freq - q)) < 0.015
+
+
+def test_nucleus_edges_ties_and_tiny_top_p():
+    # bf16-like ties: equal values are ordered by index, the boundary can cut a tie group
+    x = np.array([1.0, 2.0, 2.0, 2.0, 0.0, 2.0], dtype=np.float32)
+    p = np.exp(x - 2.0) / np.exp(x - 2.0).sum()
+    keep = native.nucleus_kept(x, 1.0, 0.5)
+    k = int(np.argmax(np.cumsum(p[[1, 2, 3, 5, 0, 4]]) > 0.5))
+    assert keep.tolist() == [i in [1, 2, 3, 5, 0, 4][: k + 1] for i in range(6)]
+    # a tiny top_p keeps only the first maximum: the draw is the argmax for every u
+    u = np.linspace(0, 1 - 2 ** -24, 64, dtype=np.float32)
+    assert set(native.sample_rows(np.broadcast_to(x, (64, 6)).copy(), u, top_p=1e-6).tolist()) == {1}
+    # top_p outside (0, 1) is fg-icdf-v1; greedy ignores top_p
+    y = (np.random.default_rng(2).standard_normal(500)).astype(np.float32)
+    uu = native.philox_uniforms(5, np.arange(50), 0, 1)[:, 0]
+    rows = np.broadcast_to(y, (50, 500)).copy()
+    assert np.array_equal(native.sample_rows(rows, uu, top_p=1.0), native.sample_rows(rows, uu))
+    assert native.sample_rows(y, [0.3], do_sample=False, top_p=0.5)[0] == int(np.argmax(y))
+
+
 # ------------------------------------------------------------ acceptance
 def _walk(tokens, parents, logits, slots=None, do_sample=False, u=None, dcap=6, row_len=None, max_length=1 << 30,
           eos=-7):
