@@ -18,6 +18,7 @@ from __future__ import annotations
 import math
 import time
 import warnings
+import dataclasses
 from dataclasses import dataclass
 
 import torch
@@ -109,7 +110,8 @@ class FlashMedusaDecoder:
                          min_tree_nodes_per_seq=cfg.min_tree_nodes_per_seq,
                          max_tree_nodes_per_seq=cfg.max_tree_nodes_per_seq, max_tree_depth=cfg.max_tree_depth,
                          fixed_tree_topk_by_depth=list(cfg.fixed_tree_topk_by_depth),
-                         adaptive_tree_enabled=False)
+                         adaptive_tree_enabled=bool(cfg.adaptive_tree_enabled),
+                         adaptive_min_topk_by_depth=list(cfg.adaptive_min_topk_by_depth))
 
     def _params(self, active: int):
         cfg = self.config
@@ -118,7 +120,12 @@ class FlashMedusaDecoder:
             num_medusa_heads=min(cfg.num_medusa_heads, len(self.engine.heads)), cpeak_nodes=cfg.cpeak_nodes,
             min_tree_nodes_per_seq=cfg.min_tree_nodes_per_seq, max_tree_nodes_per_seq=cfg.max_tree_nodes_per_seq,
             max_tree_depth=cfg.max_tree_depth, fixed_tree_topk_by_depth=cfg.fixed_tree_topk_by_depth,
-            adaptive_tree_enabled=False)
+            adaptive_tree_enabled=bool(cfg.adaptive_tree_enabled),
+            adaptive_min_topk_by_depth=tuple(cfg.adaptive_min_topk_by_depth),
+            adaptive_confidence_metric=cfg.adaptive_confidence_metric,
+            adaptive_confidence_quantile=cfg.adaptive_confidence_quantile,
+            adaptive_confidence_low=cfg.adaptive_confidence_low, adaptive_confidence_high=cfg.adaptive_confidence_high,
+            adaptive_depth_weight_decay=cfg.adaptive_depth_weight_decay)
 
     def round_config(self, max_length: int) -> RoundConfig:
         cfg = self.config
@@ -141,8 +148,6 @@ class FlashMedusaDecoder:
                  max_length: int = 2048, statistical_time: bool = False, generation_step: int = 0,
                  collect_reflex_aux_cache=None, persistent_reflex_memory=None) -> dict:
         cfg = self.config
-        if cfg.adaptive_tree_enabled:
-            raise NotImplementedError("adaptive_tree_enabled needs the two-phase round (planned); use it off")
         eng = self.engine
         repeats = max(1, int(repeated_generate_nums or 1))
         dev = eng.device
@@ -180,12 +185,13 @@ class FlashMedusaDecoder:
             plan.topk_by_depth = plan.topk_by_depth[:nh]
             plan.active_heads = nh
             dcap = nh + 2
-            rb = eng.buffers(B, plan, nh, dcap)
+            adaptive = bool(cfg.adaptive_tree_enabled) and nh > 0
+            rb = eng.buffers(B, plan, nh, dcap, adaptive=adaptive)
             params = self._params(n_active) if nh > 0 else ops.plan_params(
                 tree_mode="explicit", active_batch_size=n_active, num_medusa_heads=0, cpeak_nodes=0,
                 min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=1, fixed_tree_topk_by_depth=())
-            key = (id(st), B, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, n_active,
-                   rcfg.do_sample, rcfg.temperature, rcfg.eos_id, rcfg.max_length, rcfg.seed, rcfg.attn_splits)
+            key = (id(st), B, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, n_active, adaptive,
+                   dataclasses.astuple(rcfg))
             tv = time.time()
             if cfg.use_cuda_graphs and key in seen:
                 if key not in graphs:
@@ -195,7 +201,7 @@ class FlashMedusaDecoder:
                 eng.run_round(st, rb, params, rcfg)
                 seen.add(key)
             out = rb.out
-            flat = torch.cat([out["acc_len"], out["finished"], st.pending, out["acc_tokens"].view(-1)])
+            flat = torch.cat([out["acc_len"], out["finished"], st.pending, rb.tree["plan"], out["acc_tokens"].view(-1)])
             if pinned is None or pinned.numel() < flat.numel():
                 pinned = torch.empty(flat.numel(), dtype=torch.int32, pin_memory=True)
             host = pinned[: flat.numel()]
@@ -206,13 +212,17 @@ class FlashMedusaDecoder:
             acc_len = vals[:B]
             fin = vals[B:2 * B]
             pend = vals[2 * B:3 * B]
-            toks = vals[3 * B:]
+            plan_dev = vals[3 * B:3 * B + 16]
+            toks = vals[3 * B + 16:]
+            # the round's tree as built on the device (adaptive rounds may be smaller)
+            n_tree = plan_dev[10] if nh > 0 else 1
+            topk_round = plan_dev[2:2 + plan_dev[1]] if nh > 0 else []
             stats["total_verify_rounds"] += 1
             active_batch_sum += n_active
-            tree_node_sum += rb.N
+            tree_node_sum += n_tree
             tree_plan_last = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
-                              "active_heads": plan.active_heads, "topk_by_depth": list(plan.topk_by_depth),
-                              "actual_nodes": rb.N, "proposal_mode": "medusa"}
+                              "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
+                              "actual_nodes": n_tree, "proposal_mode": "medusa"}
             for r in range(B):
                 if not active_host[r]:
                     continue
@@ -223,7 +233,7 @@ class FlashMedusaDecoder:
                 stats["total_acc_length"] += a
                 stats["total_decoded_token_num"] += 1
                 stats["total_accepted_medusa_tokens"] += max(a - 1, 0)
-                stats["total_proposed_medusa_tokens"] += max(rb.N - 1, 0)
+                stats["total_proposed_medusa_tokens"] += max(n_tree - 1, 0)
                 accept_hist[a] = accept_hist.get(a, 0) + 1
                 for d in range(2, a + 1):
                     accept_by_depth[d] = accept_by_depth.get(d, 0) + 1

@@ -206,6 +206,12 @@ class RoundBuffers:
         self.tree_hidden = torch.empty((B, N_, H), dtype=spec.dtype, **f)
         idx = [b * N_ + i for b in range(B) for i in self.internal]
         self.int_idx = torch.tensor(idx if idx else [0], dtype=torch.int32, **f)
+        # Adaptive rounds keep this (base plan) shape: the tree that K2 builds
+        # is never larger, its unused nodes are inert (parent -2, no slot),
+        # and the internal-row gather is rebuilt on the device from K2's
+        # internal list each round.
+        self.adaptive = adaptive
+        self.j_int = torch.arange(max(len(idx), 1), dtype=torch.int32, **f)
         self.hid_int = torch.empty((max(len(idx), 1), H), dtype=spec.dtype, **f)
         self.tree_logits = torch.empty((max(len(idx), 1), V), dtype=spec.dtype, **f)
         self.dcap = dcap
@@ -383,6 +389,13 @@ class VerifyEngine:
     def accept(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
         B = st.B
         if rb.n_int > 0:
+            if rb.adaptive:
+                # row b * ni + rank -> tree_hidden[b, internal[rank]] (ni = this round's internal count)
+                ni = rb.tree["plan"][11:12].clamp_min(1)
+                b = torch.div(rb.j_int, ni, rounding_mode="floor")
+                r = rb.j_int - b * ni
+                idx = b * rb.N + rb.tree["internal"][r.long()]
+                torch.where(rb.j_int < B * ni, idx, torch.zeros_like(idx), out=rb.int_idx)
             ops.gather_rows(rb.tree_hidden.view(B * rb.N, -1), rb.int_idx, out=rb.hid_int)
             torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
         rb.corr_used += (st.pending >= 0).sum()

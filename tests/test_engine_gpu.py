@@ -38,6 +38,9 @@ def _heads_list(st, n):
          greedy=True),
     # nucleus sampling, the reference's default top_p
     dict(tree_mode="fixed", fixed=(4, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=5, top_p=0.95),
+    # adaptive top-k from head confidences (two thresholds, quantile over the rows)
+    dict(tree_mode="concurrency_aware", cpeak=128, fixed=(4, 3, 2), mx=32, depth=4, repeats=2, max_new=20, seed=7,
+         adaptive=True),
 ])
 def test_generate_config1_matches_oracle(run):
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -53,12 +56,15 @@ def test_generate_config1_matches_oracle(run):
     ocfg = rp.OracleConfig(tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
                            fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy,
-                           top_p=run.get("top_p", 1.0))
+                           top_p=run.get("top_p", 1.0), adaptive_tree_enabled=run.get("adaptive", False),
+                           adaptive_confidence_low=0.3, adaptive_confidence_high=0.9)
     ref = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(run["seed"]),
                       repeats=run["repeats"], max_length=128 + run["max_new"])
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                             max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
                             fixed_tree_topk_by_depth=run["fixed"], top_p=run.get("top_p", 1.0), do_sample=not greedy,
+                            adaptive_tree_enabled=run.get("adaptive", False), adaptive_confidence_low=0.3,
+                            adaptive_confidence_high=0.9,
                             sampling_seed=run["seed"])
     dec = FlashMedusaDecoder(gpu_model, {k: v.cuda() for k, v in st.items()}, _Tok(), cfg)
     res = dec.generate(ids, mask, repeated_generate_nums=run["repeats"], max_length=128 + run["max_new"])
@@ -66,6 +72,14 @@ def test_generate_config1_matches_oracle(run):
     for k in ("total_acc_length", "total_decoded_token_num", "total_verify_rounds", "total_correction_tokens",
               "total_accepted_medusa_tokens", "total_proposed_medusa_tokens"):
         assert res[k] == ref[k], k
+    if run.get("adaptive"):
+        # the confidences did shrink some trees below the base plan
+        base = rp.plan_tree(active_batch_size=ids.shape[0] * run["repeats"], num_medusa_heads=3,
+                            tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512), min_tree_nodes_per_seq=1,
+                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
+                            fixed_tree_topk_by_depth=list(run["fixed"]), adaptive_tree_enabled=True,
+                            adaptive_min_topk_by_depth=[1, 1, 1])
+        assert res["total_proposed_medusa_tokens"] < res["total_decoded_token_num"] * (base.actual_nodes - 1)
     from flashgrpo_b200 import _native
 
     assert _native.read_device_error(clear=True) == 0
