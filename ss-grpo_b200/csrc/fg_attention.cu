@@ -216,7 +216,23 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
         }
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    dim3 grid(p.splits, n_kv_heads * p.groups, B);
-    tc::attn_tc_kernel<<<grid, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, p);
+    // Programmatic launch: the CTAs may start (TMEM, barriers, prefix tile
+    // loads) while the preceding kernel of the stream finishes; the kernel
+    // waits for it (griddepcontrol.wait) before reading Q or tree slots.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.splits, n_kv_heads * p.groups, B);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mk, mv, p);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return FG_ECUDA;
+    }
     return launch_status();
 }

@@ -350,9 +350,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         bars->abort_flag = 0;
         bars->last_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        // the first tiles of the ring load while Q is staged and TMEM allocated
-        for (int i = 0; i < min(kStages, nmine); ++i) load_k(i);
-        for (int i = 0; i < min(kStages, nmine); ++i) load_v(i);
+        // The first tiles of the ring load while Q is staged and TMEM
+        // allocated.  Tiles wholly inside the prefix (written by earlier
+        // rounds) may load before the preceding kernel -- the RoPE/KV write
+        // of this layer, launched as our programmatic predecessor -- has
+        // finished; the others wait for it below.
+        for (int i = 0; i < min(kStages, nmine); ++i)
+            if ((c0 + i + 1) * kBlk <= kv_len) {
+                load_k(i);
+                load_v(i);
+            }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&bars->tmem_base)),
@@ -360,6 +367,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    // Q and this round's tree K/V slots are written by the preceding kernel:
+    // every thread waits for it (a no-op without programmatic launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x == 0)
+        for (int i = 0; i < min(kStages, nmine); ++i)
+            if ((c0 + i + 1) * kBlk > kv_len) {
+                load_k(i);
+                load_v(i);
+            }
     const int wg = warp >= 4 ? (warp - 4) >> 2 : -1;  // softmax warpgroup
     const int r = (warp & 3) * 32 + lane;              // query row = TMEM lane
     // Q tile (rows beyond R zero) -> swizzled smem; warpgroup w loads dims [64w, 64w + 64)

@@ -41,6 +41,9 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
                                T* __restrict__ vc, int64_t sb, int64_t sh, int64_t ss, int32_t cap,
                                T* __restrict__ q_out) {
     __shared__ float cs[2][128];  // cos / sin per frequency, once per token
+    // the tree attention that follows may start its prefix loads now; it
+    // waits for this grid to finish before reading Q or the tree K/V
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int32_t tokn = blockIdx.x;  // b * n_nodes + node
     const int32_t b = tokn / n_nodes, node = tokn % n_nodes;
     const float pos = (float)positions[tokn];

@@ -356,7 +356,9 @@ class VerifyEngine:
 
     def verify_forward(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig, attn_events=None):
         """attn_events (optional): per-layer (start, end) CUDA events recorded
-        around the tree-attention launch, for live per-launch timing."""
+        around the tree-attention launch, for live per-launch timing (None
+        entries skip a layer; an event between the RoPE/KV write and the
+        attention keeps that layer's attention from starting early)."""
         sp, w = self.spec, self.w
         B, N_ = st.B, rb.N
         ops.gather_rows(w.embed, rb.tree["tokens"].view(-1), out=rb.h)
@@ -371,11 +373,11 @@ class VerifyEngine:
             ops.rope_kv_write(rb.qkv, rb.tree["positions"], w.inv_freq, w.attention_scaling, B=B, n_nodes=N_,
                               n_q_heads=sp.n_q_heads, n_kv_heads=sp.n_kv_heads, head_dim=sp.head_dim,
                               kv_len=st.row_len, k_cache=None, v_cache=None, q_out=rb.q, kv=kv)
-            if attn_events is not None:
+            if attn_events is not None and attn_events[l] is not None:
                 attn_events[l][0].record()
             ops.tree_attention(rb.q, st.k[l], st.v[l], st.row_len, rb.tree["anc"], scale=self.scale, out=rb.attn,
                                workspace=ws, num_splits=cfg.attn_splits, max_kv_len=st.capacity, kv=kv)
-            if attn_events is not None:
+            if attn_events is not None and attn_events[l] is not None:
                 attn_events[l][1].record()
             torch.addmm(rb.h, rb.attn.view(B * N_, -1), lw["w_o"].t(), out=rb.h)
             if lw["b_o"] is not None:
