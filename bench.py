@@ -272,11 +272,13 @@ def run_ours(args, rank, world, local_rank):
             if world > 1:
                 dist.barrier()
             t0 = time.perf_counter()
-            tok, rounds_total = 0, 0
+            tok, rounds_total, pre_s, ver_s = 0, 0, 0.0, 0.0
             for _ in range(args.e2e_calls):
                 res = dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + args.e2e_new)
                 tok += res["total_acc_length"]
                 rounds_total += res["total_verify_rounds"]
+                pre_s += res["prefill_time_cost"]
+                ver_s += res["tree_verify_time_cost"]
             torch.cuda.synchronize()
             e_s = shard.reduce_scalar(time.perf_counter() - t0, "max", device)
             tok = int(shard.reduce_scalar(tok, "sum", device))
@@ -286,7 +288,8 @@ def run_ours(args, rank, world, local_rank):
                    "d2h_bytes_per_step": int(rounds_total / args.e2e_calls * rows * (3 + dcap) * 4),
                    "step": f"one generate() call: {prompts} prompts x {args.prefix} tokens prefilled, x8 samples, "
                            f"{args.e2e_new} new tokens per row",
-                   "calls": args.e2e_calls}
+                   "calls": args.e2e_calls, "prefill_s_per_call": pre_s / args.e2e_calls,
+                   "verify_rounds_s_per_call": ver_s / args.e2e_calls, "rounds_per_call": rounds_total / args.e2e_calls}
     result = {
         "metric": METRIC, "value": accepted_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,

@@ -273,22 +273,22 @@ class VerifyEngine:
         n_valid = mask.sum(-1)
         P, S = ids.shape
         B = P * repeats
-        if int(n_valid.max()) + 1 > capacity:
+        if int(n_valid.max()) + 1 > capacity:  # the one host sync of the prefill
             raise ValueError("KV capacity smaller than the prompt")
         st = self.state(B, capacity, n_heads)
-        layers = [(l.keys, l.values) for l in out.past_key_values.layers]
-        for p in range(P):
-            nv = int(n_valid[p])
-            rows = slice(p * repeats, (p + 1) * repeats)
-            # valid tokens are the mask==1 positions (left padding): positions 0..nv-1
-            sel = mask[p].nonzero().squeeze(-1)
-            for l, (k, v) in enumerate(layers):
-                st.k[l, rows, :, :nv] = k[p][:, sel].unsqueeze(0)
-                st.v[l, rows, :, :nv] = v[p][:, sel].unsqueeze(0)
-            last = int(sel[-1]) if nv > 0 else S - 1
-            st.X[rows] = hid[p, last].unsqueeze(0)
-            st.row_len[rows] = nv
-        del out, layers
+        # valid (mask == 1) positions first, in order: slot j of a row holds its
+        # j-th valid token; slots past the row's length hold finite padding K/V
+        order = torch.argsort((mask == 0).to(torch.int8), dim=-1, stable=True)
+        W = min(S, capacity)
+        for l, layer in enumerate(out.past_key_values.layers):
+            for src, dst in ((layer.keys, st.k), (layer.values, st.v)):
+                idx = order[:, None, :W, None].expand(-1, src.shape[1], -1, src.shape[3])
+                dst[l, :, :, :W] = torch.gather(src, 2, idx).repeat_interleave(repeats, 0)
+        last = (mask * torch.arange(S, device=mask.device)).argmax(-1)  # last valid position
+        last = torch.where(n_valid > 0, last, torch.full_like(last, S - 1))
+        st.X[:B] = hid[torch.arange(P, device=hid.device), last].repeat_interleave(repeats, 0)
+        st.row_len[:B] = n_valid.to(torch.int32).repeat_interleave(repeats)
+        del out
         return st
 
     # ---------------------------------------------------------------- round
