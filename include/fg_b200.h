@@ -304,10 +304,18 @@ fg_status fg_extract_path(int32_t n_layers, const uint64_t *k_layers, const uint
  * the verify forward (transformers Qwen2/Llama attention, called from
  * qwen_flashgrpo_wrapper.py:150-186).  dtype bf16/f16 rounds like the
  * reference's half-precision arithmetic; f32 stays in f32. */
+/* cos_sin (nullable): the table fg_rope_table made for these positions; the
+ * kernel then reads it instead of evaluating cos/sin (same values). */
 fg_status fg_rope_kv_write(const void *qkv, int32_t dtype, const int32_t *positions, const float *inv_freq,
                            float attention_scaling, int32_t B, int32_t n_nodes, int32_t n_q_heads,
                            int32_t n_kv_heads, int32_t head_dim, const int32_t *kv_len, const fg_kv_layer *kv,
-                           void *q_out, void *stream);
+                           void *q_out, const void *cos_sin, void *stream);
+/* cos(pos * inv_freq) * attention_scaling and the sine, rounded to `dtype`
+ * like the reference's rotary embedding, for every (token, frequency):
+ * cos_sin [2][n_tokens][half] (cosines, then sines).  Positions do not change
+ * between the layers of a round, so one table serves them all. */
+fg_status fg_rope_table(const int32_t *positions, int32_t n_tokens, const float *inv_freq, int32_t half,
+                        float attention_scaling, int32_t dtype, void *cos_sin, void *stream);
 /* y = weight * (x * rsqrt(mean(x^2) + eps)) per row (Qwen2RMSNorm / LlamaRMSNorm). */
 fg_status fg_rmsnorm(const void *x, const void *weight, int32_t dtype, int32_t n_rows, int32_t dim, float eps,
                      void *y, void *stream);

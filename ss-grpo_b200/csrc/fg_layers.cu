@@ -31,6 +31,15 @@ template <typename T>
 __device__ __forceinline__ float rnd(float v) { return tf<T>(from_f<T>(v)); }
 
 // --------------------------------------------------------------- RoPE + KV
+// One rotation pair as the reference evaluates q*cos + rotate_half(q)*sin:
+// each product and the sum rounded separately (no fused multiply-add), then
+// rounded to the activation dtype.
+template <typename T>
+__device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& o1, float& o2) {
+    o1 = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(a, c)), rnd<T>(__fmul_rn(-b, s))));
+    o2 = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(b, c)), rnd<T>(__fmul_rn(a, s))));
+}
+
 // One CTA per (row, node); threads over (head, pair).  HF computes
 // cos/sin(pos * inv_freq) in fp32, casts them to the activation dtype and
 // evaluates q*cos + rotate_half(q)*sin in that dtype.
@@ -68,8 +77,8 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
         const T* x = src + (int64_t)h * D;
         const float x1 = tf<T>(x[i]), x2 = tf<T>(x[i + half]);
         // out[i] = x1*c - x2*s ; out[i+half] = x2*c + x1*s  (each product rounded)
-        const float o1 = rnd<T>(rnd<T>(x1 * c) + rnd<T>(-x2 * s));
-        const float o2 = rnd<T>(rnd<T>(x2 * c) + rnd<T>(x1 * s));
+        float o1, o2;
+        rope_pair<T>(x1, x2, c, s, o1, o2);
         if (h < Hq) {
             T* qo = q_out + ((int64_t)tokn * Hq + h) * D;
             qo[i] = from_f<T>(o1);
@@ -85,6 +94,79 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
         for (int32_t e = threadIdx.x; e < Hkv * D; e += blockDim.x) {
             const int32_t kh = e / D, d = e % D;
             vc[(int64_t)b * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d] = src[(int64_t)(Hq + Hkv + kh) * D + d];
+        }
+}
+
+// cos/sin(pos * inv_freq) * scaling rounded to the activation dtype, once per
+// round: [2][n_tokens][half] (cos rows, then sin rows).  Positions are the
+// same for every layer of a round, so the layers share one table.
+template <typename T>
+__global__ void rope_table_kernel(const int32_t* __restrict__ positions, int32_t n_tokens,
+                                  const float* __restrict__ inv_freq, int32_t half, float attn_scaling,
+                                  T* __restrict__ cs) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= (int64_t)n_tokens * half) return;
+    const int32_t t = (int32_t)(e / half), i = (int32_t)(e % half);
+    const float f = __fmul_rn((float)positions[t], inv_freq[i]);
+    float c = cosf(f), s = sinf(f);
+    if (attn_scaling != 1.0f) {
+        c = c * attn_scaling;
+        s = s * attn_scaling;
+    }
+    cs[e] = from_f<T>(c);
+    cs[(int64_t)n_tokens * half + e] = from_f<T>(s);
+}
+
+// RoPE + tree K/V write from a cos/sin table: one CTA per (row, node), one
+// thread per 8 consecutive rotation pairs of a head (16-byte vectors), the
+// same roundings as rope_kv_kernel.
+template <typename T>
+__global__ void __launch_bounds__(128) rope_kv_table_kernel(
+    const T* __restrict__ qkv, const T* __restrict__ cs, int32_t n_tokens, int32_t n_nodes, int32_t Hq, int32_t Hkv,
+    int32_t D, const int32_t* __restrict__ kv_len, T* __restrict__ kc, T* __restrict__ vc, int64_t sb, int64_t sh,
+    int64_t ss, int32_t cap, T* __restrict__ q_out) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    constexpr int NV = 16 / sizeof(T);
+    const int32_t tokn = blockIdx.x;
+    const int32_t b = tokn / n_nodes, node = tokn % n_nodes;
+    const int32_t half = D / 2, vph = half / NV;  // vectors per half-head
+    const T* src = qkv + (int64_t)tokn * (Hq + 2 * Hkv) * D;
+    const int32_t slotpos = kv_len[b] + node;
+    const bool in_cap = slotpos < cap;
+    const T* cr = cs + (int64_t)tokn * half;
+    const T* sr = cs + ((int64_t)n_tokens + tokn) * half;
+    for (int32_t e = threadIdx.x; e < (Hq + Hkv) * vph; e += blockDim.x) {
+        const int32_t h = e / vph, i = (e % vph) * NV;
+        const T* x = src + (int64_t)h * D;
+        const uint4 u1 = *reinterpret_cast<const uint4*>(x + i), u2 = *reinterpret_cast<const uint4*>(x + i + half);
+        const uint4 uc = *reinterpret_cast<const uint4*>(cr + i), us = *reinterpret_cast<const uint4*>(sr + i);
+        const T *x1 = reinterpret_cast<const T*>(&u1), *x2 = reinterpret_cast<const T*>(&u2);
+        const T *cc = reinterpret_cast<const T*>(&uc), *sv = reinterpret_cast<const T*>(&us);
+        uint4 r1, r2;
+        T *o1 = reinterpret_cast<T*>(&r1), *o2 = reinterpret_cast<T*>(&r2);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            float v1, v2;
+            rope_pair<T>(tf<T>(x1[k]), tf<T>(x2[k]), tf<T>(cc[k]), tf<T>(sv[k]), v1, v2);
+            o1[k] = from_f<T>(v1);
+            o2[k] = from_f<T>(v2);
+        }
+        T* dst = nullptr;
+        if (h < Hq) {
+            dst = q_out + ((int64_t)tokn * Hq + h) * D;
+        } else if (in_cap) {
+            dst = kc + (int64_t)b * sb + (int64_t)(h - Hq) * sh + (int64_t)slotpos * ss;
+        }
+        if (dst) {
+            *reinterpret_cast<uint4*>(dst + i) = r1;
+            *reinterpret_cast<uint4*>(dst + i + half) = r2;
+        }
+    }
+    if (in_cap)
+        for (int32_t e = threadIdx.x; e < Hkv * (D / NV); e += blockDim.x) {
+            const int32_t kh = e / (D / NV), d = (e % (D / NV)) * NV;
+            *reinterpret_cast<uint4*>(vc + (int64_t)b * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d) =
+                *reinterpret_cast<const uint4*>(src + (int64_t)(Hq + Hkv + kh) * D + d);
         }
 }
 
@@ -142,6 +224,50 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const T* __restrict__ 
     }
 }
 
+// Warp-per-row RMSNorm (4 rows per 128-thread CTA): the sum of squares is a
+// warp reduction, no block barrier.  Rows of up to 32 * 8 vectors.
+template <typename T>
+__global__ void __launch_bounds__(128) rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                           int32_t n_rows, int32_t dim, float eps,
+                                                           T* __restrict__ y) {
+    constexpr int NV = 16 / sizeof(T);
+    const int32_t row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= n_rows) return;
+    const int32_t nvec = dim / NV;
+    const T* xr = x + (int64_t)row * dim;
+    uint4 u[8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int32_t vi = lane + k * 32;
+        u[k] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * NV) : make_uint4(0, 0, 0, 0);
+        const T* e = reinterpret_cast<const T*>(&u[k]);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const float v = tf<T>(e[j]);
+            ss += v * v;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss / (float)dim + eps);
+    T* yr = y + (int64_t)row * dim;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int32_t vi = lane + k * 32;
+        if (vi >= nvec) break;
+        const uint4 uw = *reinterpret_cast<const uint4*>(w + vi * NV);
+        const T* e = reinterpret_cast<const T*>(&u[k]);
+        const T* we = reinterpret_cast<const T*>(&uw);
+        uint4 res;
+        T* o = reinterpret_cast<T*>(&res);
+#pragma unroll
+        for (int j = 0; j < NV; ++j) o[j] = from_f<T>(tf<T>(we[j]) * rnd<T>(tf<T>(e[j]) * r));
+        *reinterpret_cast<uint4*>(yr + vi * NV) = res;
+    }
+}
+
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int32_t dim, float eps,
                                T* __restrict__ y) {
@@ -179,7 +305,11 @@ __global__ void layernorm_kernel(const T* __restrict__ x, const T* __restrict__ 
 }
 
 // ---------------------------------------------------------- activations
-__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+// v * sigmoid(v) in fp32 with the fast exponential and division intrinsics;
+// the result is rounded to the activation dtype like the reference's, so the
+// few-ulp fp32 difference rarely reaches the rounded value.  Large negative v:
+// exp overflows to inf and the quotient is -0.
+__device__ __forceinline__ float silu(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gu, int32_t inter, int64_t total, T* __restrict__ out) {
@@ -242,14 +372,37 @@ using namespace fg;
         default: return FG_EINVAL;                            \
     }
 
+extern "C" fg_status fg_rope_table(const int32_t* positions, int32_t n_tokens, const float* inv_freq, int32_t half,
+                                   float attention_scaling, int32_t dtype, void* cos_sin, void* stream) {
+    if (n_tokens == 0) return FG_OK;
+    if (!positions || !inv_freq || !cos_sin || n_tokens < 0 || half <= 0) return FG_EINVAL;
+    const int64_t n = (int64_t)n_tokens * half;
+    cudaStream_t st = (cudaStream_t)stream;
+    FG_DISPATCH(dtype, (rope_table_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+                            positions, n_tokens, inv_freq, half, attention_scaling, (T*)cos_sin)));
+    return launch_status();
+}
+
 extern "C" fg_status fg_rope_kv_write(const void* qkv, int32_t dtype, const int32_t* positions, const float* inv_freq,
                                       float attention_scaling, int32_t B, int32_t n_nodes, int32_t n_q_heads,
                                       int32_t n_kv_heads, int32_t head_dim, const int32_t* kv_len,
-                                      const fg_kv_layer* kv, void* q_out, void* stream) {
+                                      const fg_kv_layer* kv, void* q_out, const void* cos_sin, void* stream) {
     if (B * n_nodes == 0) return FG_OK;
     if (!qkv || !positions || !inv_freq || !kv_len || !kv || !kv->k || !kv->v || !q_out || head_dim % 2) return FG_EINVAL;
     if (head_dim > 256) return FG_ECAPACITY;
     cudaStream_t st = (cudaStream_t)stream;
+    const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
+    const bool vec = cos_sin != nullptr && ((head_dim / 2) * esz) % 16 == 0 && ((uintptr_t)qkv % 16) == 0 &&
+                     ((uintptr_t)q_out % 16) == 0 && ((uintptr_t)cos_sin % 16) == 0 && ((uintptr_t)kv->k % 16) == 0 &&
+                     ((uintptr_t)kv->v % 16) == 0 && (kv->stride_s * esz) % 16 == 0 && (kv->stride_h * esz) % 16 == 0 &&
+                     (kv->stride_b * esz) % 16 == 0;
+    if (vec) {
+        FG_DISPATCH(dtype, (rope_kv_table_kernel<T><<<B * n_nodes, 128, 0, st>>>(
+                                (const T*)qkv, (const T*)cos_sin, B * n_nodes, n_nodes, n_q_heads, n_kv_heads,
+                                head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b, kv->stride_h, kv->stride_s,
+                                kv->capacity, (T*)q_out)));
+        return launch_status();
+    }
     FG_DISPATCH(dtype, (rope_kv_kernel<T><<<B * n_nodes, 128, 0, st>>>(
                             (const T*)qkv, positions, inv_freq, attention_scaling, n_nodes, n_q_heads, n_kv_heads,
                             head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b, kv->stride_h, kv->stride_s,
@@ -265,7 +418,10 @@ extern "C" fg_status fg_rmsnorm(const void* x, const void* weight, int32_t dtype
     const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
     const bool vec = (dim * esz) % 16 == 0 && dim * esz <= 128 * 4 * 16 && ((uintptr_t)x % 16) == 0 &&
                      ((uintptr_t)y % 16) == 0 && ((uintptr_t)weight % 16) == 0;
-    if (vec) {
+    if (vec && dim * esz <= 32 * 8 * 16) {
+        FG_DISPATCH(dtype, (rmsnorm_warp_kernel<T><<<(n_rows + 3) / 4, 128, 0, st>>>(
+                                (const T*)x, (const T*)weight, n_rows, dim, eps, (T*)y)));
+    } else if (vec) {
         FG_DISPATCH(dtype, (rmsnorm_vec_kernel<T><<<n_rows, 128, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
                                                                          (T*)y)));
     } else {

@@ -81,7 +81,8 @@ SIGNATURES = {
     "fg_extract_path": (c_i32, [c_i32, ctypes.POINTER(c_u64), ctypes.POINTER(c_u64), c_i32, c_i32, c_i32, c_i32,
                                 c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_i32, c_vp]),
     "fg_rope_kv_write": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_f32, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp,
-                                 ctypes.POINTER(KvLayer), c_vp, c_vp]),
+                                 ctypes.POINTER(KvLayer), c_vp, c_vp, c_vp]),
+    "fg_rope_table": (c_i32, [c_vp, c_i32, c_vp, c_i32, c_f32, c_i32, c_vp, c_vp]),
     "fg_rmsnorm": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_f32, c_vp, c_vp]),
     "fg_layernorm": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_f32, c_vp, c_vp]),
     "fg_silu_mul": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_vp]),
@@ -120,7 +121,7 @@ def load():
 
 # Entry points that enqueue exactly one kernel; `launches` counts them so a
 # caller can report how many of this library's kernels a step runs.
-LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree",
+LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree", "fg_rope_table",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
              "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows"}
 launches = 0

@@ -204,6 +204,7 @@ class RoundBuffers:
         self.gu = torch.empty((T, 2 * spec.inter), dtype=spec.dtype, **f)
         self.act = torch.empty((T, spec.inter), dtype=spec.dtype, **f)
         self.tree_hidden = torch.empty((B, N_, H), dtype=spec.dtype, **f)
+        self.rope_cs = torch.empty((2, B * N_, spec.head_dim // 2), dtype=spec.dtype, **f)
         idx = [b * N_ + i for b in range(B) for i in self.internal]
         self.int_idx = torch.tensor(idx if idx else [0], dtype=torch.int32, **f)
         # Adaptive rounds keep this (base plan) shape: the tree that K2 builds
@@ -362,6 +363,8 @@ class VerifyEngine:
         sp, w = self.spec, self.w
         B, N_ = st.B, rb.N
         ops.gather_rows(w.embed, rb.tree["tokens"].view(-1), out=rb.h)
+        # the tree positions are fixed for the round: one cos/sin table for all layers
+        ops.rope_table(rb.tree["positions"], w.inv_freq, w.attention_scaling, sp.dtype, out=rb.rope_cs)
         ws = self._attn_workspace(rb, st, cfg.attn_splits)
         for l, lw in enumerate(w.layers):
             ops.rmsnorm(rb.h, lw["in_norm"], sp.eps, out=rb.xn)
@@ -372,7 +375,7 @@ class VerifyEngine:
             kv = st.kv_layers[l]
             ops.rope_kv_write(rb.qkv, rb.tree["positions"], w.inv_freq, w.attention_scaling, B=B, n_nodes=N_,
                               n_q_heads=sp.n_q_heads, n_kv_heads=sp.n_kv_heads, head_dim=sp.head_dim,
-                              kv_len=st.row_len, k_cache=None, v_cache=None, q_out=rb.q, kv=kv)
+                              kv_len=st.row_len, k_cache=None, v_cache=None, q_out=rb.q, kv=kv, cos_sin=rb.rope_cs)
             if attn_events is not None and attn_events[l] is not None:
                 attn_events[l][0].record()
             ops.tree_attention(rb.q, st.k[l], st.v[l], st.row_len, rb.tree["anc"], scale=self.scale, out=rb.attn,

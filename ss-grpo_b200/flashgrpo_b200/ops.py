@@ -278,12 +278,24 @@ def extract_path(k_layers, v_layers, row_len, acc_nodes, acc_len) -> None:
 
 
 # ------------------------------------------------------------- layer pieces
+def rope_table(positions, inv_freq, attention_scaling, dtype, out=None):
+    """[2, n_tokens, head_dim / 2] cos/sin in `dtype` for fg_rope_kv_write."""
+    _need(positions, "positions", torch.int32)
+    n, half = positions.numel(), inv_freq.numel()
+    if out is None:
+        out = torch.empty((2, n, half), dtype=dtype, device=positions.device)
+    N.call("fg_rope_table", _ptr(positions), n, _ptr(inv_freq), half, float(attention_scaling),
+           _DTYPES[dtype], _ptr(out), _stream(positions))
+    return out
+
+
 def rope_kv_write(qkv, positions, inv_freq, attention_scaling, *, B, n_nodes, n_q_heads, n_kv_heads, head_dim,
-                  kv_len, k_cache, v_cache, q_out, kv: N.KvLayer | None = None):
+                  kv_len, k_cache, v_cache, q_out, kv: N.KvLayer | None = None, cos_sin=None):
     if kv is None:
         kv = kv_layer(k_cache, v_cache)
     N.call("fg_rope_kv_write", _ptr(qkv), dtype_code(qkv), _ptr(positions), _ptr(inv_freq), float(attention_scaling),
-           B, n_nodes, n_q_heads, n_kv_heads, head_dim, _ptr(kv_len), ctypes.byref(kv), _ptr(q_out), _stream(qkv))
+           B, n_nodes, n_q_heads, n_kv_heads, head_dim, _ptr(kv_len), ctypes.byref(kv), _ptr(q_out), _ptr(cos_sin),
+           _stream(qkv))
     return q_out
 
 

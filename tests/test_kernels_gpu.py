@@ -441,6 +441,12 @@ def test_rope_kv_write_matches_hf(ops, dtype):
     q_out = torch.empty(B, n, hq, D, dtype=dtype, device=DEV)
     ops.rope_kv_write(qkv, positions, inv_freq.to(DEV), 1.0, B=B, n_nodes=n, n_q_heads=hq, n_kv_heads=hkv,
                       head_dim=D, kv_len=kv_len, k_cache=kc, v_cache=vc, q_out=q_out)
+    # the per-round cos/sin table path (vectorized kernel) gives the same bits
+    table = ops.rope_table(positions, inv_freq.to(DEV), 1.0, dtype)
+    kc2, vc2, q2 = torch.zeros_like(kc), torch.zeros_like(vc), torch.empty_like(q_out)
+    ops.rope_kv_write(qkv, positions, inv_freq.to(DEV), 1.0, B=B, n_nodes=n, n_q_heads=hq, n_kv_heads=hkv,
+                      head_dim=D, kv_len=kv_len, k_cache=kc2, v_cache=vc2, q_out=q2, cos_sin=table)
+    assert torch.equal(q2, q_out) and torch.equal(kc2, kc) and torch.equal(vc2, vc)
     # HF reference: cos/sin in fp32 -> activation dtype, rotate in that dtype
     freqs = positions.float()[..., None] * inv_freq.to(DEV)
     emb = torch.cat([freqs, freqs], -1)
