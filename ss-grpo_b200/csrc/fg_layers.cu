@@ -224,50 +224,6 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const T* __restrict__ 
     }
 }
 
-// Warp-per-row RMSNorm (4 rows per 128-thread CTA): the sum of squares is a
-// warp reduction, no block barrier.  Rows of up to 32 * 8 vectors.
-template <typename T>
-__global__ void __launch_bounds__(128) rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w,
-                                                           int32_t n_rows, int32_t dim, float eps,
-                                                           T* __restrict__ y) {
-    constexpr int NV = 16 / sizeof(T);
-    const int32_t row = blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= n_rows) return;
-    const int32_t nvec = dim / NV;
-    const T* xr = x + (int64_t)row * dim;
-    uint4 u[8];
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int32_t vi = lane + k * 32;
-        u[k] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * NV) : make_uint4(0, 0, 0, 0);
-        const T* e = reinterpret_cast<const T*>(&u[k]);
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-            const float v = tf<T>(e[j]);
-            ss += v * v;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float r = rsqrtf(ss / (float)dim + eps);
-    T* yr = y + (int64_t)row * dim;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int32_t vi = lane + k * 32;
-        if (vi >= nvec) break;
-        const uint4 uw = *reinterpret_cast<const uint4*>(w + vi * NV);
-        const T* e = reinterpret_cast<const T*>(&u[k]);
-        const T* we = reinterpret_cast<const T*>(&uw);
-        uint4 res;
-        T* o = reinterpret_cast<T*>(&res);
-#pragma unroll
-        for (int j = 0; j < NV; ++j) o[j] = from_f<T>(tf<T>(we[j]) * rnd<T>(tf<T>(e[j]) * r));
-        *reinterpret_cast<uint4*>(yr + vi * NV) = res;
-    }
-}
-
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int32_t dim, float eps,
                                T* __restrict__ y) {
@@ -311,27 +267,30 @@ __global__ void layernorm_kernel(const T* __restrict__ x, const T* __restrict__ 
 // exp overflows to inf and the quotient is -0.
 __device__ __forceinline__ float silu(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
+// One CTA per row (no index division), 16-byte vectors of gate and up.
+template <typename T>
+__global__ void __launch_bounds__(256) silu_mul_rows_kernel(const T* __restrict__ gu, int32_t inter,
+                                                            T* __restrict__ out) {
+    constexpr int NV = 16 / sizeof(T);
+    const int64_t r = blockIdx.x;
+    const T* g_row = gu + r * 2 * inter;
+    const T* u_row = g_row + inter;
+    T* o_row = out + r * inter;
+    for (int32_t i = threadIdx.x * NV; i < inter; i += blockDim.x * NV) {
+        const uint4 ug = *reinterpret_cast<const uint4*>(g_row + i);
+        const uint4 uu = *reinterpret_cast<const uint4*>(u_row + i);
+        const T* g = reinterpret_cast<const T*>(&ug);
+        const T* u = reinterpret_cast<const T*>(&uu);
+        uint4 res;
+        T* o = reinterpret_cast<T*>(&res);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) o[k] = from_f<T>(rnd<T>(silu(tf<T>(g[k]))) * tf<T>(u[k]));
+        *reinterpret_cast<uint4*>(o_row + i) = res;
+    }
+}
+
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gu, int32_t inter, int64_t total, T* __restrict__ out) {
-    constexpr int NV = 16 / sizeof(T);
-    if (inter % NV == 0 && (reinterpret_cast<uintptr_t>(gu) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
-        const int64_t nvec = total / NV;
-        const int32_t vrow = inter / NV;
-        for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nvec;
-             e += (int64_t)gridDim.x * blockDim.x) {
-            const int64_t r = e / vrow, i = (e % vrow) * NV;
-            const uint4 ug = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + i);
-            const uint4 uu = *reinterpret_cast<const uint4*>(gu + r * 2 * inter + inter + i);
-            const T* g = reinterpret_cast<const T*>(&ug);
-            const T* u = reinterpret_cast<const T*>(&uu);
-            uint4 res;
-            T* o = reinterpret_cast<T*>(&res);
-#pragma unroll
-            for (int k = 0; k < NV; ++k) o[k] = from_f<T>(rnd<T>(silu(tf<T>(g[k]))) * tf<T>(u[k]));
-            *reinterpret_cast<uint4*>(out + e * NV) = res;
-        }
-        return;
-    }
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = e / inter, i = e % inter;
         const float g = tf<T>(gu[r * 2 * inter + i]), u = tf<T>(gu[r * 2 * inter + inter + i]);
@@ -418,10 +377,7 @@ extern "C" fg_status fg_rmsnorm(const void* x, const void* weight, int32_t dtype
     const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
     const bool vec = (dim * esz) % 16 == 0 && dim * esz <= 128 * 4 * 16 && ((uintptr_t)x % 16) == 0 &&
                      ((uintptr_t)y % 16) == 0 && ((uintptr_t)weight % 16) == 0;
-    if (vec && dim * esz <= 32 * 8 * 16) {
-        FG_DISPATCH(dtype, (rmsnorm_warp_kernel<T><<<(n_rows + 3) / 4, 128, 0, st>>>(
-                                (const T*)x, (const T*)weight, n_rows, dim, eps, (T*)y)));
-    } else if (vec) {
+    if (vec) {
         FG_DISPATCH(dtype, (rmsnorm_vec_kernel<T><<<n_rows, 128, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
                                                                          (T*)y)));
     } else {
@@ -446,7 +402,12 @@ extern "C" fg_status fg_silu_mul(const void* gu, int32_t dtype, int32_t n_rows, 
     if (total == 0) return FG_OK;
     if (!gu || !out) return FG_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
-    FG_DISPATCH(dtype, (silu_mul_kernel<T><<<grid_for(total), 256, 0, st>>>((const T*)gu, inter, total, (T*)out)));
+    const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
+    if ((inter * esz) % 16 == 0 && ((uintptr_t)gu % 16) == 0 && ((uintptr_t)out % 16) == 0) {
+        FG_DISPATCH(dtype, (silu_mul_rows_kernel<T><<<n_rows, 256, 0, st>>>((const T*)gu, inter, (T*)out)));
+    } else {
+        FG_DISPATCH(dtype, (silu_mul_kernel<T><<<grid_for(total), 256, 0, st>>>((const T*)gu, inter, total, (T*)out)));
+    }
     return launch_status();
 }
 
