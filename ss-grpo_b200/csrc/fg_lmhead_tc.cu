@@ -89,18 +89,32 @@ struct Bars {
     int abort_flag;
 };
 
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* b) {
+// L2 eviction policies: X (small, re-read for every tile) is kept, the W
+// stream (read once) goes first.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* b,
+                                       uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(sa(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(sa(b))
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3}], [%4], %5;" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(sa(b)), "l"(policy)
         : "memory");
 }
 
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1, uint64_t policy) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1)
+                 "r"(c0), "r"(c1), "l"(policy)
                  : "memory");
 }
 
@@ -157,15 +171,16 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
         // ------------------------------------------------------------ TMA
         if (lane == 0) {
             // W chunk `c` (tile c / nk, k chunk c % nk) into L2 ahead of its TMA load
+            const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
             auto prefetch_w = [&](int c) {
                 const int t2 = c / p.nk, kc2 = c % p.nk;
                 if (t2 >= n_tiles) return;
                 const int v2 = v_begin + t2 * kN;
                 const int w2 = min(kN, u1 * kUnit - v2);
                 if (w2 == kN) {
-                    tma_prefetch_2d(&tmW256, kc2 * kKc, v2);
+                    tma_prefetch_2d(&tmW256, kc2 * kKc, v2, pol_w);
                 } else {
-                    for (int j = 0; j < w2 / kUnit; ++j) tma_prefetch_2d(&tmW16, kc2 * kKc, v2 + j * kUnit);
+                    for (int j = 0; j < w2 / kUnit; ++j) tma_prefetch_2d(&tmW16, kc2 * kKc, v2 + j * kUnit, pol_w);
                 }
             };
             int it = 0, issued = 0;
@@ -183,12 +198,12 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                     bar_expect(&bars->full[s], bytes);
                     uint8_t* sw = st + p.x_area;
                     if (w == kN) {
-                        tma_2d(sw, &tmW256, kc * kKc, v0, &bars->full[s]);
+                        tma_2d(sw, &tmW256, kc * kKc, v0, &bars->full[s], pol_w);
                     } else {
                         for (int j = 0; j < w / kUnit; ++j)
-                            tma_2d(sw + j * kUnit * 128, &tmW16, kc * kKc, v0 + j * kUnit, &bars->full[s]);
+                            tma_2d(sw + j * kUnit * 128, &tmW16, kc * kKc, v0 + j * kUnit, &bars->full[s], pol_w);
                     }
-                    tma_2d(st, &tmX, kc * kKc, 0, &bars->full[s]);
+                    tma_2d(st, &tmX, kc * kKc, 0, &bars->full[s], pol_x);
                     issued = it + 1;
                 }
             }
