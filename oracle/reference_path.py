@@ -194,6 +194,67 @@ def build_dense_trees(root_tokens, head_logits, plan: Plan) -> list[Tree]:
     return trees
 
 
+def chain_cell_forward(cell, state, token_embedding):
+    """ChainDraftCell.forward (medusa_heads.py:154-160):
+    state + sigmoid(gate) * out_proj(SiLU(state_proj(LN(state)) + token_proj(LN(embedding))))."""
+    F = torch.nn.functional
+    dt = cell["state_norm.weight"].dtype
+    s = state.to(dt)
+    t = token_embedding.to(dt)
+    H = s.shape[-1]
+    mixed = (F.linear(F.layer_norm(s, (H,), cell["state_norm.weight"], cell["state_norm.bias"], 1e-5),
+                      cell["state_proj.weight"])
+             + F.linear(F.layer_norm(t, (H,), cell["token_norm.weight"], cell["token_norm.bias"], 1e-5),
+                        cell["token_proj.weight"]))
+    delta = F.linear(F.silu(mixed), cell["out_proj.weight"], cell["out_proj.bias"])
+    return s + torch.sigmoid(cell["gate"]) * delta
+
+
+def build_chain_trees(root_tokens, cur_hidden, plan: Plan, heads, cell, lm_w, embed_w, *,
+                      bootstrap_from_medusa=True) -> list[Tree]:
+    """_build_chain_batch_trees (flash_medusa_decoder.py:1141-1261) with Reflex
+    off and fixed widths: per depth, the lm_head of every parent state, its
+    top-k (stable ties), children in parent then rank order under the node
+    budget, and the next states from the chain cell on the chosen tokens."""
+    B = len(root_tokens)
+    tokens = [[int(t)] for t in root_tokens]
+    parents = [[-1] for _ in range(B)]
+    depths = [[1] for _ in range(B)]
+    root = torch.as_tensor([int(t) for t in root_tokens], dtype=torch.long)
+    if bootstrap_from_medusa and heads:
+        states = project_heads(heads, cur_hidden, 1)[0]
+    else:
+        states = chain_cell_forward(cell, cur_hidden, embed_w[root])
+    parent_rows = list(range(B))
+    parent_nodes = [0] * B
+    budget = plan.node_budget_per_seq
+    for d, k in enumerate(plan.topk_by_depth):
+        if states.shape[0] == 0:
+            break
+        logits = torch.nan_to_num(torch.nn.functional.linear(states.to(lm_w.dtype), lm_w).float(), nan=-1.0e9,
+                                  posinf=1.0e9, neginf=-1.0e9)
+        idx = stable_topk(logits, min(int(k), logits.shape[-1]))[1].tolist()
+        nxt_state, nxt_tok, nxt_rows, nxt_nodes = [], [], [], []
+        for ps, row in enumerate(parent_rows):
+            if len(tokens[row]) >= budget:
+                continue
+            for tok in idx[ps]:
+                if len(tokens[row]) >= budget:
+                    break
+                tokens[row].append(int(tok))
+                parents[row].append(parent_nodes[ps])
+                depths[row].append(d + 2)
+                nxt_state.append(ps)
+                nxt_tok.append(int(tok))
+                nxt_rows.append(row)
+                nxt_nodes.append(len(tokens[row]) - 1)
+        if not nxt_tok:
+            break
+        states = chain_cell_forward(cell, states[torch.as_tensor(nxt_state)], embed_w[torch.as_tensor(nxt_tok)])
+        parent_rows, parent_nodes = nxt_rows, nxt_nodes
+    return [Tree(tokens[b], parents[b], depths[b]) for b in range(B)]
+
+
 def tree_attention_inputs(trees, full_attention_mask, logical_lengths, *, pad_token_id, dtype):
     """Dense ancestor-only mask, positions logical_len + depth - 1, padding."""
     B = len(trees)
@@ -404,6 +465,9 @@ class OracleConfig:
     adaptive_min_topk_by_depth: tuple = (1, 1, 1)
     adaptive_depth_weight_decay: float = 0.5
     project_internal_tree_logits_only: bool = True
+    proposal_mode: str = "medusa"          # "chain": ChainDraftCell proposals
+    chain_bootstrap_from_medusa: bool = True
+    chain_cell: dict | None = None         # chain_cell.* tensors keyed without the prefix
 
 
 @dataclass
@@ -497,7 +561,8 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
                          adaptive_tree_enabled=cfg.adaptive_tree_enabled,
                          adaptive_min_topk_by_depth=list(cfg.adaptive_min_topk_by_depth))
         n_heads = min(plan.active_heads, len(heads))
-        projected = project_heads(heads, cur_hidden, n_heads)
+        chain = cfg.proposal_mode == "chain"
+        projected = project_heads(heads, cur_hidden, n_heads) if not chain else []
         head_logits = (list(torch.nn.functional.linear(torch.cat(projected, 0), lm_w).split(B, 0))
                        if projected else [])
         if cfg.adaptive_tree_enabled and head_logits and plan.topk_by_depth:
@@ -510,7 +575,12 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
                                          min_topk_by_depth=list(cfg.adaptive_min_topk_by_depth)[: len(adapted)],
                                          depth_weight_decay=cfg.adaptive_depth_weight_decay)
             plan = Plan(plan.node_budget_per_seq, len(adapted), adapted, dense_node_count(adapted), plan.mode)
-        trees = build_dense_trees(root, head_logits, plan)
+        if chain and plan.topk_by_depth:
+            trees = build_chain_trees(root, cur_hidden, plan, heads, cfg.chain_cell, lm_w,
+                                      model.get_input_embeddings().weight,
+                                      bootstrap_from_medusa=cfg.chain_bootstrap_from_medusa)
+        else:
+            trees = build_dense_trees(root, head_logits, plan)
         for t in trees:
             stats["total_proposed_medusa_tokens"] += t.node_count - 1
         tree_logits = slots = tree_hidden = None

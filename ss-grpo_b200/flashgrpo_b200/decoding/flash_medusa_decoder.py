@@ -47,6 +47,8 @@ class FlashMedusaConfig:
     top_k: int | None = None
     clone_tree_cache: bool = True
     proposal_mode: str = "medusa"
+    chain_enable_after: int = 0
+    chain_bootstrap_from_medusa: bool = True
     enable_medusa_spec_after: int = 0
     adaptive_tree_enabled: bool = False
     adaptive_confidence_metric: str = "top1_prob"
@@ -79,8 +81,8 @@ class FlashMedusaDecoder:
             raise ValueError(f"Unsupported cache_update_mode={config.cache_update_mode}")
         if config.proposal_mode not in {"medusa", "chain"}:
             raise ValueError(f"Unsupported proposal_mode={config.proposal_mode}")
-        if config.proposal_mode == "chain":
-            raise NotImplementedError("chain proposals are not on the B200 path yet (proposal_mode='medusa')")
+        if config.proposal_mode == "chain" and config.adaptive_tree_enabled:
+            raise NotImplementedError("adaptive widths for chain proposals are not on the B200 path")
         if config.tree_layout != "dense":
             raise NotImplementedError("sparse tree layouts belong to the Reflex/HRDCR subsystem (tree_layout='dense')")
         if config.reflex_enabled:
@@ -127,8 +129,11 @@ class FlashMedusaDecoder:
             adaptive_confidence_low=cfg.adaptive_confidence_low, adaptive_confidence_high=cfg.adaptive_confidence_high,
             adaptive_depth_weight_decay=cfg.adaptive_depth_weight_decay)
 
-    def round_config(self, max_length: int) -> RoundConfig:
+    def round_config(self, max_length: int, generation_step: int = 0) -> RoundConfig:
         cfg = self.config
+        chain = cfg.proposal_mode == "chain" and int(generation_step) >= int(cfg.chain_enable_after)
+        if chain and self.engine.heads.chain is None:
+            raise ValueError("proposal_mode='chain' needs a ChainDraftCell (chain_cell.*) in the MEDUSA heads")
         eos = getattr(self.tokenizer, "eos_token_id", None)
         pad = getattr(self.tokenizer, "pad_token_id", None)
         eos = eos if eos is not None else (pad if pad is not None else 0)
@@ -136,7 +141,8 @@ class FlashMedusaDecoder:
         return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), top_p=top_p,
                            eos_id=int(eos),
                            max_length=int(max_length), seed=int(cfg.sampling_seed),
-                           attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel))
+                           attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel), chain=chain,
+                           chain_bootstrap=bool(cfg.chain_bootstrap_from_medusa))
 
     def max_heads(self) -> int:
         cfg = self.config
@@ -159,7 +165,7 @@ class FlashMedusaDecoder:
         st = eng.prefill(input_ids, attention_mask, repeats=repeats, capacity=capacity, n_heads=n_heads)
         torch.cuda.synchronize(dev)
         prefill_time = time.time() - t0
-        rcfg = self.round_config(max_length)
+        rcfg = self.round_config(max_length, generation_step)
         B = st.B
         generated = [[] for _ in range(B)]
         active_host = [True] * B
@@ -222,7 +228,7 @@ class FlashMedusaDecoder:
             tree_node_sum += n_tree
             tree_plan_last = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
                               "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
-                              "actual_nodes": n_tree, "proposal_mode": "medusa"}
+                              "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa"}
             for r in range(B):
                 if not active_host[r]:
                     continue

@@ -119,6 +119,10 @@ class HeadWeights:
             self.heads.append({"norm_w": g("norm.weight"), "norm_b": g("norm.bias"), "fc_w": g("fc.weight"),
                                "fc_b": g("fc.bias")})
             i += 1
+        # ChainDraftCell (chain_cell.*), present when the checkpoint has one
+        cell = {k[len("chain_cell."):]: v.detach().to(device=device, dtype=dtype) for k, v in state.items()
+                if k.startswith("chain_cell.")}
+        self.chain = cell if "state_proj.weight" in cell else None
         if any(k.startswith("heads.") and k.endswith("output.weight") for k in state):
             raise NotImplementedError("untied MEDUSA output heads are not on the B200 path (tie_lm_head=True)")
 
@@ -136,6 +140,9 @@ class RoundConfig:
     max_length: int = 1 << 30
     seed: int = 0
     attn_splits: int = 0
+    # chain proposals (ChainDraftCell): per-parent top-k instead of per-head
+    chain: bool = False
+    chain_bootstrap: bool = True
     # proposal lm_head: "fused" = tcgen05 GEMM with the top-k in its epilogue
     # (bf16, hidden a multiple of 64, <= 256 rows), "separate" = cuBLAS GEMM
     # then fg_row_topk
@@ -172,6 +179,14 @@ class RoundBuffers:
         H, V = spec.hidden, spec.vocab
         self.n_heads = n_heads
         parents, depths = dense_topology(plan, n_heads)
+        # BFS levels of the shared topology: level d = nodes at depth d + 1
+        self.widths = [int(k) for k in plan.topk_by_depth[:n_heads]]
+        self.level_off, self.level_count = [], []
+        for d in range(1, max(depths, default=1) + 1):
+            ids = [i for i, dd in enumerate(depths) if dd == d]
+            self.level_off.append(ids[0] if ids else len(depths))
+            self.level_count.append(len(ids))
+        self.chain_tokens = []
         self.N = len(parents)
         self.internal = internal_nodes(parents)
         self.n_int = len(self.internal)
@@ -342,6 +357,75 @@ class VerifyEngine:
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
                         top_p=cfg.top_p, forced=st.pending, out=rb.root)
 
+    # ------------------------------------------------------ chain proposals
+    def _chain_cell(self, state: torch.Tensor, emb: torch.Tensor) -> torch.Tensor:
+        """ChainDraftCell.forward (medusa_heads.py:154-160) in the cell's dtype."""
+        F = torch.nn.functional
+        c = self.heads.chain
+        H = state.shape[-1]
+        mixed = (F.linear(F.layer_norm(state, (H,), c["state_norm.weight"], c["state_norm.bias"], 1e-5),
+                          c["state_proj.weight"])
+                 + F.linear(F.layer_norm(emb, (H,), c["token_norm.weight"], c["token_norm.bias"], 1e-5),
+                            c["token_proj.weight"]))
+        delta = F.linear(F.silu(mixed), c["out_proj.weight"], c["out_proj.bias"])
+        return state + torch.sigmoid(c["gate"]) * delta
+
+    def _rows_topk(self, x: torch.Tensor, k: int, cfg: RoundConfig) -> torch.Tensor:
+        """Stable top-k indices [M, k] of the lm_head logits of the rows of x."""
+        M, V = x.shape[0], self.spec.vocab
+        idx = torch.empty((M, k), dtype=torch.int32, device=self.device)
+        val = torch.empty((M, k), dtype=torch.float32, device=self.device)
+        mx = torch.empty(M, dtype=torch.float32, device=self.device)
+        if self._fused_lm_head(cfg, min(M, 256)):
+            for r0 in range(0, M, 256):
+                r1 = min(M, r0 + 256)
+                ws = self._lm_head_ws(r1 - r0, 0, k)
+                ops.lm_head_topk(x[r0:r1], self.w.lm_head, n_logit_rows=0, logits=None, topk_row0=0, k=k,
+                                 topk_out=(idx[r0:r1], val[r0:r1], mx[r0:r1], None), workspace=ws)
+        else:
+            logits = torch.mm(x, self.w.lm_head.t())
+            ops.row_topk(logits, k, out=(idx, val, mx, None))
+        return idx
+
+    def propose_chain(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
+        """_build_chain_batch_trees (flash_medusa_decoder.py:1141-1261), Reflex
+        off, fixed widths: the root token as in propose(), then per depth the
+        lm_head top-k of every parent state and the chain cell on the chosen
+        tokens.  The dense topology is the one K2 builds; the tokens of each
+        level are written over K2's after build_tree."""
+        B = st.B
+        h = st.hidden
+        if self._fused_lm_head(cfg, B):
+            ops.lm_head_topk(st.X[:B], self.w.lm_head, n_logit_rows=B, logits=rb.logits, topk_row0=B, k=1,
+                             topk_out=None, workspace=self._lm_head_ws(B, B, 1))
+        else:
+            torch.mm(st.X[:B], self.w.lm_head.t(), out=rb.logits[:B])
+        ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
+        ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
+                        top_p=cfg.top_p, forced=st.pending, out=rb.root)
+        if cfg.chain_bootstrap and len(self.heads) > 0:
+            hw = self.heads.heads[0]
+            ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
+            torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
+            state = ops.silu_residual(h, rb.fc)
+        else:
+            state = self._chain_cell(h, self.w.embed[rb.root.long()])
+        H = state.shape[-1]
+        states, n_par = state.view(B, 1, H), 1
+        rb.chain_tokens = []
+        for d, k in enumerate(rb.widths):
+            n_ch = rb.level_count[d + 1] if d + 1 < len(rb.level_count) else 0
+            if n_ch == 0:
+                break
+            idx = self._rows_topk(states.reshape(B * n_par, H), k, cfg)
+            tok = idx.view(B, n_par * k)[:, :n_ch]
+            rb.chain_tokens.append((rb.level_off[d + 1], n_ch, tok))
+            if d + 2 < len(rb.level_count) and rb.level_count[d + 2] > 0:
+                par = torch.arange(n_ch, device=self.device) // k
+                emb = self.w.embed[tok.reshape(-1).long()]
+                states = self._chain_cell(states[:, par].reshape(-1, H), emb).view(B, n_ch, H)
+                n_par = n_ch
+
     def build_tree(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams):
         nh = rb.n_heads
         B = st.B
@@ -419,8 +503,14 @@ class VerifyEngine:
     def run_round(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig,
                   attn_events=None):
         """All device work of one round, enqueued on the current stream."""
-        self.propose(st, rb, cfg)
-        self.build_tree(st, rb, params)
+        if cfg.chain:
+            self.propose_chain(st, rb, cfg)
+            self.build_tree(st, rb, params)
+            for off, n, tok in rb.chain_tokens:
+                rb.tree["tokens"][:, off:off + n] = tok
+        else:
+            self.propose(st, rb, cfg)
+            self.build_tree(st, rb, params)
         self.verify_forward(st, rb, cfg, attn_events)
         self.accept(st, rb, cfg)
 

@@ -75,12 +75,16 @@ def build_model(cfg_id: int, *, device="cpu", seed: int = 0, attn_implementation
     return model
 
 
-def medusa_head_tensors(cfg_id: int, *, device="cpu", seed: int = 1, dtype=None, **overrides):
+def medusa_head_tensors(cfg_id: int, *, device="cpu", seed: int = 1, dtype=None, chain: bool = False,
+                        **overrides):
     """Parameters of the MEDUSA heads as plain tensors, keyed like the
     ``heads.{i}.norm`` / ``heads.{i}.fc`` entries of ``medusa_heads.pt``.
 
     fc weights are N(0, 0.02) (not the zero init of a fresh head) so the heads
-    differ from the identity; LayerNorm weight 1 and bias 0.
+    differ from the identity; LayerNorm weight 1 and bias 0.  chain=True adds
+    the ``chain_cell.*`` entries of a ChainDraftCell (bottleneck max(64, H/8))
+    with N(0, 0.02) projections, a non-zero out_proj and gate 0, so the cell
+    changes the state.
     """
     spec = dict(CONFIGS[cfg_id])
     spec.update(overrides)
@@ -93,6 +97,18 @@ def medusa_head_tensors(cfg_id: int, *, device="cpu", seed: int = 1, dtype=None,
         state[f"heads.{i}.fc.bias"] = torch.zeros(H, device=device, dtype=dtype)
         state[f"heads.{i}.norm.weight"] = torch.ones(H, device=device, dtype=dtype)
         state[f"heads.{i}.norm.bias"] = torch.zeros(H, device=device, dtype=dtype)
+    if chain:
+        bn = max(64, H // 8)
+        r = lambda *shape: (torch.randn(*shape, generator=g) * 0.02).to(device=device, dtype=dtype)
+        state["chain_cell.state_norm.weight"] = torch.ones(H, device=device, dtype=dtype)
+        state["chain_cell.state_norm.bias"] = torch.zeros(H, device=device, dtype=dtype)
+        state["chain_cell.token_norm.weight"] = torch.ones(H, device=device, dtype=dtype)
+        state["chain_cell.token_norm.bias"] = torch.zeros(H, device=device, dtype=dtype)
+        state["chain_cell.state_proj.weight"] = r(bn, H)
+        state["chain_cell.token_proj.weight"] = r(bn, H)
+        state["chain_cell.out_proj.weight"] = r(H, bn) * 10
+        state["chain_cell.out_proj.bias"] = torch.zeros(H, device=device, dtype=dtype)
+        state["chain_cell.gate"] = torch.zeros((), device=device, dtype=dtype)
     return state
 
 

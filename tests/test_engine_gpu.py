@@ -41,6 +41,10 @@ def _heads_list(st, n):
     # adaptive top-k from head confidences (two thresholds, quantile over the rows)
     dict(tree_mode="concurrency_aware", cpeak=128, fixed=(4, 3, 2), mx=32, depth=4, repeats=2, max_new=20, seed=7,
          adaptive=True),
+    # chain proposals: per-parent top-k from the ChainDraftCell state, bootstrapped from head 1
+    dict(tree_mode="fixed", fixed=(3, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=13, chain=True),
+    dict(tree_mode="fixed", fixed=(2, 2), mx=7, depth=3, repeats=2, max_new=16, seed=17, chain=True,
+         bootstrap=False),
 ])
 def test_generate_config1_matches_oracle(run):
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -48,7 +52,9 @@ def test_generate_config1_matches_oracle(run):
 
     cpu_model = synthetic.build_model(1)
     gpu_model = synthetic.build_model(1).cuda()
-    st = synthetic.medusa_head_tensors(1)
+    chain = run.get("chain", False)
+    st = synthetic.medusa_head_tensors(1, chain=chain)
+    cell = {k[len("chain_cell."):]: v for k, v in st.items() if k.startswith("chain_cell.")} if chain else None
     ids, mask = synthetic.random_prompts(4, 128, 4096, seed=0)
     if run["repeats"] > 1:
         ids, mask = ids[:2], mask[:2]
@@ -57,14 +63,17 @@ def test_generate_config1_matches_oracle(run):
                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
                            fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy,
                            top_p=run.get("top_p", 1.0), adaptive_tree_enabled=run.get("adaptive", False),
-                           adaptive_confidence_low=0.3, adaptive_confidence_high=0.9)
+                           adaptive_confidence_low=0.3, adaptive_confidence_high=0.9,
+                           proposal_mode="chain" if chain else "medusa", chain_cell=cell,
+                           chain_bootstrap_from_medusa=run.get("bootstrap", True))
     ref = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(run["seed"]),
                       repeats=run["repeats"], max_length=128 + run["max_new"])
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                             max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
                             fixed_tree_topk_by_depth=run["fixed"], top_p=run.get("top_p", 1.0), do_sample=not greedy,
                             adaptive_tree_enabled=run.get("adaptive", False), adaptive_confidence_low=0.3,
-                            adaptive_confidence_high=0.9,
+                            adaptive_confidence_high=0.9, proposal_mode="chain" if chain else "medusa",
+                            chain_bootstrap_from_medusa=run.get("bootstrap", True),
                             sampling_seed=run["seed"])
     dec = FlashMedusaDecoder(gpu_model, {k: v.cuda() for k, v in st.items()}, _Tok(), cfg)
     res = dec.generate(ids, mask, repeated_generate_nums=run["repeats"], max_length=128 + run["max_new"])
