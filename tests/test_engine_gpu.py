@@ -179,3 +179,62 @@ def test_verify_round_bf16_against_hf_eager():
             assert torch.equal(state.v[:, b, :, L + j], v_tree[:, b, :, src])
         assert torch.equal(state.hidden[b], tree_hidden[b, int(walk["last_node"][b])])
     assert not torch.equal(state.hidden, hidden0)
+
+
+def test_extracted_cache_matches_recompute():
+    # scripts/test_kv_extraction.py:29-85: after a verify round, the cache the
+    # extract_path compaction leaves behind must be the cache a plain forward
+    # over prompt + accepted tokens builds, and the next-round hidden state
+    # must be that forward's last hidden state.
+    from flashgrpo_b200 import ops
+    from flashgrpo_b200.decoding.medusa_tree import plan_tree
+    from flashgrpo_b200.engine.verify import RoundConfig, VerifyEngine
+    from flashgrpo_b200.utils import synthetic
+
+    torch.manual_seed(0)
+    model = synthetic.build_model(1).cuda()
+    heads = {k: v.cuda() for k, v in synthetic.medusa_head_tensors(1).items()}
+    ids, mask = synthetic.random_prompts(4, 40, 4096, seed=21)
+    eng = VerifyEngine(model, heads)
+    plan = plan_tree(active_batch_size=4, num_medusa_heads=3, tree_mode="fixed", cpeak_nodes=512,
+                     min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16, max_tree_depth=4,
+                     fixed_tree_topk_by_depth=[4, 2, 2])
+    params = ops.plan_params(tree_mode="fixed", active_batch_size=4, num_medusa_heads=3, cpeak_nodes=512,
+                             min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16, max_tree_depth=4,
+                             fixed_tree_topk_by_depth=(4, 2, 2))
+    st = eng.prefill(ids, mask, repeats=1, capacity=80, n_heads=plan.active_heads)
+    rb = eng.buffers(4, plan, plan.active_heads, plan.active_heads + 2)
+    cfg = RoundConfig(do_sample=False, seed=3)  # greedy: long accepted paths on the peaked heads
+    with torch.inference_mode():
+        old_len = st.row_len.clone()
+        eng.run_round(st, rb, params, cfg)
+        eng.run_round(st, rb, params, cfg)  # a second round extracts on top of the first
+    torch.cuda.synchronize()
+    n_new = (st.row_len - old_len).tolist()
+    assert max(n_new) >= 3
+    model.config._attn_implementation = "eager"
+    # the same two rounds on a fresh state, recording each round's accepted tokens
+    st2 = eng.prefill(ids, mask, repeats=1, capacity=80, n_heads=plan.active_heads)
+    with torch.inference_mode():
+        rounds = []
+        for _ in range(2):
+            eng.run_round(st2, rb, params, cfg)
+            a = rb.out["acc_len"].tolist()
+            t = rb.out["acc_tokens"].tolist()
+            rounds.append([t[b][: a[b]] for b in range(4)])
+    torch.cuda.synchronize()
+    assert (st2.row_len - old_len).tolist() == n_new  # the state object is reused: same rounds, same lengths
+    L = int(old_len[0])
+    for b in range(4):
+        acc = rounds[0][b] + rounds[1][b]
+        assert len(acc) == n_new[b]
+        full = torch.cat([ids[b].cuda(), torch.tensor(acc, device="cuda")])[None]
+        with torch.inference_mode():
+            out = model.model(input_ids=full, use_cache=True, return_dict=True)
+        ref_h = out.last_hidden_state[0, -1]
+        # the engine's next-round hidden is the final-norm hidden of the last accepted node
+        assert torch.allclose(st2.hidden[b], ref_h, atol=5e-3, rtol=5e-3), b
+        for l, layer in enumerate(out.past_key_values.layers):
+            n = L + len(acc)
+            assert torch.allclose(st2.k[l, b, :, :n], layer.keys[0, :, :n], atol=5e-3, rtol=5e-3), (b, l)
+            assert torch.allclose(st2.v[l, b, :, :n], layer.values[0, :, :n], atol=5e-3, rtol=5e-3), (b, l)
