@@ -203,7 +203,7 @@ typedef struct fg_kv_layer {
  * kv_len[b] + n_nodes up to the next multiple of 128 (within capacity) are
  * read with weight 0 and must hold finite values (a zero-filled cache does).
  * num_splits 0 = automatic (from max_kv_len, the longest prefix of the
- * batch).  workspace: fg_tree_attention_workspace_size bytes for the same
+ * batch), at most 128 (FG_EINVAL above).  workspace: fg_tree_attention_workspace_size bytes for the same
  * arguments (0 when one split suffices), zero-filled before first use (the
  * kernels leave it reusable). */
 size_t fg_tree_attention_workspace_size(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads,

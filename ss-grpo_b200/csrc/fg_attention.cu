@@ -136,7 +136,9 @@ static int resolve_splits(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t
 
 extern "C" size_t fg_tree_attention_workspace_size(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads,
                                                    int32_t head_dim, int32_t num_splits, int32_t max_kv_len) {
-    if (B <= 0 || n_nodes <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads || max_kv_len < 0) return 0;
+    if (B <= 0 || n_nodes <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads || max_kv_len < 0 ||
+        num_splits > tc::kMaxSplits)
+        return 0;
     (void)head_dim;
     const int G = n_q_heads / n_kv_heads;
     const int groups = (n_nodes * G + kMaxRows - 1) / kMaxRows;
@@ -155,6 +157,7 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
         n_q_heads % n_kv_heads)
         return FG_EINVAL;
     if (n_nodes > FG_MAX_TREE_NODES) return FG_ECAPACITY;
+    if (num_splits > tc::kMaxSplits) return FG_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
     if (dtype == FG_DTYPE_F32) {
         const int G = n_q_heads / n_kv_heads;

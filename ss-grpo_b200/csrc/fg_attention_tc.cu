@@ -61,6 +61,8 @@ constexpr uint32_t kTmemCols = 512;           // S0 [0,128) S1 [128,256) O0 [256
 constexpr uint32_t kColO0 = 256;
 constexpr int64_t kWaitNs = 1000000000LL;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kMaxSplits = 128;               // the merge keeps [2 x splits x 128] floats in smem
+static_assert(2 * kMaxSplits * kRows * 4 <= kOffBar, "split (m, l) tables fit below the barriers");
 
 struct Params {
     const __nv_bfloat16* q;
@@ -688,27 +690,71 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     __threadfence();
     const float* wo_all = p.ws_o + (int64_t)item * p.splits * (kRows * kD);
     const float* wml_all = p.ws_ml + (int64_t)item * p.splits * (2 * kRows);
-    for (int e = threadIdx.x; e < R * (kD / 2); e += blockDim.x) {
-        const int rw = e / (kD / 2), d = (e % (kD / 2)) * 2;
+    // (1) every split's (m, l) per row -> shared memory in one parallel pass
+    // (Q, P and the ring are idle now; splits <= kMaxSplits), then per row
+    // the weight of each split, exp2(m_s - m) / l, in place of m_s
+    float* wt = reinterpret_cast<float*>(smem);  // [split][row]
+    float* ls = wt + p.splits * kRows;           // [split][row]
+    for (int e = threadIdx.x; e < p.splits * R; e += blockDim.x) {
+        const int s2 = e / R, rw = e - s2 * R;
+        wt[s2 * kRows + rw] = __ldcg(wml_all + s2 * 2 * kRows + rw);
+        ls[s2 * kRows + rw] = __ldcg(wml_all + s2 * 2 * kRows + kRows + rw);
+    }
+    __syncthreads();
+    for (int rw = threadIdx.x; rw < R; rw += blockDim.x) {
         float mt = -INFINITY;
-        for (int s2 = 0; s2 < p.splits; ++s2) mt = fmaxf(mt, __ldcg(wml_all + s2 * 2 * kRows + rw));
-        float lt = 0.0f, o0 = 0.0f, o1 = 0.0f;
-        if (mt != -INFINITY) {
-            for (int s2 = 0; s2 < p.splits; ++s2) {
-                const float ms = __ldcg(wml_all + s2 * 2 * kRows + rw);
-                if (ms == -INFINITY) continue;
-                const float w = ex2(ms - mt);
-                lt += w * __ldcg(wml_all + s2 * 2 * kRows + kRows + rw);
-                const float2 ov =
-                    __ldcg(reinterpret_cast<const float2*>(wo_all + (int64_t)s2 * kRows * kD + rw * kD + d));
-                o0 += w * ov.x;
-                o1 += w * ov.y;
-            }
+        for (int s2 = 0; s2 < p.splits; ++s2) mt = fmaxf(mt, wt[s2 * kRows + rw]);
+        float lt = 0.0f;
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+            const float ms = wt[s2 * kRows + rw];
+            const float w = (ms == -INFINITY) ? 0.0f : ex2(ms - mt);
+            lt += w * ls[s2 * kRows + rw];
+            wt[s2 * kRows + rw] = w;
         }
         const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-        const int rr = row0 + rw;
-        __nv_bfloat16* orow = p.out + (((int64_t)b * p.N + rr / p.G) * p.Hq + kvh * p.G + rr % p.G) * kD;
-        *reinterpret_cast<__nv_bfloat162*>(orow + d) = __floats2bfloat162_rn(o0 * inv, o1 * inv);
+        for (int s2 = 0; s2 < p.splits; ++s2) wt[s2 * kRows + rw] *= inv;
+    }
+    __syncthreads();
+    // (2) out[row, 4 dims] = sum_s wt[s][row] O_s[row, 4 dims]; each thread
+    // keeps four such outputs in flight so that the partials' L2 reads overlap
+    // (partials are finite: splits without visible slots wrote zeros)
+    const int total = R * (kD / 4);
+    for (int e0 = threadIdx.x; e0 < total; e0 += 4 * blockDim.x) {
+        float4 acc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 2
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+            float4 v[4];
+            float w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = min(e0 + u * (int)blockDim.x, total - 1);
+                const int rw = e / (kD / 4), d = (e % (kD / 4)) * 4;
+                v[u] = __ldcg(reinterpret_cast<const float4*>(wo_all + (int64_t)s2 * kRows * kD + rw * kD + d));
+                w[u] = wt[s2 * kRows + rw];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                acc[u].x = fmaf(w[u], v[u].x, acc[u].x);
+                acc[u].y = fmaf(w[u], v[u].y, acc[u].y);
+                acc[u].z = fmaf(w[u], v[u].z, acc[u].z);
+                acc[u].w = fmaf(w[u], v[u].w, acc[u].w);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u * (int)blockDim.x;
+            if (e < total) {
+                const int rw = e / (kD / 4), d = (e % (kD / 4)) * 4;
+                const int rr = row0 + rw;
+                __nv_bfloat16* orow = p.out + (((int64_t)b * p.N + rr / p.G) * p.Hq + kvh * p.G + rr % p.G) * kD;
+                uint2 pk;
+                pk.x = pack2(acc[u].x, acc[u].y);
+                pk.y = pack2(acc[u].z, acc[u].w);
+                *reinterpret_cast<uint2*>(orow + d) = pk;
+            }
+        }
     }
     if (threadIdx.x == 0) p.ws_cnt[item] = 0;
 }

@@ -384,7 +384,7 @@ def _attn_reference(q, k, v, kv_len, tree, scale):
 @pytest.mark.parametrize("B,n,hq,hkv,L,splits", [
     (8, 13, 12, 2, 1024, 0), (8, 13, 12, 2, 1024, 1), (4, 13, 12, 2, 700, 3), (6, 32, 28, 4, 517, 0),
     (2, 64, 32, 8, 300, 2), (3, 128, 32, 8, 129, 0), (1, 16, 32, 8, 4000, 0), (5, 1, 12, 2, 63, 0),
-    (2, 8, 8, 8, 0, 0), (64, 13, 12, 2, 1024, 0),
+    (2, 8, 8, 8, 0, 0), (64, 13, 12, 2, 1024, 0), (1, 16, 32, 8, 4000, 24), (2, 13, 12, 2, 1500, 64),
 ])
 def test_tree_attention_bf16(ops, B, n, hq, hkv, L, splits):
     g = torch.Generator().manual_seed(B * 1000 + n)
