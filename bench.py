@@ -302,7 +302,9 @@ def run_ours(args, rank, world, local_rank):
         if not args.no_e2e and args.e2e_calls > 0:
             e_ids = ids.pin_memory()
             e_mask = mask.pin_memory()
-            dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + 4)  # warm
+            # warm-up with the timed calls' arguments: the same decode state and
+            # round configuration, so every timed round replays a captured graph
+            dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + args.e2e_new)
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
