@@ -182,12 +182,19 @@ fg_status fg_build_tree(const fg_plan_params *plan, const int32_t *root, const i
 
 /* -------------------------------------------------------- tree attention */
 typedef struct fg_kv_layer {
-    void *k;          /* [B, Hkv, capacity, D] addressed with the strides below */
+    void *k;          /* [batch, Hkv, capacity, D] addressed with the strides below */
     void *v;
     int64_t stride_b; /* elements */
     int64_t stride_h;
     int64_t stride_s;
     int32_t capacity; /* positions per (row, head) */
+    /* Row map for rounds over a subset of the cache's rows (finished rows
+     * retired without moving any K/V): call row b uses cache row rows[b].
+     * NULL = identity (then batch is ignored and the cache has the call's B
+     * rows).  A mapped row outside [0, batch) is skipped and records
+     * FG_EINVAL in the device error word. */
+    const int32_t *rows;
+    int32_t batch;    /* rows of the cache when rows != NULL */
 } fg_kv_layer;
 
 /* Flash-decoding GQA attention of the tree queries of one layer:
@@ -277,6 +284,10 @@ typedef struct fg_accept_args {
     void *hidden_out;          /* [B][hidden_dim] */
     int32_t hidden_dim;
     int32_t hidden_elem_bytes;
+    /* compaction row map (see fg_kv_layer.rows): row b compacts cache row
+     * kv_rows[b] of kv_batch rows; NULL = identity */
+    const int32_t *kv_rows;
+    int32_t kv_batch;
 } fg_accept_args;
 
 /* One CTA per row: the exact_target walk of exact_accept_paths_batch

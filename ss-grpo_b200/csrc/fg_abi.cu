@@ -9,6 +9,18 @@ __device__ int32_t g_fg_error_word = 0;
 
 namespace fg {
 
+// Cache row of call row b under a row map (fg_kv_layer.rows): -1 (and
+// FG_EINVAL recorded) when the mapped row lies outside the cache.
+__device__ __forceinline__ int32_t cache_row(const int32_t* rows, int32_t batch, int32_t b) {
+    if (rows == nullptr) return b;
+    const int32_t r = rows[b];
+    if (r < 0 || r >= batch) {
+        atomicCAS(&g_fg_error_word, 0, FG_EINVAL);
+        return -1;
+    }
+    return r;
+}
+
 static thread_local int32_t t_last_cuda_error = 0;
 
 void set_cuda_error(cudaError_t e) { t_last_cuda_error = (int32_t)e; }

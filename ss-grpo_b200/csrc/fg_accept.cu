@@ -65,6 +65,8 @@ struct AcceptParams {
     void* hidden_out;
     int32_t hidden_dim;
     int32_t hidden_elem_bytes;
+    const int32_t* kv_rows;  // row -> cache row for the compaction (NULL = identity)
+    int32_t kv_batch;
 };
 
 // g_fg_error_word is defined in fg_abi.cu (same translation unit).
@@ -206,10 +208,11 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
         p.last_node[b] = s_path[a - 1];
         p.finished[b] = fin ? 1 : 0;
     }
-    // extract_path compaction of the accepted slots
-    if (p.n_layers > 0)
+    // extract_path compaction of the accepted slots (in the row's cache row)
+    const int32_t bk = cache_row(p.kv_rows, p.kv_batch, b);
+    if (p.n_layers > 0 && bk >= 0)
         compact_row(kv, p.n_layers, p.kv_elem_bytes, p.n_kv_heads, p.head_dim, p.kv_stride_b, p.kv_stride_h,
-                    p.kv_stride_s, b, len0, s_path, a);
+                    p.kv_stride_s, bk, len0, s_path, a);
     // next-round hidden state
     if (p.hidden_out != nullptr) {
         const int64_t bytes = (int64_t)p.hidden_dim * p.hidden_elem_bytes;
@@ -262,6 +265,7 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     }
     if (a->hidden_out && (!a->tree_hidden || ((int64_t)a->hidden_dim * a->hidden_elem_bytes) % 16 != 0))
         return FG_EINVAL;
+    if (a->kv_rows && a->kv_batch <= 0) return FG_EINVAL;
     AcceptParams p;
     p.logits = a->logits;
     p.logits_row_stride = a->logits_row_stride;
@@ -302,6 +306,8 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     p.hidden_out = a->hidden_out;
     p.hidden_dim = a->hidden_dim;
     p.hidden_elem_bytes = a->hidden_elem_bytes;
+    p.kv_rows = a->kv_rows;
+    p.kv_batch = a->kv_batch;
     KvPtrs kv;
     for (int l = 0; l < FG_MAX_LAYERS; ++l) {
         kv.k[l] = l < a->n_layers ? a->k_layers[l] : 0;

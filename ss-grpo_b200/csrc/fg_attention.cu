@@ -31,7 +31,8 @@ constexpr int kMaxRows = 128;
 __global__ void tree_attn_f32_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                      const float* __restrict__ vc, int64_t sb, int64_t sh, int64_t ss,
                                      const int32_t* __restrict__ kv_len, const uint32_t* __restrict__ anc, int32_t N,
-                                     int32_t Hq, int32_t Hkv, int32_t D, float scale, float* __restrict__ out) {
+                                     int32_t Hq, int32_t Hkv, int32_t D, float scale, const int32_t* __restrict__ kv_rows,
+                                     int32_t kv_batch, float* __restrict__ out) {
     const int node = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int G = Hq / Hkv;
     const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -48,8 +49,9 @@ __global__ void tree_attn_f32_kernel(const float* __restrict__ q, const float* _
     const int L = kv_len[b];
     const int T = L + N;
     float m = -INFINITY, l = 0.0f;
-    const float* kb = kc + (int64_t)b * sb + (int64_t)kvh * sh;
-    const float* vb = vc + (int64_t)b * sb + (int64_t)kvh * sh;
+    const int32_t bk = max(cache_row(kv_rows, kv_batch, b), 0);  // an unmapped row reads row 0 (error recorded)
+    const float* kb = kc + (int64_t)bk * sb + (int64_t)kvh * sh;
+    const float* vb = vc + (int64_t)bk * sb + (int64_t)kvh * sh;
     for (int pos = 0; pos < T; ++pos) {
         if (pos >= L) {
             const int j = pos - L;
@@ -158,6 +160,8 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
         return FG_EINVAL;
     if (n_nodes > FG_MAX_TREE_NODES) return FG_ECAPACITY;
     if (num_splits > tc::kMaxSplits) return FG_EINVAL;
+    if (kv->rows && kv->batch <= 0) return FG_EINVAL;
+    const int32_t cache_b = kv->rows ? kv->batch : B;  // rows of the K/V tensors
     cudaStream_t st = (cudaStream_t)stream;
     if (dtype == FG_DTYPE_F32) {
         const int G = n_q_heads / n_kv_heads;
@@ -165,7 +169,8 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
         dim3 grid(n_nodes, n_kv_heads, B);
         tree_attn_f32_kernel<<<grid, 32 * G, 0, st>>>((const float*)q, (const float*)kv->k, (const float*)kv->v,
                                                       kv->stride_b, kv->stride_h, kv->stride_s, kv_len, anc_bits,
-                                                      n_nodes, n_q_heads, n_kv_heads, head_dim, scale, (float*)out);
+                                                      n_nodes, n_q_heads, n_kv_heads, head_dim, scale, kv->rows,
+                                                      kv->batch, (float*)out);
         return launch_status();
     }
     if (dtype != FG_DTYPE_BF16) return FG_EUNSUPPORTED;
@@ -195,6 +200,8 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
     p.ws_o = nullptr;
     p.ws_ml = nullptr;
     p.ws_cnt = nullptr;
+    p.kv_rows = kv->rows;
+    p.kv_batch = kv->batch;
     if (p.splits > 1) {
         const size_t need = (size_t)items * p.splits * (kMaxRows * kD + 2 * kMaxRows) * sizeof(float) +
                             (size_t)items * sizeof(int32_t);
@@ -204,8 +211,8 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
         p.ws_cnt = (int32_t*)(p.ws_ml + (size_t)items * p.splits * 2 * kMaxRows);
     }
     CUtensorMap mk, mv;
-    if (!make_kv_map(&mk, kv->k, B, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s) ||
-        !make_kv_map(&mv, kv->v, B, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s))
+    if (!make_kv_map(&mk, kv->k, cache_b, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s) ||
+        !make_kv_map(&mv, kv->v, cache_b, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s))
         return FG_EINVAL;
     static bool attr_set[64] = {};
     int dev = 0;

@@ -74,6 +74,8 @@ struct Params {
     float* ws_o;
     float* ws_ml;
     int32_t* ws_cnt;
+    const int32_t* kv_rows;  // call row -> cache row (NULL = identity)
+    int32_t kv_batch;
 };
 
 // ---------------------------------------------------------------- PTX glue
@@ -307,6 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const int split = blockIdx.x;
     const int kvh = blockIdx.y / p.groups, grp = blockIdx.y % p.groups;
     const int b = blockIdx.z;
+    // cache row of this call row (a row outside the cache records FG_EINVAL
+    // and reads row 0, so the loads stay in bounds)
+    const int bkv = max(cache_row(p.kv_rows, p.kv_batch, b), 0);
     const int row0 = grp * kRows;
     const int R = min(kRows, p.rows_total - row0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -324,16 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         uint8_t* st = smem + kOffStage + s * kStageBytes;
         const int slot = (c0 + i) * kBlk;
         bar_expect(&bars->k_full[s], 2 * kBox);
-        tma_4d(st, &tmK, 0, slot, kvh, b, &bars->k_full[s]);
-        tma_4d(st + kBox, &tmK, 64, slot, kvh, b, &bars->k_full[s]);
+        tma_4d(st, &tmK, 0, slot, kvh, bkv, &bars->k_full[s]);
+        tma_4d(st + kBox, &tmK, 64, slot, kvh, bkv, &bars->k_full[s]);
     };
     auto load_v = [&](int i) {
         const int s = i % kStages;
         uint8_t* st = smem + kOffStage + s * kStageBytes + 2 * kBox;
         const int slot = (c0 + i) * kBlk;
         bar_expect(&bars->v_full[s], 2 * kBox);
-        tma_4d(st, &tmV, 0, slot, kvh, b, &bars->v_full[s]);
-        tma_4d(st + kBox, &tmV, 64, slot, kvh, b, &bars->v_full[s]);
+        tma_4d(st, &tmV, 0, slot, kvh, bkv, &bars->v_full[s]);
+        tma_4d(st + kBox, &tmV, 64, slot, kvh, bkv, &bars->v_full[s]);
     };
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {

@@ -48,7 +48,7 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
                                const float* __restrict__ inv_freq, float attn_scaling, int32_t n_nodes, int32_t Hq,
                                int32_t Hkv, int32_t D, const int32_t* __restrict__ kv_len, T* __restrict__ kc,
                                T* __restrict__ vc, int64_t sb, int64_t sh, int64_t ss, int32_t cap,
-                               T* __restrict__ q_out) {
+                               const int32_t* __restrict__ kv_rows, int32_t kv_batch, T* __restrict__ q_out) {
     __shared__ float cs[2][128];  // cos / sin per frequency, once per token
     // the tree attention that follows may start its prefix loads now; it
     // waits for this grid to finish before reading Q or the tree K/V
@@ -59,7 +59,8 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
     const int32_t half = D / 2;
     const T* src = qkv + (int64_t)tokn * (Hq + 2 * Hkv) * D;
     const int32_t slotpos = kv_len[b] + node;
-    const bool in_cap = slotpos < cap;
+    const int32_t bk = cache_row(kv_rows, kv_batch, b);
+    const bool in_cap = slotpos < cap && bk >= 0;
     for (int32_t i = threadIdx.x; i < half; i += blockDim.x) {
         const float f = __fmul_rn(pos, inv_freq[i]);
         float c = cosf(f), s = sinf(f);
@@ -85,7 +86,7 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
             qo[i + half] = from_f<T>(o2);
         } else if (in_cap) {
             const int32_t kh = h - Hq;
-            T* ko = kc + (int64_t)b * sb + (int64_t)kh * sh + (int64_t)slotpos * ss;
+            T* ko = kc + (int64_t)bk * sb + (int64_t)kh * sh + (int64_t)slotpos * ss;
             ko[i] = from_f<T>(o1);
             ko[i + half] = from_f<T>(o2);
         }
@@ -93,7 +94,7 @@ __global__ void rope_kv_kernel(const T* __restrict__ qkv, const int32_t* __restr
     if (in_cap)
         for (int32_t e = threadIdx.x; e < Hkv * D; e += blockDim.x) {
             const int32_t kh = e / D, d = e % D;
-            vc[(int64_t)b * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d] = src[(int64_t)(Hq + Hkv + kh) * D + d];
+            vc[(int64_t)bk * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d] = src[(int64_t)(Hq + Hkv + kh) * D + d];
         }
 }
 
@@ -124,7 +125,7 @@ template <typename T>
 __global__ void __launch_bounds__(128) rope_kv_table_kernel(
     const T* __restrict__ qkv, const T* __restrict__ cs, int32_t n_tokens, int32_t n_nodes, int32_t Hq, int32_t Hkv,
     int32_t D, const int32_t* __restrict__ kv_len, T* __restrict__ kc, T* __restrict__ vc, int64_t sb, int64_t sh,
-    int64_t ss, int32_t cap, T* __restrict__ q_out) {
+    int64_t ss, int32_t cap, const int32_t* __restrict__ kv_rows, int32_t kv_batch, T* __restrict__ q_out) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr int NV = 16 / sizeof(T);
     const int32_t tokn = blockIdx.x;
@@ -132,7 +133,8 @@ __global__ void __launch_bounds__(128) rope_kv_table_kernel(
     const int32_t half = D / 2, vph = half / NV;  // vectors per half-head
     const T* src = qkv + (int64_t)tokn * (Hq + 2 * Hkv) * D;
     const int32_t slotpos = kv_len[b] + node;
-    const bool in_cap = slotpos < cap;
+    const int32_t bk = cache_row(kv_rows, kv_batch, b);
+    const bool in_cap = slotpos < cap && bk >= 0;
     const T* cr = cs + (int64_t)tokn * half;
     const T* sr = cs + ((int64_t)n_tokens + tokn) * half;
     for (int32_t e = threadIdx.x; e < (Hq + Hkv) * vph; e += blockDim.x) {
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(128) rope_kv_table_kernel(
         if (h < Hq) {
             dst = q_out + ((int64_t)tokn * Hq + h) * D;
         } else if (in_cap) {
-            dst = kc + (int64_t)b * sb + (int64_t)(h - Hq) * sh + (int64_t)slotpos * ss;
+            dst = kc + (int64_t)bk * sb + (int64_t)(h - Hq) * sh + (int64_t)slotpos * ss;
         }
         if (dst) {
             *reinterpret_cast<uint4*>(dst + i) = r1;
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(128) rope_kv_table_kernel(
     if (in_cap)
         for (int32_t e = threadIdx.x; e < Hkv * (D / NV); e += blockDim.x) {
             const int32_t kh = e / (D / NV), d = (e % (D / NV)) * NV;
-            *reinterpret_cast<uint4*>(vc + (int64_t)b * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d) =
+            *reinterpret_cast<uint4*>(vc + (int64_t)bk * sb + (int64_t)kh * sh + (int64_t)slotpos * ss + d) =
                 *reinterpret_cast<const uint4*>(src + (int64_t)(Hq + Hkv + kh) * D + d);
         }
 }
@@ -359,13 +361,13 @@ extern "C" fg_status fg_rope_kv_write(const void* qkv, int32_t dtype, const int3
         FG_DISPATCH(dtype, (rope_kv_table_kernel<T><<<B * n_nodes, 128, 0, st>>>(
                                 (const T*)qkv, (const T*)cos_sin, B * n_nodes, n_nodes, n_q_heads, n_kv_heads,
                                 head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b, kv->stride_h, kv->stride_s,
-                                kv->capacity, (T*)q_out)));
+                                kv->capacity, kv->rows, kv->batch, (T*)q_out)));
         return launch_status();
     }
     FG_DISPATCH(dtype, (rope_kv_kernel<T><<<B * n_nodes, 128, 0, st>>>(
                             (const T*)qkv, positions, inv_freq, attention_scaling, n_nodes, n_q_heads, n_kv_heads,
                             head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b, kv->stride_h, kv->stride_s,
-                            kv->capacity, (T*)q_out)));
+                            kv->capacity, kv->rows, kv->batch, (T*)q_out)));
     return launch_status();
 }
 

@@ -38,7 +38,7 @@ class PlanParams(ctypes.Structure):
 
 class KvLayer(ctypes.Structure):
     _fields_ = [("k", c_vp), ("v", c_vp), ("stride_b", c_i64), ("stride_h", c_i64), ("stride_s", c_i64),
-                ("capacity", c_i32)]
+                ("capacity", c_i32), ("rows", c_vp), ("batch", c_i32)]
 
 
 class AcceptArgs(ctypes.Structure):
@@ -52,7 +52,7 @@ class AcceptArgs(ctypes.Structure):
         ("n_layers", c_i32), ("k_layers", ctypes.POINTER(c_u64)), ("v_layers", ctypes.POINTER(c_u64)),
         ("kv_elem_bytes", c_i32), ("n_kv_heads", c_i32), ("head_dim", c_i32), ("kv_stride_b", c_i64),
         ("kv_stride_h", c_i64), ("kv_stride_s", c_i64), ("tree_hidden", c_vp), ("hidden_out", c_vp),
-        ("hidden_dim", c_i32), ("hidden_elem_bytes", c_i32),
+        ("hidden_dim", c_i32), ("hidden_elem_bytes", c_i32), ("kv_rows", c_vp), ("kv_batch", c_i32),
     ]
 
 

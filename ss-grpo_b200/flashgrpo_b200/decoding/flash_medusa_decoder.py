@@ -182,7 +182,11 @@ class FlashMedusaDecoder:
         pinned = None
         verify_time = 0.0
         while any(active_host):
-            n_active = sum(active_host)
+            # finished rows retire: the round runs on the active rows only
+            # (select_cache_batch semantics), through a row map into the
+            # cache when some rows have finished
+            act_rows = [r for r in range(B) if active_host[r]]
+            n_active = len(act_rows)
             use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
             plan = self._plan(n_active)
             if not use_tree:
@@ -192,22 +196,28 @@ class FlashMedusaDecoder:
             plan.active_heads = nh
             dcap = nh + 2
             adaptive = bool(cfg.adaptive_tree_enabled) and nh > 0
-            rb = eng.buffers(B, plan, nh, dcap, adaptive=adaptive)
+            if n_active < B:
+                rs = eng.view(st, n_active, n_heads)
+                rows_host = torch.tensor(act_rows, dtype=torch.int32).pin_memory()
+                rs.rows.copy_(rows_host, non_blocking=True)
+            else:
+                rs = st
+            rb = eng.buffers(n_active, plan, nh, dcap, adaptive=adaptive)
             params = self._params(n_active) if nh > 0 else ops.plan_params(
                 tree_mode="explicit", active_batch_size=n_active, num_medusa_heads=0, cpeak_nodes=0,
                 min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=1, fixed_tree_topk_by_depth=())
-            key = (id(st), B, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, n_active, adaptive,
+            key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive,
                    dataclasses.astuple(rcfg))
             tv = time.time()
             if cfg.use_cuda_graphs and key in seen:
                 if key not in graphs:
-                    graphs[key] = (eng.graph_round(st, rb, params, rcfg), params)
+                    graphs[key] = (eng.graph_round(rs, rb, params, rcfg), params)
                 graphs[key][0].replay()
             else:
-                eng.run_round(st, rb, params, rcfg)
+                eng.run_round(rs, rb, params, rcfg)
                 seen.add(key)
             out = rb.out
-            flat = torch.cat([out["acc_len"], out["finished"], st.pending, rb.tree["plan"], out["acc_tokens"].view(-1)])
+            flat = torch.cat([out["acc_len"], out["finished"], rs.pending, rb.tree["plan"], out["acc_tokens"].view(-1)])
             if pinned is None or pinned.numel() < flat.numel():
                 pinned = torch.empty(flat.numel(), dtype=torch.int32, pin_memory=True)
             host = pinned[: flat.numel()]
@@ -215,11 +225,12 @@ class FlashMedusaDecoder:
             torch.cuda.current_stream(dev).synchronize()
             verify_time += time.time() - tv
             vals = host.tolist()
-            acc_len = vals[:B]
-            fin = vals[B:2 * B]
-            pend = vals[2 * B:3 * B]
-            plan_dev = vals[3 * B:3 * B + 16]
-            toks = vals[3 * B + 16:]
+            Br = n_active  # outputs are per round row: round row i is state row act_rows[i]
+            acc_len = vals[:Br]
+            fin = vals[Br:2 * Br]
+            pend = vals[2 * Br:3 * Br]
+            plan_dev = vals[3 * Br:3 * Br + 16]
+            toks = vals[3 * Br + 16:]
             # the round's tree as built on the device (adaptive rounds may be smaller)
             n_tree = plan_dev[10] if nh > 0 else 1
             topk_round = plan_dev[2:2 + plan_dev[1]] if nh > 0 else []
@@ -229,13 +240,11 @@ class FlashMedusaDecoder:
             tree_plan_last = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
                               "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
                               "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa"}
-            for r in range(B):
-                if not active_host[r]:
-                    continue
+            for i, r in enumerate(act_rows):
                 if pending_host[r] >= 0:
                     stats["total_correction_tokens"] += 1
-                a = acc_len[r]
-                generated[r].extend(toks[r * dcap: r * dcap + a])
+                a = acc_len[i]
+                generated[r].extend(toks[i * dcap: i * dcap + a])
                 stats["total_acc_length"] += a
                 stats["total_decoded_token_num"] += 1
                 stats["total_accepted_medusa_tokens"] += max(a - 1, 0)
@@ -244,9 +253,9 @@ class FlashMedusaDecoder:
                 for d in range(2, a + 1):
                     accept_by_depth[d] = accept_by_depth.get(d, 0) + 1
                 row_len_host[r] += a
-                if fin[r]:
+                if fin[i]:
                     active_host[r] = False
-            pending_host = pend
+                pending_host[r] = pend[i]
         total_time = time.time() - total_start
         rounds = max(stats["total_verify_rounds"], 1)
         decoded = max(stats["total_decoded_token_num"], 1)

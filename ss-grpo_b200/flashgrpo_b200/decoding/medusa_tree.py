@@ -12,6 +12,8 @@ not part of this path.
 """
 from __future__ import annotations
 
+import dataclasses
+import itertools
 import math
 from dataclasses import dataclass, field
 
@@ -177,6 +179,31 @@ def dense_topology(plan: TreePlan, n_heads_available: int | None = None) -> tupl
 def internal_nodes(parents: list[int]) -> list[int]:
     has_child = set(p for p in parents if p >= 0)
     return [i for i in range(len(parents)) if i in has_child]
+
+
+def max_adaptive_internal(plan: TreePlan, n_heads_available: int | None = None) -> int:
+    """Most internal nodes that any adaptive tree of this base plan can have.
+
+    Adaptive top-k (flash_medusa_decoder.py:1021-1095) keeps every depth's
+    width in [1, base width] and may drop trailing depths; the tree is then
+    expanded in BFS order up to the node budget.  A narrower, deeper tree can
+    have more internal nodes than the base plan's own (e.g. a 16-node budget:
+    base (4, 3, 2) has 5 internal nodes, (4, 1, 1) has 9), so buffers of
+    internal-node rows are sized by this bound.  Every width vector is tried
+    (few: the product of the base widths); past 4096 of them the bound is
+    the node budget - 1."""
+    ks = [int(k) for k in plan.topk_by_depth[: plan.active_heads]]
+    if n_heads_available is not None:
+        ks = ks[:n_heads_available]
+    ks = [k for k in ks if k > 0]
+    if math.prod(ks) * max(len(ks), 1) > 4096:
+        return max(plan.node_budget_per_seq - 1, 1)
+    best = len(internal_nodes(dense_topology(plan, n_heads_available)[0]))
+    for depth in range(1, len(ks) + 1):
+        for widths in itertools.product(*[range(1, k + 1) for k in ks[:depth]]):
+            p = dataclasses.replace(plan, active_heads=depth, topk_by_depth=list(widths))
+            best = max(best, len(internal_nodes(dense_topology(p)[0])))
+    return best
 
 
 def build_batch_trees(root_tokens: torch.Tensor, medusa_logits: list[torch.Tensor], plan: TreePlan,

@@ -32,7 +32,7 @@ import torch
 
 from .. import _native as N
 from .. import ops
-from ..decoding.medusa_tree import TreePlan, dense_topology, internal_nodes
+from ..decoding.medusa_tree import TreePlan, dense_topology, internal_nodes, max_adaptive_internal
 
 
 # ------------------------------------------------------------------ weights
@@ -171,6 +171,50 @@ class DecodeState:
         return self.X[: self.B]
 
 
+class RoundView:
+    """The active rows of a DecodeState as a compact batch for one round:
+    finished rows are retired without moving any K/V (the replacement of
+    select_cache_batch, qwen_flashgrpo_wrapper.py:100-118).  Round row i is
+    state row rows[i]; the per-row scalars and the hidden state are gathered
+    before the round and scattered back after it (a few hundred KB), while
+    the RoPE/KV write, the tree attention and the extract_path compaction
+    address the shared cache through the row map.  It has DecodeState's
+    attributes, so a round runs on it unchanged."""
+
+    def __init__(self, st: DecodeState, B: int, n_heads: int):
+        dev = st.row_len.device
+        self.base = st
+        self.B, self.capacity = B, st.capacity
+        self.rows = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.row_len = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.pending = torch.full((B,), -1, dtype=torch.int32, device=dev)
+        self.active = torch.ones(B, dtype=torch.int32, device=dev)
+        self.seq_ids = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.round_dev = st.round_dev  # the round counter is shared by all rows
+        self.X = torch.zeros(((n_heads + 1) * B, st.X.shape[1]), dtype=st.X.dtype, device=dev)
+        self.k, self.v = st.k, st.v
+        self.kv_layers = [ops.kv_layer(st.k[l], st.v[l], rows=self.rows) for l in range(st.k.shape[0])]
+
+    @property
+    def hidden(self) -> torch.Tensor:
+        return self.X[: self.B]
+
+    def gather(self):
+        st, idx = self.base, self.rows.long()
+        torch.index_select(st.row_len, 0, idx, out=self.row_len)
+        torch.index_select(st.pending, 0, idx, out=self.pending)
+        torch.index_select(st.active, 0, idx, out=self.active)
+        torch.index_select(st.seq_ids, 0, idx, out=self.seq_ids)
+        torch.index_select(st.hidden, 0, idx, out=self.hidden)
+
+    def scatter(self):
+        st, idx = self.base, self.rows.long()
+        st.row_len.index_copy_(0, idx, self.row_len)
+        st.pending.index_copy_(0, idx, self.pending)
+        st.active.index_copy_(0, idx, self.active)
+        st.hidden.index_copy_(0, idx, self.hidden)
+
+
 class RoundBuffers:
     """Every intermediate of one round for a fixed (rows, plan) shape."""
 
@@ -226,10 +270,13 @@ class RoundBuffers:
         # is never larger, its unused nodes are inert (parent -2, no slot),
         # and the internal-row gather is rebuilt on the device from K2's
         # internal list each round.
+        # internal rows an adaptive tree can have: a narrower, deeper tree may
+        # have more internal nodes than the base plan's own
         self.adaptive = adaptive
-        self.j_int = torch.arange(max(len(idx), 1), dtype=torch.int32, **f)
-        self.hid_int = torch.empty((max(len(idx), 1), H), dtype=spec.dtype, **f)
-        self.tree_logits = torch.empty((max(len(idx), 1), V), dtype=spec.dtype, **f)
+        n_rows = B * max_adaptive_internal(plan, n_heads) if adaptive else len(idx)
+        self.j_int = torch.arange(max(n_rows, 1), dtype=torch.int32, **f)
+        self.hid_int = torch.empty((max(n_rows, 1), H), dtype=spec.dtype, **f)
+        self.tree_logits = torch.empty((max(n_rows, 1), V), dtype=spec.dtype, **f)
         self.dcap = dcap
         self.out = {k: torch.empty((B, dcap), **i32) for k in ("acc_tokens", "acc_nodes")}
         for k in ("acc_len", "correction", "last_node", "finished"):
@@ -496,13 +543,31 @@ class VerifyEngine:
                            max_length=cfg.max_length, row_len=st.row_len, outputs=outs, dcap=rb.dcap,
                            update_len=True, active=st.active, k_layers=[st.k[l] for l in range(self.spec.n_layers)],
                            v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,
-                           hidden_out=st.hidden)
+                           hidden_out=st.hidden, kv_rows=st.rows if isinstance(st, RoundView) else None)
         rb.acc_sum += rb.out["acc_len"].sum()
         st.round_dev += 1
 
-    def run_round(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig,
-                  attn_events=None):
-        """All device work of one round, enqueued on the current stream."""
+    def view(self, st: DecodeState, B: int, n_heads: int) -> RoundView:
+        """A (cached) compact view of B of st's rows; fill view.rows before
+        each round run on it."""
+        key = ("view", id(st), B, n_heads)
+        v = self._graphs.get(key)
+        if v is None:
+            v = RoundView(st, B, n_heads)
+            self._graphs[key] = v
+        return v
+
+    def run_round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None):
+        """All device work of one round, enqueued on the current stream.  st is
+        a DecodeState or a RoundView (gathered before, scattered after)."""
+        if isinstance(st, RoundView):
+            st.gather()
+            self._round(st, rb, params, cfg, attn_events)
+            st.scatter()
+        else:
+            self._round(st, rb, params, cfg, attn_events)
+
+    def _round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None):
         if cfg.chain:
             self.propose_chain(st, rb, cfg)
             self.build_tree(st, rb, params)

@@ -187,10 +187,15 @@ def build_tree(params: N.PlanParams, root: torch.Tensor, cand_idx: torch.Tensor 
 
 
 # --------------------------------------------------------------- attention
-def kv_layer(k: torch.Tensor, v: torch.Tensor) -> N.KvLayer:
+def kv_layer(k: torch.Tensor, v: torch.Tensor, rows: torch.Tensor | None = None) -> N.KvLayer:
+    """fg_kv_layer of caches [batch, Hkv, capacity, D]; rows (int32 [B],
+    optional): call row b reads / writes cache row rows[b]."""
     if k.shape != v.shape or k.stride() != v.stride() or k.dim() != 4 or k.stride(3) != 1:
         raise ValueError("K and V caches must be [B, Hkv, capacity, D] views with identical strides")
-    return N.KvLayer(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[2])
+    if rows is not None:
+        _need(rows, "rows", torch.int32)
+    return N.KvLayer(k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), k.shape[2],
+                     _ptr(rows), k.shape[0] if rows is not None else 0)
 
 
 def attention_workspace_bytes(B, n_nodes, n_q_heads, n_kv_heads, head_dim, *, num_splits=0, max_kv_len=0) -> int:
@@ -229,9 +234,10 @@ def layer_pointer_arrays(k_layers, v_layers):
 def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
                    row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
                    tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0,
-                   top_p: float = 1.0):
+                   top_p: float = 1.0, kv_rows=None):
     """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
-    acc_len/correction/pending/last_node/finished [B]."""
+    acc_len/correction/pending/last_node/finished [B]; kv_rows (int32 [B],
+    optional): row b compacts cache row kv_rows[b] of k_layers/v_layers."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     for name, t in (("slot", slot), ("tokens", tokens), ("parents", parents), ("row_len", row_len)):
@@ -261,6 +267,9 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
         a.k_layers, a.v_layers = kp, vp
         a.kv_elem_bytes, a.n_kv_heads, a.head_dim = ref.element_size(), ref.shape[1], ref.shape[3]
         a.kv_stride_b, a.kv_stride_h, a.kv_stride_s = ref.stride(0), ref.stride(1), ref.stride(2)
+        if kv_rows is not None:
+            _need(kv_rows, "kv_rows", torch.int32)
+            a.kv_rows, a.kv_batch = kv_rows.data_ptr(), ref.shape[0]
     if hidden_out is not None:
         a.tree_hidden, a.hidden_out = tree_hidden.data_ptr(), hidden_out.data_ptr()
         a.hidden_dim, a.hidden_elem_bytes = hidden_out.shape[-1], hidden_out.element_size()

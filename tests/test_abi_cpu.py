@@ -72,3 +72,36 @@ def test_plan_params_tables():
         ops.plan_params(tree_mode="sparse", active_batch_size=1, num_medusa_heads=1, cpeak_nodes=1,
                         min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=2,
                         fixed_tree_topk_by_depth=(1,))
+
+
+def test_ctypes_structures_match_the_header(tmp_path):
+    """The ctypes mirrors of fg_plan_params, fg_kv_layer and fg_accept_args
+    have the C structs' size and field offsets (compiled with gcc from the
+    header)."""
+    import shutil
+    import subprocess
+
+    from flashgrpo_b200 import _native as N
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"fg_plan_params": N.PlanParams, "fg_kv_layer": N.KvLayer, "fg_accept_args": N.AcceptArgs}
+    lines = []
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"fg_b200.h\"\nint main(void) {\n" +
+                   "\n".join(lines) + "\nreturn 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(REPO / "include"), "-o", str(exe), str(src)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, field, val = line.split()
+        got[(cname, field)] = int(val)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, (cname, f)

@@ -94,6 +94,52 @@ def test_generate_config1_matches_oracle(run):
     assert _native.read_device_error(clear=True) == 0
 
 
+@pytest.mark.parametrize("adaptive", [False, True])
+def test_generate_retires_finished_rows(adaptive):
+    """Rows that reach EOS at different rounds leave the batch (the reference's
+    select_cache_batch); later rounds run on the remaining rows through a row
+    map into the unmoved cache.  Tokens and statistics equal the oracle's,
+    which drops finished rows by index_select -- with adaptive trees this also
+    pins the confidence quantile to the active rows."""
+    from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
+    from flashgrpo_b200.utils import synthetic
+
+    cpu_model = synthetic.build_model(1)
+    gpu_model = synthetic.build_model(1).cuda()
+    st = synthetic.medusa_head_tensors(1)
+    ids, mask = synthetic.random_prompts(4, 128, 4096, seed=2)
+    run = dict(tree_mode="concurrency_aware", cpeak_nodes=128, max_tree_nodes_per_seq=32, max_tree_depth=4,
+               fixed_tree_topk_by_depth=(4, 3, 2), do_sample=True, top_p=1.0, adaptive_tree_enabled=adaptive,
+               adaptive_confidence_low=0.3, adaptive_confidence_high=0.9)
+    ocfg = rp.OracleConfig(**run)
+    max_length = 128 + 24
+    # an EOS token that one row emits early: that row retires while others go on
+    free = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(11), repeats=2,
+                       max_length=max_length, eos_token_id=-1)
+    eos = free["generated_token_ids"][0][3]
+    ref = rp.generate(cpu_model, _heads_list(st, 3), ids, mask, ocfg, rp.SeqRoundSampler(11), repeats=2,
+                      max_length=max_length, eos_token_id=eos)
+    lens = [len(t) for t in ref["generated_token_ids"]]
+    assert min(lens) < 24 and max(lens) > min(lens), lens  # rows retired at different rounds
+
+    class Tok:
+        pad_token_id = 0
+        eos_token_id = eos
+
+    cfg = FlashMedusaConfig(num_medusa_heads=3, sampling_seed=11, **run)
+    dec = FlashMedusaDecoder(gpu_model, {k: v.cuda() for k, v in st.items()}, Tok(), cfg)
+    for _ in range(2):  # the second call replays the graphs captured for the shrinking batches
+        res = dec.generate(ids, mask, repeated_generate_nums=2, max_length=max_length)
+        assert res["generated_token_ids"] == ref["generated_token_ids"]
+        for k in ("total_acc_length", "total_decoded_token_num", "total_verify_rounds", "total_correction_tokens",
+                  "total_accepted_medusa_tokens", "total_proposed_medusa_tokens"):
+            assert res[k] == ref[k], k
+        assert res["average_active_batch_size"] < 8
+    from flashgrpo_b200 import _native
+
+    assert _native.read_device_error(clear=True) == 0
+
+
 def test_verify_round_bf16_against_hf_eager():
     from flashgrpo_b200 import ops
     from flashgrpo_b200.decoding.medusa_tree import plan_tree

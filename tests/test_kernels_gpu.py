@@ -246,7 +246,7 @@ def test_build_tree_matches_oracle(ops, case):
 # ------------------------------------------------ acceptance + compaction
 def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sample, temperature, row_len,
                 max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None,
-                top_p=1.0):
+                top_p=1.0, kv_rows=None):
     B = tokens.shape[0]
     outs = {k: torch.full((B, dcap), -9, dtype=torch.int32, device=DEV) for k in ("acc_tokens", "acc_nodes")}
     for k in ("acc_len", "correction", "pending", "last_node", "finished"):
@@ -256,7 +256,7 @@ def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sa
                        uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
                        max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=False,
                        k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out,
-                       top_p=top_p)
+                       top_p=top_p, kv_rows=kv_rows)
     torch.cuda.synchronize()
     return outs, rl
 
@@ -460,6 +460,86 @@ def test_rope_kv_write_matches_hf(ops, dtype):
         assert torch.allclose(kc[b, :, L:L + n].float(), kr[b].float(), atol=tol, rtol=tol)
         assert torch.equal(vc[b, :, L:L + n], x[b, hq + hkv:])
         assert torch.count_nonzero(kc[b, :, :L]) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_row_map_matches_gathered_cache(ops, dtype):
+    """Retired rows: RoPE/KV write, tree attention and the accept compaction
+    over a subset of the cache's rows through the row map (fg_kv_layer.rows,
+    kv_rows) give the bits of the same calls on a gathered copy of those rows
+    and leave every other row untouched."""
+    g = torch.Generator().manual_seed(21)
+    Bc, n, hq, hkv, D, cap = 7, 13, 12, 2, 128, 320
+    rows = [5, 0, 3, 6]
+    others = [r for r in range(Bc) if r not in rows]
+    B = len(rows)
+    rows_d = torch.tensor(rows, dtype=torch.int32, device=DEV)
+    kc = torch.randn(Bc, hkv, cap, D, generator=g).to(dtype).to(DEV)
+    vc = torch.randn(Bc, hkv, cap, D, generator=g).to(dtype).to(DEV)
+    kv_len = torch.randint(150, 290, (B,), generator=g, dtype=torch.int32).to(DEV)
+    # --- RoPE + tree K/V write (scalar path, and the cos/sin table path for bf16)
+    qkv = torch.randn(B * n, (hq + 2 * hkv) * D, generator=g).to(dtype).to(DEV)
+    positions = (kv_len[:, None] + torch.arange(n, device=DEV)[None]).to(torch.int32)
+    inv_freq = (1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))).to(DEV)
+    tables = [None] + ([ops.rope_table(positions, inv_freq, 1.0, dtype)] if dtype == torch.bfloat16 else [])
+    for table in tables:
+        kg, vg = kc[rows].clone(), vc[rows].clone()
+        km, vm = kc.clone(), vc.clone()
+        q1, q2 = (torch.empty(B, n, hq, D, dtype=dtype, device=DEV) for _ in range(2))
+        common = dict(B=B, n_nodes=n, n_q_heads=hq, n_kv_heads=hkv, head_dim=D, kv_len=kv_len, cos_sin=table)
+        ops.rope_kv_write(qkv, positions, inv_freq, 1.0, k_cache=kg, v_cache=vg, q_out=q1, **common)
+        ops.rope_kv_write(qkv, positions, inv_freq, 1.0, k_cache=None, v_cache=None, q_out=q2,
+                          kv=ops.kv_layer(km, vm, rows=rows_d), **common)
+        torch.cuda.synchronize()
+        assert torch.equal(q1, q2)
+        assert torch.equal(km[rows], kg) and torch.equal(vm[rows], vg)
+        assert torch.equal(km[others], kc[others]) and torch.equal(vm[others], vc[others])
+    kc, vc = km, vm
+    # --- tree attention over the mapped rows (one and several splits for bf16)
+    tree = _random_tree(n, g)
+    anc = torch.from_numpy(_anc_bits(tree, n)).to(DEV)
+    q = torch.randn(B, n, hq, D, generator=g).to(dtype).to(DEV)
+    kg, vg = kc[rows].contiguous(), vc[rows].contiguous()
+    for splits in ([0, 3] if dtype == torch.bfloat16 else [0]):
+        ws_bytes = ops.attention_workspace_bytes(B, n, hq, hkv, D, num_splits=splits, max_kv_len=cap)
+        ws = torch.zeros(max(ws_bytes, 16) // 4 + 4, dtype=torch.int32, device=DEV)
+        o1 = ops.tree_attention(q, kg, vg, kv_len, anc, scale=D ** -0.5, workspace=ws, num_splits=splits,
+                                max_kv_len=cap)
+        o2 = ops.tree_attention(q, kc, vc, kv_len, anc, scale=D ** -0.5, workspace=ws, num_splits=splits,
+                                max_kv_len=cap, kv=ops.kv_layer(kc, vc, rows=rows_d))
+        torch.cuda.synchronize()
+        assert torch.equal(o1, o2), splits
+    if dtype != torch.bfloat16:
+        return
+    # --- acceptance + extract_path compaction of the mapped rows
+    V = 512
+    plan = rp.Plan(16, 3, [4, 2, 2], 0, "fixed")
+    # one peaked distribution for every depth: the draws usually match a child
+    h = (torch.randn(B, V, generator=g) * 8).to(dtype).float()
+    heads = [h, h, h]
+    root = torch.randint(0, V, (B,), generator=g)
+    trees = rp.build_dense_trees(root.tolist(), heads, plan)
+    nn = trees[0].node_count
+    trows, tnodes, slots = rp.internal_logit_layout(trees)
+    packed = torch.stack([heads[min(trees[r].depths[nd] - 1, 2)][r] for r, nd in zip(trows, tnodes)]).to(dtype)
+    tok = torch.tensor([t.tokens for t in trees], dtype=torch.int32).to(DEV)
+    par = torch.tensor([t.parents for t in trees], dtype=torch.int32).to(DEV)
+    U = torch.rand(B, 6, generator=g).to(DEV)
+    layers_g = [(kc[rows].clone(), vc[rows].clone()) for _ in range(2)]
+    layers_m = [(kc.clone(), vc.clone()) for _ in range(2)]
+    args = (ops, packed.to(DEV), torch.tensor(slots, dtype=torch.int32).to(DEV), tok, par,
+            torch.full((B,), nn, dtype=torch.int32, device=DEV), U)
+    o_g, rl_g = _run_accept(*args, do_sample=True, temperature=1.0, row_len=kv_len, k_layers=[k for k, _ in layers_g],
+                            v_layers=[v for _, v in layers_g])
+    o_m, rl_m = _run_accept(*args, do_sample=True, temperature=1.0, row_len=kv_len, k_layers=[k for k, _ in layers_m],
+                            v_layers=[v for _, v in layers_m], kv_rows=rows_d)
+    for key in o_g:
+        assert torch.equal(o_g[key], o_m[key]), key
+    assert torch.equal(rl_g, rl_m)
+    assert int(o_g["acc_len"].max()) >= 2  # some row moved slots
+    for (kg_, vg_), (km_, vm_) in zip(layers_g, layers_m):
+        assert torch.equal(km_[rows], kg_) and torch.equal(vm_[rows], vg_)
+        assert torch.equal(km_[others], kc[others]) and torch.equal(vm_[others], vc[others])
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

@@ -1,0 +1,85 @@
+"""Host logic of the round on CPU: the internal-row bound of adaptive trees
+and the compact row view that retires finished rows (no GPU, no kernels)."""
+from __future__ import annotations
+
+import itertools
+
+import torch
+
+from flashgrpo_b200.decoding.medusa_tree import TreePlan, dense_topology, internal_nodes, max_adaptive_internal
+
+
+def _bfs_internal(widths, budget):
+    """Independent count: BFS expansion of a dense tree up to `budget` nodes."""
+    n, frontier, internal = 1, [0], set()
+    for k in widths:
+        nxt = []
+        for p in frontier:
+            for _ in range(k):
+                if n >= budget:
+                    break
+                internal.add(p)
+                nxt.append(n)
+                n += 1
+        frontier = nxt
+        if not frontier or n >= budget:
+            break
+    return len(internal)
+
+
+def test_adaptive_internal_bound_covers_every_adapted_tree():
+    for base, budget in (([4, 3, 2], 16), ([4, 3, 2], 32), ([3, 2, 2], 10), ([5, 1], 8), ([2, 2, 2, 2], 64)):
+        plan = TreePlan(budget, len(base), base, budget, "concurrency_aware")
+        bound = max_adaptive_internal(plan)
+        assert bound >= len(internal_nodes(dense_topology(plan)[0]))
+        worst = 0
+        for depth in range(1, len(base) + 1):
+            for w in itertools.product(*[range(1, k + 1) for k in base[:depth]]):
+                worst = max(worst, _bfs_internal(w, budget))
+        assert bound == worst, (base, budget)
+    # the case that needed it: narrower and deeper than the base plan
+    plan = TreePlan(16, 3, [4, 3, 2], 16, "concurrency_aware")
+    assert len(internal_nodes(dense_topology(plan)[0])) == 5 and max_adaptive_internal(plan) == 10
+
+
+def test_round_view_gathers_and_scatters_only_its_rows(monkeypatch):
+    from types import SimpleNamespace
+
+    from flashgrpo_b200.engine import verify
+    from flashgrpo_b200.engine.verify import DecodeState, ModelSpec, RoundView
+
+    # the fg_kv_layer structs need device tensors: stand-ins that keep the row map
+    monkeypatch.setattr(verify.ops, "kv_layer", lambda k, v, rows=None: SimpleNamespace(
+        rows=None if rows is None else rows.data_ptr(), batch=0 if rows is None else k.shape[0]))
+
+    spec = ModelSpec(n_layers=2, hidden=8, n_q_heads=2, n_kv_heads=1, head_dim=16, inter=16, vocab=32, eps=1e-6,
+                     dtype=torch.float32)
+    st = DecodeState(spec, 6, 20, torch.device("cpu"), n_heads=2)
+    st.row_len.copy_(torch.tensor([10, 11, 12, 13, 14, 15], dtype=torch.int32))
+    st.pending.copy_(torch.tensor([-1, 5, -1, 7, -1, 9], dtype=torch.int32))
+    st.active.copy_(torch.tensor([1, 1, 0, 1, 1, 1], dtype=torch.int32))
+    st.seq_ids.copy_(torch.arange(100, 106, dtype=torch.int32))
+    st.hidden.copy_(torch.arange(48, dtype=torch.float32).view(6, 8))
+    before = {k: getattr(st, k).clone() for k in ("row_len", "pending", "active", "seq_ids")}
+    hidden0 = st.hidden.clone()
+    v = RoundView(st, 3, n_heads=2)
+    assert v.round_dev is st.round_dev and v.k is st.k
+    assert all(kv.rows == v.rows.data_ptr() and kv.batch == 6 for kv in v.kv_layers)
+    rows = [4, 1, 5]
+    v.rows.copy_(torch.tensor(rows, dtype=torch.int32))
+    v.gather()
+    assert v.row_len.tolist() == [14, 11, 15] and v.pending.tolist() == [-1, 5, 9]
+    assert v.seq_ids.tolist() == [104, 101, 105] and torch.equal(v.hidden, hidden0[rows])
+    # a round advances the view's rows; scatter writes back exactly those rows
+    v.row_len += 3
+    v.pending.copy_(torch.tensor([2, -1, 4], dtype=torch.int32))
+    v.active.copy_(torch.tensor([0, 1, 1], dtype=torch.int32))
+    v.hidden.mul_(-1)
+    v.scatter()
+    assert st.row_len.tolist() == [10, 14, 12, 13, 17, 18]
+    assert st.pending.tolist() == [-1, -1, -1, 7, 2, 4]
+    assert st.active.tolist() == [1, 1, 0, 1, 0, 1]
+    assert torch.equal(st.seq_ids, before["seq_ids"])
+    for r in range(6):
+        want = -hidden0[r] if r in rows else hidden0[r]
+        assert torch.equal(st.hidden[r], want), r
