@@ -13,6 +13,10 @@ internal-node lm_head, exact_target acceptance + extract_path compaction,
 replayed from a CUDA graph.  `value` = accepted tokens of all ranks / the
 slowest rank's device time (CUDA events) over `--steps` steps.  Inputs are
 larger than L2 (3.1 GB of weights and a 3.7 GB KV cache are read per step).
+`e2e` runs config 2's rollout through the public API: generate() on 8
+prompts of 256 uniform-random tokens (x8 samples) until every row holds 1024
+tokens, prompts copied from pinned host memory and tokens read back each
+round, timed on the host clock.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
@@ -47,7 +51,9 @@ def parse_args():
     ap.add_argument("--prefix", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (profiling only)")
     ap.add_argument("--e2e-calls", type=int, default=2)
-    ap.add_argument("--e2e-new", type=int, default=32)
+    ap.add_argument("--e2e-prompt", type=int, default=256,
+                    help="e2e prompt tokens (config 2: 256-token prompts whose KV grows to --e2e-len by decoding)")
+    ap.add_argument("--e2e-len", type=int, default=1024, help="e2e max_length: prompt + generated tokens per row")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-splits", type=int, default=0)
@@ -300,18 +306,21 @@ def run_ours(args, rank, world, local_rank):
         # ---- end-to-end through the public generate() API (prompts H2D, tokens D2H)
         e2e = None
         if not args.no_e2e and args.e2e_calls > 0:
-            e_ids = ids.pin_memory()
-            e_mask = mask.pin_memory()
+            # config 2's rollout: 256-token prompts decoded until the rows hold
+            # 1024 tokens, through the public generate() call
+            e_all, m_all = synthetic.random_prompts(prompts * world, args.e2e_prompt, spec.vocab, seed=101)
+            e_ids = e_all[my_prompts.start:my_prompts.stop].pin_memory()
+            e_mask = m_all[my_prompts.start:my_prompts.stop].pin_memory()
             # warm-up with the timed calls' arguments: the same decode state and
             # round configuration, so every timed round replays a captured graph
-            dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + args.e2e_new)
+            dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.e2e_len)
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
             t0 = time.perf_counter()
             tok, rounds_total, pre_s, ver_s = 0, 0, 0.0, 0.0
             for _ in range(args.e2e_calls):
-                res = dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.prefix + args.e2e_new)
+                res = dec.generate(e_ids, e_mask, repeated_generate_nums=8, max_length=args.e2e_len)
                 tok += res["total_acc_length"]
                 rounds_total += res["total_verify_rounds"]
                 pre_s += res["prefill_time_cost"]
@@ -321,10 +330,10 @@ def run_ours(args, rank, world, local_rank):
             tok = int(shard.reduce_scalar(tok, "sum", device))
             dcap = plan.active_heads + 2
             e2e = {"value": tok / e_s, "unit": UNIT,
-                   "h2d_bytes_per_step": int(ids.numel() * 8 + mask.numel() * 8),
+                   "h2d_bytes_per_step": int(e_ids.numel() * 8 + e_mask.numel() * 8),
                    "d2h_bytes_per_step": int(rounds_total / args.e2e_calls * rows * (3 + dcap) * 4),
-                   "step": f"one generate() call: {prompts} prompts x {args.prefix} tokens prefilled, x8 samples, "
-                           f"{args.e2e_new} new tokens per row",
+                   "step": f"one generate() call: {prompts} prompts x {args.e2e_prompt} tokens prefilled, x8 samples, "
+                           f"decoded to max_length {args.e2e_len}",
                    "calls": args.e2e_calls, "prefill_s_per_call": pre_s / args.e2e_calls,
                    "verify_rounds_s_per_call": ver_s / args.e2e_calls, "rounds_per_call": rounds_total / args.e2e_calls}
     result = {

@@ -181,21 +181,50 @@ class FlashMedusaDecoder:
         graphs, seen = self._graphs, self._seen
         pinned = None
         verify_time = 0.0
+        rcfg_key = dataclasses.astuple(rcfg)
+        setups: dict = {}
+        flat_bufs: dict = {}
+
+        def account(d):
+            """Host bookkeeping of a finished round (tokens, statistics); runs
+            while the next round executes on the device."""
+            rows_d, acc_d, toks_d, dcap_d, n_tree_d, pend_before = d
+            for i, r in enumerate(rows_d):
+                if pend_before[i] >= 0:
+                    stats["total_correction_tokens"] += 1
+                a = acc_d[i]
+                generated[r].extend(toks_d[i * dcap_d: i * dcap_d + a])
+                stats["total_acc_length"] += a
+                stats["total_decoded_token_num"] += 1
+                stats["total_accepted_medusa_tokens"] += max(a - 1, 0)
+                stats["total_proposed_medusa_tokens"] += max(n_tree_d - 1, 0)
+                accept_hist[a] = accept_hist.get(a, 0) + 1
+                for d_ in range(2, a + 1):
+                    accept_by_depth[d_] = accept_by_depth.get(d_, 0) + 1
+
+        deferred = None
         while any(active_host):
             # finished rows retire: the round runs on the active rows only
             # (select_cache_batch semantics), through a row map into the
             # cache when some rows have finished
             act_rows = [r for r in range(B) if active_host[r]]
             n_active = len(act_rows)
-            use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
-            plan = self._plan(n_active)
-            if not use_tree:
-                plan.topk_by_depth, plan.active_heads = [], 0
-            nh = min(n_heads, plan.active_heads)
-            plan.topk_by_depth = plan.topk_by_depth[:nh]
-            plan.active_heads = nh
-            dcap = nh + 2
-            adaptive = bool(cfg.adaptive_tree_enabled) and nh > 0
+            setup = setups.get(n_active)
+            if setup is None:
+                use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
+                plan = self._plan(n_active)
+                if not use_tree:
+                    plan.topk_by_depth, plan.active_heads = [], 0
+                nh = min(n_heads, plan.active_heads)
+                plan.topk_by_depth = plan.topk_by_depth[:nh]
+                plan.active_heads = nh
+                adaptive = bool(cfg.adaptive_tree_enabled) and nh > 0
+                params = self._params(n_active) if nh > 0 else ops.plan_params(
+                    tree_mode="explicit", active_batch_size=n_active, num_medusa_heads=0, cpeak_nodes=0,
+                    min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=1,
+                    fixed_tree_topk_by_depth=())
+                setup = setups[n_active] = (plan, nh, nh + 2, adaptive, params)
+            plan, nh, dcap, adaptive, params = setup
             if n_active < B:
                 rs = eng.view(st, n_active, n_heads)
                 rows_host = torch.tensor(act_rows, dtype=torch.int32).pin_memory()
@@ -203,11 +232,7 @@ class FlashMedusaDecoder:
             else:
                 rs = st
             rb = eng.buffers(n_active, plan, nh, dcap, adaptive=adaptive)
-            params = self._params(n_active) if nh > 0 else ops.plan_params(
-                tree_mode="explicit", active_batch_size=n_active, num_medusa_heads=0, cpeak_nodes=0,
-                min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=1, max_tree_depth=1, fixed_tree_topk_by_depth=())
-            key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive,
-                   dataclasses.astuple(rcfg))
+            key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive, rcfg_key)
             tv = time.time()
             if cfg.use_cuda_graphs and key in seen:
                 if key not in graphs:
@@ -217,11 +242,19 @@ class FlashMedusaDecoder:
                 eng.run_round(rs, rb, params, rcfg)
                 seen.add(key)
             out = rb.out
-            flat = torch.cat([out["acc_len"], out["finished"], rs.pending, rb.tree["plan"], out["acc_tokens"].view(-1)])
-            if pinned is None or pinned.numel() < flat.numel():
-                pinned = torch.empty(flat.numel(), dtype=torch.int32, pin_memory=True)
-            host = pinned[: flat.numel()]
-            host.copy_(flat, non_blocking=True)
+            parts = [out["acc_len"], out["finished"], rs.pending, rb.tree["plan"], out["acc_tokens"].view(-1)]
+            fb = flat_bufs.get((id(rb), id(rs)))
+            if fb is None:
+                fb = flat_bufs[(id(rb), id(rs))] = torch.empty(sum(t.numel() for t in parts), dtype=torch.int32,
+                                                              device=dev)
+            torch.cat(parts, out=fb)
+            if pinned is None or pinned.numel() < fb.numel():
+                pinned = torch.empty(fb.numel(), dtype=torch.int32, pin_memory=True)
+            host = pinned[: fb.numel()]
+            host.copy_(fb, non_blocking=True)
+            if deferred is not None:
+                account(deferred)
+                deferred = None
             torch.cuda.current_stream(dev).synchronize()
             verify_time += time.time() - tv
             vals = host.tolist()
@@ -240,22 +273,16 @@ class FlashMedusaDecoder:
             tree_plan_last = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
                               "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
                               "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa"}
+            # what the next round's shape depends on now; the rest after its launch
+            pend_before = [pending_host[r] for r in act_rows]
             for i, r in enumerate(act_rows):
-                if pending_host[r] >= 0:
-                    stats["total_correction_tokens"] += 1
-                a = acc_len[i]
-                generated[r].extend(toks[i * dcap: i * dcap + a])
-                stats["total_acc_length"] += a
-                stats["total_decoded_token_num"] += 1
-                stats["total_accepted_medusa_tokens"] += max(a - 1, 0)
-                stats["total_proposed_medusa_tokens"] += max(n_tree - 1, 0)
-                accept_hist[a] = accept_hist.get(a, 0) + 1
-                for d in range(2, a + 1):
-                    accept_by_depth[d] = accept_by_depth.get(d, 0) + 1
-                row_len_host[r] += a
+                row_len_host[r] += acc_len[i]
                 if fin[i]:
                     active_host[r] = False
                 pending_host[r] = pend[i]
+            deferred = (act_rows, acc_len, toks, dcap, n_tree, pend_before)
+        if deferred is not None:
+            account(deferred)
         total_time = time.time() - total_start
         rounds = max(stats["total_verify_rounds"], 1)
         decoded = max(stats["total_decoded_token_num"], 1)
