@@ -83,3 +83,25 @@ def test_round_view_gathers_and_scatters_only_its_rows(monkeypatch):
     for r in range(6):
         want = -hidden0[r] if r in rows else hidden0[r]
         assert torch.equal(st.hidden[r], want), r
+
+
+def test_hf_plugin_registration_cache_and_ancestor_bits():
+    from transformers import AttentionInterface
+
+    from flashgrpo_b200.models.hf_tree_attention import FGStaticCache, ancestor_bits
+
+    assert "fg_tree" in AttentionInterface._global_mapping
+    cache = FGStaticCache.empty(2, 3, 2, 16, 8, dtype=torch.float32, device="cpu")
+    cache.row_len.copy_(torch.tensor([0, 3, 5], dtype=torch.int32))
+    k, v = torch.randn(3, 2, 4, 8), torch.randn(3, 2, 4, 8)
+    cache.update(k, v, 1)
+    for b, start in enumerate((0, 3, 5)):
+        assert torch.equal(cache.k[1][b, :, start:start + 4], k[b]) and torch.equal(cache.v[1][b, :, start:start + 4],
+                                                                                   v[b])
+        assert torch.count_nonzero(cache.k[1][b, :, :start]) == 0
+    assert torch.count_nonzero(cache.k[0]) == 0 and cache.row_len.tolist() == [0, 3, 5]
+    # self + ancestors, as build_tree_attention_inputs; node 40 sits in word 1
+    parents = [-1, 0, 0, 1, 2] + [4] * 36
+    bits = ancestor_bits(parents)
+    assert bits[:5, 0].tolist() == [0b1, 0b11, 0b101, 0b1011, 0b10101]
+    assert bits[40].tolist()[0] == 0b10101 and bits[40].tolist()[1] == 1 << (40 - 32)
