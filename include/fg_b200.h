@@ -134,6 +134,41 @@ fg_status fg_lm_head_topk(const void *x, int32_t dtype, int64_t x_ld, int32_t M,
                           int32_t topk_row0, int32_t k, int32_t *out_idx, float *out_val, float *out_max,
                           float *out_lse, void *workspace, size_t workspace_bytes, void *stream);
 
+/* One MEDUSA head (heads.{i}.norm and heads.{i}.fc of a medusa_heads.pt
+ * state dict): device pointers to the LayerNorm weight and bias [H] and the
+ * fc weight [H, H] (nn.Linear layout, out x in, row-major) and bias [H]. */
+typedef struct fg_medusa_head {
+    const void *norm_w;
+    const void *norm_b;
+    const void *fc_w;
+    const void *fc_b;
+} fg_medusa_head;
+
+/* The whole MEDUSA proposal step of a round on the tensor cores.
+ * x is [(1 + n_heads) * B, H] bf16, row-major: rows [0, B) hold the root
+ * hidden states on entry; rows [(i + 1) B, (i + 2) B) receive head i's
+ * projected states h + silu(fc(layer_norm(h)))
+ * (MedusaPredictionHead.project_hidden, flashgrpo_b200/models/
+ * medusa_heads.py:240-244; the fc runs as a split-K tcgen05 GEMM whose
+ * fp32 partial sums are combined with the bias, SiLU and residual in one
+ * pass).  Then the tied lm_head over all (1 + n_heads) B rows
+ * (fg_lm_head_topk): the root rows' logits go to root_logits (row stride
+ * logits_ld; NULL skips them) and every head row keeps its k best tokens,
+ * maximum and (out_lse != NULL) logsumexp in out_* rows i * B + b.
+ * Replaces _medusa_logits_for_last_hidden
+ * (flashgrpo_b200/decoding/flash_medusa_decoder.py:906-1005) with the
+ * torch.topk of build_batch_trees (medusa_tree.py:767) and the confidence
+ * reductions (flash_medusa_decoder.py:1034-1040).  heads: host array of
+ * n_heads entries (n_heads >= 0; 0 computes the root logits only).
+ * (1 + n_heads) B <= 256, H a multiple of 64 and at most 8192, dtype
+ * FG_DTYPE_BF16 only, head weights 16-byte aligned (fc_b 8-byte);
+ * workspace: fg_medusa_propose_workspace_size bytes, 256-byte aligned. */
+size_t fg_medusa_propose_workspace_size(int32_t B, int32_t H, int32_t V, int32_t n_heads, int32_t k);
+fg_status fg_medusa_propose(void *x, int32_t dtype, int32_t B, int32_t H, const fg_medusa_head *heads,
+                            int32_t n_heads, float eps, const void *lm_head_w, int64_t w_ld, int32_t V,
+                            void *root_logits, int64_t logits_ld, int32_t k, int32_t *out_idx, float *out_val,
+                            float *out_max, float *out_lse, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------ tree build */
 typedef struct fg_plan_params {
     int32_t tree_mode;          /* 0 = "fixed", 1 = "concurrency_aware", 2 = explicit

@@ -11,3 +11,4 @@
 #include "fg_attention.cu"
 #include "fg_attention_noalloc.cu"
 #include "fg_lmhead_tc.cu"
+#include "fg_propose.cu"

@@ -77,6 +77,8 @@ struct Params {
     float* part_val;
     float* part_m;          // [M - topk_row0][2 nctas]
     float* part_s;
+    int32_t ksplit;         // partial-sum form: CTAs per column group, each over nk / ksplit k chunks
+    float* part;            // partial-sum form: [ksplit][M][V] fp32 sums, unrounded
 };
 
 struct Bars {
@@ -129,7 +131,11 @@ __device__ __forceinline__ void cta_range(int n_units, int c, int nctas, int& u0
     u1 = u0 + base + (c < extra ? 1 : 0);
 }
 
-template <int K>
+// kPart: the partial-sum form for narrow GEMMs (the MEDUSA head fc layers,
+// V = H): CTA c takes column group c / ksplit (at most 128 columns) and k
+// range (c % ksplit) of the nk chunks, and stores its fp32 sums unrounded
+// into part[c % ksplit]; a separate pass adds them up.  No logits, no top-k.
+template <int K, bool kPart = false>
 __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_constant__ CUtensorMap tmW256,
                                                                   const __grid_constant__ CUtensorMap tmW16,
                                                                   const __grid_constant__ CUtensorMap tmX, Params p) {
@@ -139,8 +145,16 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
     const int kStages = p.stages;
     volatile int* abort_flag = &bars->abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int u0, u1;
-    cta_range(p.n_units, blockIdx.x, gridDim.x, u0, u1);
+    int u0, u1, kc0 = 0, kc1 = p.nk;
+    const int ks = kPart ? (int)blockIdx.x % p.ksplit : 0;
+    if constexpr (kPart) {
+        cta_range(p.n_units, blockIdx.x / p.ksplit, gridDim.x / p.ksplit, u0, u1);
+        kc0 = ks * p.nk / p.ksplit;
+        kc1 = (ks + 1) * p.nk / p.ksplit;
+    } else {
+        cta_range(p.n_units, blockIdx.x, gridDim.x, u0, u1);
+    }
+    const int nkc = kc1 - kc0;
     const int v_begin = u0 * kUnit, v_end = min(u1 * kUnit, p.V);
     const int n_tiles = (u1 - u0 + (kN / kUnit) - 1) / (kN / kUnit);
     const int nmb = p.M > 128 ? 2 : 1;
@@ -173,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
             // W chunk `c` (tile c / nk, k chunk c % nk) into L2 ahead of its TMA load
             const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
             auto prefetch_w = [&](int c) {
-                const int t2 = c / p.nk, kc2 = c % p.nk;
+                const int t2 = c / nkc, kc2 = kc0 + c % nkc;
                 if (t2 >= n_tiles) return;
                 const int v2 = v_begin + t2 * kN;
                 const int w2 = min(kN, u1 * kUnit - v2);
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                 const int v0 = v_begin + t * kN;
                 const int w = min(kN, u1 * kUnit - v0);  // multiple of 16
                 const uint32_t bytes = (uint32_t)w * 128u + (uint32_t)p.xrows * 128u;
-                for (int kc = 0; kc < p.nk; ++kc, ++it) {
+                for (int kc = kc0; kc < kc1; ++kc, ++it) {
                     const int s = it % kStages;
                     if (it >= kStages && !(ok = bar_wait(&bars->empty[s], ((it / kStages) - 1) & 1, abort_flag)))
                         break;
@@ -221,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                 const uint32_t idesc = tc::idesc_bf16(w, false);
                 if (t > 0 && !(ok = bar_wait(&bars->acc_free, (t - 1) & 1, abort_flag))) break;
                 fence_after();
-                for (int kc = 0; kc < p.nk; ++kc, ++it) {
+                for (int kc = kc0; kc < kc1; ++kc, ++it) {
                     const int s = it % kStages;
                     if (!(ok = bar_wait(&bars->full[s], (it / kStages) & 1, abort_flag))) break;
                     fence_after();
@@ -235,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                         for (int kk = 0; kk < kKc / 16; ++kk) {
                             const uint64_t da = sdesc(x_addr + b * (128 * 128) + kk * 32, 16, 1024);
                             const uint64_t db = sdesc(w_addr + kk * 32, 16, 1024);
-                            umma(tmem + (uint32_t)(b * kN), da, db, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+                            umma(tmem + (uint32_t)(b * kN), da, db, idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
                         }
                     }
                     umma_commit(&bars->empty[s]);
@@ -290,6 +304,22 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                     float x[32];
                     tld32(lane_addr + (uint32_t)(b * kN + c), x);
                     const int vb = v0 + c;
+                    if constexpr (kPart) {
+                        if (valid) {
+                            float* dst = p.part + ((int64_t)ks * p.M + row) * p.V + vb;
+                            if (vb + 32 <= v_end) {  // V is a multiple of 64 here: 16-byte aligned
+#pragma unroll
+                                for (int qq = 0; qq < 8; ++qq)
+                                    *reinterpret_cast<float4*>(dst + 4 * qq) =
+                                        make_float4(x[4 * qq], x[4 * qq + 1], x[4 * qq + 2], x[4 * qq + 3]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 32; ++j)
+                                    if (vb + j < v_end) dst[j] = x[j];
+                            }
+                        }
+                        continue;
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(__float2bfloat16_rn(x[j]));
                     if (write) {
@@ -556,10 +586,13 @@ extern "C" size_t fg_lm_head_topk_workspace_size(int32_t M, int32_t V, int32_t t
     return rows * nlists * ((size_t)k * 8 + 8) + 256;
 }
 
-extern "C" fg_status fg_lm_head_topk(const void* x, int32_t dtype, int64_t x_ld, int32_t M, int32_t H, const void* w,
-                                     int64_t w_ld, int32_t V, int32_t n_logit_rows, void* logits, int64_t logits_ld,
-                                     int32_t topk_row0, int32_t k, int32_t* out_idx, float* out_val, float* out_max,
-                                     float* out_lse, void* workspace, size_t workspace_bytes, void* stream) {
+namespace fg {
+namespace lmh {
+
+static fg_status run(const void* x, int32_t dtype, int64_t x_ld, int32_t M, int32_t H, const void* w, int64_t w_ld,
+                     int32_t V, int32_t n_logit_rows, void* logits, int64_t logits_ld, int32_t topk_row0, int32_t k,
+                     int32_t* out_idx, float* out_val, float* out_max, float* out_lse, void* workspace,
+                     size_t workspace_bytes, void* stream) {
     if (M == 0) return FG_OK;
     if (dtype != FG_DTYPE_BF16) return FG_EUNSUPPORTED;
     if (!x || !w || M < 0 || V <= 0 || H <= 0 || n_logit_rows < 0 || n_logit_rows > M || topk_row0 < 0 ||
@@ -595,6 +628,8 @@ extern "C" fg_status fg_lm_head_topk(const void* x, int32_t dtype, int64_t x_ld,
     p.want_lse = out_lse != nullptr ? 1 : 0;
     p.part_idx = nullptr;
     p.part_val = p.part_m = p.part_s = nullptr;
+    p.ksplit = 1;
+    p.part = nullptr;
     if (has_topk) {
         const size_t need = fg_lm_head_topk_workspace_size(M, V, topk_row0, k);
         if (!workspace || workspace_bytes < need || ((uintptr_t)workspace % 16)) return FG_ECAPACITY;
@@ -637,4 +672,67 @@ extern "C" fg_status fg_lm_head_topk(const void* x, int32_t dtype, int64_t x_ld,
     lmh::lmhead_merge_kernel<<<M - topk_row0, 256, 0, st>>>(p.part_idx, p.part_val, p.part_m, p.part_s, 2 * nctas, k,
                                                            p.want_lse, out_idx, out_val, out_max, out_lse);
     return launch_status();
+}
+
+// Partial-sum form: column groups of at most 8 units (128 columns), and as
+// many k ranges per group as fill the SMs once (at most nk).
+static int part_groups(int32_t V) { return ((V + kUnit - 1) / kUnit + 7) / 8; }
+static int part_split(int32_t V, int32_t H) {
+    const int g = part_groups(V), nk = H / kKc;
+    const int s = sm_count() / g;
+    return s < 1 ? 1 : s > nk ? nk : s;
+}
+
+// part[ks][r][v] = the sum over k chunks [ks nk / S, (ks + 1) nk / S) of
+// x[r, k] w[v, k] (fp32, unrounded) for x [M, H], w [V, H] bf16 (row strides
+// H), S = part_split(V, H); part holds S * M * V floats, 16-byte aligned.
+static fg_status run_partials(const void* x, int32_t M, int32_t H, const void* w, int32_t V, float* part,
+                              void* stream) {
+    if (!x || !w || !part || M <= 0 || M > kMaxRows || H % kKc || V % 64 || ((uintptr_t)x % 16) ||
+        ((uintptr_t)w % 16) || ((uintptr_t)part % 16))
+        return FG_EINVAL;
+    Params p{};
+    p.M = M;
+    p.H = H;
+    p.V = V;
+    p.n_units = (V + kUnit - 1) / kUnit;
+    p.nk = H / kKc;
+    p.xrows = (M + 7) & ~7;
+    p.x_area = (p.xrows * 128 + 1023) & ~1023;
+    p.stage_bytes = p.x_area + kWBytes;
+    p.stages = (kSmemBytes - 1024 - kOffStage) / p.stage_bytes;
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    p.topk_row0 = M;
+    p.k = 1;
+    p.ksplit = part_split(V, H);
+    p.part = part;
+    CUtensorMap m256, m16, mx;
+    if (!make_map_2d(&m256, w, H, V, H, kN) || !make_map_2d(&m16, w, H, V, H, kUnit) ||
+        !make_map_2d(&mx, x, H, M, H, (uint32_t)p.xrows))
+        return FG_EINVAL;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto kern = lmhead_topk_kernel<1, true>;
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) {
+            set_cuda_error(e);
+            return FG_ECUDA;
+        }
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    kern<<<part_groups(V) * p.ksplit, kThreads, kSmemBytes, (cudaStream_t)stream>>>(m256, m16, mx, p);
+    return launch_status();
+}
+
+}  // namespace lmh
+}  // namespace fg
+
+extern "C" fg_status fg_lm_head_topk(const void* x, int32_t dtype, int64_t x_ld, int32_t M, int32_t H, const void* w,
+                                     int64_t w_ld, int32_t V, int32_t n_logit_rows, void* logits, int64_t logits_ld,
+                                     int32_t topk_row0, int32_t k, int32_t* out_idx, float* out_val, float* out_max,
+                                     float* out_lse, void* workspace, size_t workspace_bytes, void* stream) {
+    return lmh::run(x, dtype, x_ld, M, H, w, w_ld, V, n_logit_rows, logits, logits_ld, topk_row0, k, out_idx, out_val,
+                    out_max, out_lse, workspace, workspace_bytes, stream);
 }

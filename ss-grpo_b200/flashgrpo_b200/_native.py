@@ -41,6 +41,10 @@ class KvLayer(ctypes.Structure):
                 ("capacity", c_i32), ("rows", c_vp), ("batch", c_i32)]
 
 
+class MedusaHead(ctypes.Structure):
+    _fields_ = [("norm_w", c_vp), ("norm_b", c_vp), ("fc_w", c_vp), ("fc_b", c_vp)]
+
+
 class AcceptArgs(ctypes.Structure):
     _fields_ = [
         ("logits", c_vp), ("logits_dtype", c_i32), ("logits_row_stride", c_i64), ("vocab", c_i32),
@@ -70,6 +74,9 @@ SIGNATURES = {
     "fg_lm_head_topk_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32]),
     "fg_lm_head_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32,
                                 c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "fg_medusa_propose_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "fg_medusa_propose": (c_i32, [c_vp, c_i32, c_i32, c_i32, ctypes.POINTER(MedusaHead), c_i32, c_f32, c_vp, c_i64,
+                                  c_i32, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                               c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
@@ -119,21 +126,22 @@ def load():
     return _lib
 
 
-# Entry points that enqueue exactly one kernel; `launches` counts them so a
-# caller can report how many of this library's kernels a step runs.
+# Entry points that enqueue kernels; `launches` counts them so a caller can
+# report how many of this library's kernels a step runs (one per call unless
+# the caller passes the call's own count, e.g. the lm_head's top-k merge).
 LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree", "fg_rope_table",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
-             "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows"}
+             "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows", "fg_medusa_propose"}
 launches = 0
 
 
-def call(name: str, *args) -> None:
+def call(name: str, *args, n_launch: int | None = None) -> None:
     global launches
     status = getattr(load(), name)(*args)
     if status != FG_OK:
         raise NativeError(name, status)
     if name in LAUNCHING:
-        launches += 1
+        launches += 1 if n_launch is None else n_launch
 
 
 def read_device_error(clear: bool = True) -> int:

@@ -275,6 +275,8 @@ class RoundBuffers:
         self.adaptive = adaptive
         n_rows = B * max_adaptive_internal(plan, n_heads) if adaptive else len(idx)
         self.j_int = torch.arange(max(n_rows, 1), dtype=torch.int32, **f)
+        if adaptive:
+            self.int_idx = torch.zeros(max(n_rows, 1), dtype=torch.int32, **f)
         self.hid_int = torch.empty((max(n_rows, 1), H), dtype=spec.dtype, **f)
         self.tree_logits = torch.empty((max(n_rows, 1), V), dtype=spec.dtype, **f)
         self.dcap = dcap
@@ -381,22 +383,30 @@ class VerifyEngine:
             rb.attn_ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=self.device)
         return rb.attn_ws
 
+    def _propose_ws(self, B: int, nh: int, k: int) -> torch.Tensor:
+        need = ops.medusa_propose_workspace_bytes(B, self.spec.hidden, self.spec.vocab, nh, k)
+        ws = getattr(self, "_prop_ws", None)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.empty(max(need, 16) // 4 + 64, dtype=torch.int32, device=self.device)
+            self._prop_ws = ws
+        return ws
+
     def propose(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
         B, nh = st.B, rb.n_heads
         h = st.hidden
-        for i in range(nh):
-            hw = self.heads.heads[i]
-            ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
-            torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
-            ops.silu_residual(h, rb.fc, out=st.X[(i + 1) * B:(i + 2) * B])
         M = (nh + 1) * B
         if self._fused_lm_head(cfg, M):
-            # root rows keep their logits (the sampler reads them); head rows
-            # only produce their top-k (fg_row_topk semantics)
-            ws = self._lm_head_ws(M, B, rb.kmax)
-            ops.lm_head_topk(st.X[:M], self.w.lm_head, n_logit_rows=B, logits=rb.logits, topk_row0=B, k=rb.kmax,
-                             topk_out=rb.topk if nh > 0 else None, workspace=ws)
+            # heads and lm_head in one call: root rows keep their logits (the
+            # sampler reads them); head rows only produce their top-k
+            ops.medusa_propose(st.X[:M], B, self.heads.heads[:nh], self.w.lm_head, root_logits=rb.logits,
+                               k=rb.kmax, topk_out=rb.topk if nh > 0 else None,
+                               workspace=self._propose_ws(B, nh, rb.kmax))
         else:
+            for i in range(nh):
+                hw = self.heads.heads[i]
+                ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
+                torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
+                ops.silu_residual(h, rb.fc, out=st.X[(i + 1) * B:(i + 2) * B])
             torch.mm(st.X[:M], self.w.lm_head.t(), out=rb.logits[:M])
             if nh > 0:
                 ops.row_topk(rb.logits[B:M], rb.kmax, out=rb.topk)

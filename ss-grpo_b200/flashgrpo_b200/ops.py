@@ -115,7 +115,48 @@ def lm_head_topk(x: torch.Tensor, weight: torch.Tensor, *, n_logit_rows: int, lo
     N.call("fg_lm_head_topk", _ptr(x), N.FG_DTYPE_BF16, x.stride(0), M, H, _ptr(weight), weight.stride(0), V,
            int(n_logit_rows), _ptr(logits), logits.stride(0) if logits is not None else 0, int(topk_row0), int(k),
            _ptr(idx), _ptr(val), _ptr(mx), _ptr(lse), _ptr(workspace),
-           workspace.numel() * workspace.element_size() if workspace is not None else 0, _stream(x))
+           workspace.numel() * workspace.element_size() if workspace is not None else 0, _stream(x),
+           n_launch=1 + (int(topk_row0) < M))
+    return topk_out
+
+
+def medusa_propose_workspace_bytes(B: int, H: int, V: int, n_heads: int, k: int) -> int:
+    return int(N.load().fg_medusa_propose_workspace_size(int(B), int(H), int(V), int(n_heads), int(k)))
+
+
+def medusa_propose(x: torch.Tensor, B: int, heads: list[dict], lm_head: torch.Tensor, *, root_logits, k: int,
+                   topk_out, workspace: torch.Tensor, eps: float = 1e-5):
+    """fg_medusa_propose (bf16): x [(1 + len(heads)) B, H] holds the root
+    hidden states in rows [0, B); head i's projected states are written to
+    rows [(i + 1) B, (i + 2) B), then the lm_head writes the root rows'
+    logits to root_logits (or skips them when None) and the head rows' top-k
+    to topk_out (idx, val, max, lse-or-None; rows i * B + b).  heads: dicts
+    with norm_w, norm_b, fc_w, fc_b."""
+    n = len(heads)
+    _need(x, "x")
+    _need(lm_head, "lm_head", contiguous=False)
+    M, H = x.shape
+    if M != (1 + n) * B:
+        raise ValueError("x must have (1 + n_heads) * B rows")
+    if x.dtype != torch.bfloat16 or lm_head.dtype != torch.bfloat16 or lm_head.stride(1) != 1:
+        raise ValueError("medusa_propose is the bf16 path with row-contiguous weights")
+    arr = (N.MedusaHead * max(n, 1))()
+    for i, hw in enumerate(heads):
+        for f in ("norm_w", "norm_b", "fc_w", "fc_b"):
+            _need(hw[f], f)
+            if hw[f].dtype != torch.bfloat16:
+                raise ValueError(f"head {i} {f} must be bf16")
+        if hw["fc_w"].shape != (H, H) or hw["fc_b"].shape != (H,):
+            raise ValueError(f"head {i}: fc must be [H, H] with bias [H]")
+        arr[i] = N.MedusaHead(_ptr(hw["norm_w"]), _ptr(hw["norm_b"]), _ptr(hw["fc_w"]), _ptr(hw["fc_b"]))
+    idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
+    # LayerNorm and finishing pass per 8 heads, one fc GEMM per head, lm_head (+ top-k merge)
+    n_launch = (2 * ((n + 7) // 8) + n if n > 0 else 0) + 1 + (n > 0)
+    N.call("fg_medusa_propose", _ptr(x), N.FG_DTYPE_BF16, int(B), H, arr, n, float(eps), _ptr(lm_head),
+           lm_head.stride(0), lm_head.shape[0], _ptr(root_logits),
+           root_logits.stride(0) if root_logits is not None else 0, int(k), _ptr(idx), _ptr(val), _ptr(mx),
+           _ptr(lse), _ptr(workspace), workspace.numel() * workspace.element_size() if workspace is not None else 0,
+           _stream(x), n_launch=n_launch)
     return topk_out
 
 

@@ -55,6 +55,21 @@ def test_host_only_entry_points():
     assert lmh(_native.FG_DTYPE_BF16, 64, 100, 4) == _native.FG_ECAPACITY
     assert lib.fg_lm_head_topk_workspace_size(192, 151936, 64, 4) > 0
     assert lib.fg_lm_head_topk_workspace_size(192, 151936, 192, 4) == 0
+    # MEDUSA proposal: dtype, row and width limits, head pointers, workspace
+    heads = (_native.MedusaHead * 2)(*[_native.MedusaHead(256, 256, 256, 256)] * 2)
+    prop = lambda dtype, B, H, hs, n, ws_bytes: lib.fg_medusa_propose(
+        p, dtype, B, H, hs, n, 1e-5, p, H, 1000, p, 1000, 4, p, p, p, None, p, ws_bytes, None)
+    big = 1 << 30
+    assert prop(_native.FG_DTYPE_F32, 64, 128, heads, 2, big) == _native.FG_EUNSUPPORTED
+    assert prop(_native.FG_DTYPE_BF16, 86, 128, heads, 2, big) == _native.FG_ECAPACITY    # 3 x 86 rows > 256
+    assert prop(_native.FG_DTYPE_BF16, 64, 100, heads, 2, big) == _native.FG_ECAPACITY    # H not a multiple of 64
+    assert prop(_native.FG_DTYPE_BF16, 64, 128, None, 2, big) == _native.FG_EINVAL
+    bad = (_native.MedusaHead * 2)(_native.MedusaHead(256, 256, 256, 256), _native.MedusaHead(256, None, 256, 256))
+    assert prop(_native.FG_DTYPE_BF16, 64, 128, bad, 2, big) == _native.FG_EINVAL
+    assert prop(_native.FG_DTYPE_BF16, 64, 128, heads, 2, 1024) == _native.FG_ECAPACITY   # workspace too small
+    need = lib.fg_medusa_propose_workspace_size(64, 1536, 151936, 2, 4)
+    assert need >= 2 * 2 * 64 * 1536 * 2 + lib.fg_lm_head_topk_workspace_size(192, 151936, 64, 4)
+    assert lib.fg_medusa_propose_workspace_size(64, 1536, 151936, 0, 4) == 256
 
 
 def test_plan_params_tables():
@@ -75,8 +90,8 @@ def test_plan_params_tables():
 
 
 def test_ctypes_structures_match_the_header(tmp_path):
-    """The ctypes mirrors of fg_plan_params, fg_kv_layer and fg_accept_args
-    have the C structs' size and field offsets (compiled with gcc from the
+    """The ctypes mirrors of fg_plan_params, fg_kv_layer, fg_accept_args and
+    fg_medusa_head have the C structs' size and field offsets (compiled with gcc from the
     header)."""
     import shutil
     import subprocess
@@ -86,7 +101,8 @@ def test_ctypes_structures_match_the_header(tmp_path):
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no C compiler")
-    structs = {"fg_plan_params": N.PlanParams, "fg_kv_layer": N.KvLayer, "fg_accept_args": N.AcceptArgs}
+    structs = {"fg_plan_params": N.PlanParams, "fg_kv_layer": N.KvLayer, "fg_accept_args": N.AcceptArgs,
+               "fg_medusa_head": N.MedusaHead}
     lines = []
     for cname, py in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')

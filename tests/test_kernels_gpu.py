@@ -168,6 +168,60 @@ def test_lm_head_topk_matches_gemm_then_row_topk(ops, M, H, V, n_write, row0, k,
                 assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("B,H,V,n_heads,k,lse", [
+    (64, 1536, 151936, 2, 4, False),   # config 2 proposal: 64 rows, 2 active heads
+    (8, 3584, 152064, 3, 8, True),     # config 3 width (fc GEMMs wider than the SM count in 16-column units)
+    (5, 256, 5000, 1, 2, True),        # ragged row count
+    (16, 512, 3000, 0, 4, False),      # no heads: root logits only
+    (20, 256, 2064, 9, 4, False),      # more heads than one LayerNorm launch serves, 200 rows
+])
+def test_medusa_propose_matches_torch_heads_then_lm_head(ops, B, H, V, n_heads, k, lse):
+    """fg_medusa_propose: the heads' projected rows against
+    MedusaPredictionHead.project_hidden evaluated by torch in bf16, and the
+    lm_head part bit-identical to fg_lm_head_topk on the rows it produced."""
+    F = torch.nn.functional
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(B * 7 + H + n_heads)
+    M = (1 + n_heads) * B
+    x = torch.full((M, H), float("nan"), dtype=bf, device=DEV)
+    x[:B] = (torch.randn(B, H, generator=g) * 0.5).to(bf).to(DEV)
+    mk = lambda *shape, s=1.0, o=0.0: (torch.randn(*shape, generator=g) * s + o).to(bf).to(DEV)
+    heads = [dict(norm_w=mk(H, s=0.1, o=1.0), norm_b=mk(H, s=0.1), fc_w=mk(H, H, s=H ** -0.5), fc_b=mk(H, s=0.1))
+             for _ in range(n_heads)]
+    w = mk(V, H, s=0.05)
+    n_top = n_heads * B
+    out = lambda: (torch.empty((n_top, k), dtype=torch.int32, device=DEV),
+                   torch.empty((n_top, k), dtype=torch.float32, device=DEV),
+                   torch.empty(n_top, dtype=torch.float32, device=DEV),
+                   torch.empty(n_top, dtype=torch.float32, device=DEV) if lse else None) if n_heads else None
+    root = torch.full((B, V), float("nan"), dtype=bf, device=DEV)
+    ws = torch.empty(ops.medusa_propose_workspace_bytes(B, H, V, n_heads, k) // 4 + 64, dtype=torch.int32,
+                     device=DEV)
+    got = out()
+    ops.medusa_propose(x, B, heads, w, root_logits=root, k=k, topk_out=got, workspace=ws)
+    torch.cuda.synchronize()
+    h = x[:B]
+    for i, hw in enumerate(heads):
+        ref = h + F.silu(F.linear(F.layer_norm(h, (H,), hw["norm_w"], hw["norm_b"], 1e-5), hw["fc_w"], hw["fc_b"]))
+        d = x[(i + 1) * B:(i + 2) * B].float() - ref.float()
+        # bf16 on both sides, different GEMM summation orders: 1e-2 relative
+        # in norm, no element further than 2e-2 of the largest magnitude
+        assert (d.norm() / ref.float().norm()).item() <= 1e-2, i
+        assert d.abs().max().item() <= 2e-2 * ref.float().abs().max().item(), i
+    want_root = torch.full((B, V), float("nan"), dtype=bf, device=DEV)
+    want = out()
+    lws = torch.empty(max(ops.lm_head_topk_workspace_bytes(M, V, B, k), 16) // 4 + 4, dtype=torch.int32, device=DEV)
+    ops.lm_head_topk(x, w, n_logit_rows=B, logits=want_root, topk_row0=B, k=k, topk_out=want, workspace=lws)
+    torch.cuda.synchronize()
+    assert torch.equal(root, want_root)
+    if n_heads:
+        for a, b in zip(got, want):
+            if a is not None:
+                assert torch.equal(a, b)
+    err = (root.float() - x[:B].float() @ w.float().t()).abs().max().item()
+    assert err <= 1e-2 * root.float().abs().max().item() + 1e-3
+
+
 # -------------------------------------------------------------- tree build
 def _check_tree(ops, *, tree_mode, B, cpeak, mx, depth, fixed, n_heads, V=300, adaptive=False, amin=(1, 1, 1),
                 metric="top1_prob", seed=0, dtype=torch.bfloat16):
