@@ -169,6 +169,51 @@ fg_status fg_medusa_propose(void *x, int32_t dtype, int32_t B, int32_t H, const 
                             void *root_logits, int64_t logits_ld, int32_t k, int32_t *out_idx, float *out_val,
                             float *out_max, float *out_lse, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The ChainDraftCell of a Chain-MEDUSA checkpoint (chain_cell.* entries):
+ * device pointers, bf16.  norms [H]; state_proj / token_proj [bottleneck, H]
+ * and out_proj [H, bottleneck] in nn.Linear layout (out x in, row-major);
+ * out_b [H]; gate: one element. */
+typedef struct fg_chain_cell {
+    const void *state_norm_w;
+    const void *state_norm_b;
+    const void *token_norm_w;
+    const void *token_norm_b;
+    const void *state_proj_w;
+    const void *token_proj_w;
+    const void *out_proj_w;
+    const void *out_proj_b;
+    const void *gate;
+    int32_t bottleneck;
+} fg_chain_cell;
+
+/* One level of a chain proposal on the tensor cores.  Rows are grouped by
+ * sequence: row r = b * n_child + j (b < n_seq, j < n_child) extends parent
+ * state s = state[b * n_parent + j / fanout] with token
+ * t = tokens[b * tok_ld + j] (t in [0, V): the embedding table has the
+ * lm_head's V rows; others record FG_EINVAL in the device error word and
+ * read row 0):
+ *   state_out[r] = s + sigmoid(gate) * out_proj(silu(state_proj(LN_s(s)) + token_proj(LN_t(embed[t]))))
+ * (ChainDraftCell.forward, flashgrpo_b200/models/medusa_heads.py:154-160,
+ * rounded to bf16 after every op as the reference's bf16 module does; the
+ * three projections run as split-K tcgen05 GEMMs), then, when k > 0, what
+ * fg_lm_head_topk returns for every state_out row (k best, maximum,
+ * logsumexp when out_lse != NULL) -- the per-parent candidates of the next
+ * level.  Replaces one iteration of the chain loop of
+ * _build_chain_batch_trees (flashgrpo_b200/decoding/flash_medusa_decoder.py:
+ * 1141-1261).  state [n_seq * n_parent, H], state_out [n_seq * n_child, H]
+ * and embed rows (stride embed_ld) are bf16 with contiguous rows; state_out
+ * must not overlap state.  n_child <= n_parent * fanout <= tok_ld * fanout;
+ * any number of rows (processed 256 at a time); H and bottleneck multiples
+ * of 64, H at most 8192; dtype FG_DTYPE_BF16 only; workspace:
+ * fg_chain_step_workspace_size bytes for M = n_seq * n_child rows, 256-byte
+ * aligned. */
+size_t fg_chain_step_workspace_size(int32_t M, int32_t H, int32_t bottleneck, int32_t V, int32_t k);
+fg_status fg_chain_step(const void *state, const int32_t *tokens, int32_t tok_ld, int32_t n_seq, int32_t n_parent,
+                        int32_t fanout, int32_t n_child, const void *embed, int64_t embed_ld, int32_t H,
+                        int32_t dtype, const fg_chain_cell *cell, float eps, void *state_out, const void *lm_head_w,
+                        int64_t w_ld, int32_t V, int32_t k, int32_t *out_idx, float *out_val, float *out_max,
+                        float *out_lse, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------ tree build */
 typedef struct fg_plan_params {
     int32_t tree_mode;          /* 0 = "fixed", 1 = "concurrency_aware", 2 = explicit

@@ -12,3 +12,4 @@
 #include "fg_attention_noalloc.cu"
 #include "fg_lmhead_tc.cu"
 #include "fg_propose.cu"
+#include "fg_chain.cu"

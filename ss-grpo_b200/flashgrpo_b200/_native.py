@@ -45,6 +45,12 @@ class MedusaHead(ctypes.Structure):
     _fields_ = [("norm_w", c_vp), ("norm_b", c_vp), ("fc_w", c_vp), ("fc_b", c_vp)]
 
 
+class ChainCell(ctypes.Structure):
+    _fields_ = [("state_norm_w", c_vp), ("state_norm_b", c_vp), ("token_norm_w", c_vp), ("token_norm_b", c_vp),
+                ("state_proj_w", c_vp), ("token_proj_w", c_vp), ("out_proj_w", c_vp), ("out_proj_b", c_vp),
+                ("gate", c_vp), ("bottleneck", c_i32)]
+
+
 class AcceptArgs(ctypes.Structure):
     _fields_ = [
         ("logits", c_vp), ("logits_dtype", c_i32), ("logits_row_stride", c_i64), ("vocab", c_i32),
@@ -77,6 +83,10 @@ SIGNATURES = {
     "fg_medusa_propose_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32]),
     "fg_medusa_propose": (c_i32, [c_vp, c_i32, c_i32, c_i32, ctypes.POINTER(MedusaHead), c_i32, c_f32, c_vp, c_i64,
                                   c_i32, c_vp, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "fg_chain_step_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "fg_chain_step": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32,
+                              ctypes.POINTER(ChainCell), c_f32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                               c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
@@ -131,7 +141,8 @@ def load():
 # the caller passes the call's own count, e.g. the lm_head's top-k merge).
 LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree", "fg_rope_table",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
-             "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows", "fg_medusa_propose"}
+             "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows", "fg_medusa_propose",
+             "fg_chain_step"}
 launches = 0
 
 

@@ -9,9 +9,10 @@ CUDA graph and reads back the accepted tokens.
 
 Sampling: draws come from Philox uniforms indexed by (sequence id, round,
 draw) and the fg-icdf-v1 inverse CDF, so a seeded run is reproducible bit for
-bit.  ``top_p < 1`` (nucleus), ``top_k`` sampling, the sparse tree layouts,
-chain proposals and the Reflex/HRDCR machinery are not on this path and are
-rejected explicitly.
+bit.  Nucleus sampling (``top_p < 1``), adaptive trees and chain proposals
+are supported; ``top_k`` sampling, the sparse tree layouts, adaptive widths
+with chain proposals and the Reflex/HRDCR machinery are not on this path and
+are rejected explicitly.
 """
 from __future__ import annotations
 

@@ -3,9 +3,10 @@
 A round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1649-2938 of the
 reference, Reflex off) runs as one stream of work with no host sync:
 
-  propose   X = [h ; head_1(h) ; ... ; head_k(h)] -> X @ lm_head^T   (cuBLAS)
-            root token  = fg_sample_rows(rows of h, forced = pending correction)
-            candidates  = fg_row_topk(head rows)                      (K1 top-k)
+  propose   fg_medusa_propose: X = [h ; head_1(h) ; ... ; head_k(h)], the
+            tied lm_head over X with the head rows' top-k fused       (K1)
+            root token  = fg_sample_rows(root logits, forced = pending correction)
+            chain proposals: one fg_chain_step per tree level (cell + top-k)
   tree      fg_build_tree: plan, dense tree, ancestor bits, slots     (K2)
   verify    per layer: RMSNorm, QKV GEMM (+bias), fg_rope_kv_write (RoPE +
             tree K/V written at each row's cache tail), fg_tree_attention
@@ -444,15 +445,54 @@ class VerifyEngine:
             ops.row_topk(logits, k, out=(idx, val, mx, None))
         return idx
 
+    def _fused_chain(self, cfg: RoundConfig) -> bool:
+        c, sp = self.heads.chain, self.spec
+        return (cfg.lm_head == "fused" and sp.dtype == torch.bfloat16 and sp.hidden % 64 == 0
+                and sp.hidden <= 8192 and c["state_proj.weight"].shape[0] % 64 == 0
+                and self.w.lm_head.stride(1) == 1 and self.w.embed.stride(1) == 1)
+
+    def _chain_ws(self, M: int, k: int) -> torch.Tensor:
+        sp = self.spec
+        need = ops.chain_step_workspace_bytes(M, sp.hidden, self.heads.chain["state_proj.weight"].shape[0],
+                                              sp.vocab, k)
+        ws = getattr(self, "_chain_ws_buf", None)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.empty(max(need, 16) // 4 + 64, dtype=torch.int32, device=self.device)
+            self._chain_ws_buf = ws
+        return ws
+
+    def _chain_topk_bufs(self, M: int, k: int):
+        return (torch.empty((M, k), dtype=torch.int32, device=self.device),
+                torch.empty((M, k), dtype=torch.float32, device=self.device),
+                torch.empty(M, dtype=torch.float32, device=self.device), None)
+
     def propose_chain(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
         """_build_chain_batch_trees (flash_medusa_decoder.py:1141-1261), Reflex
         off, fixed widths: the root token as in propose(), then per depth the
         lm_head top-k of every parent state and the chain cell on the chosen
         tokens.  The dense topology is the one K2 builds; the tokens of each
-        level are written over K2's after build_tree."""
+        level are written over K2's after build_tree.  bf16: each level is one
+        fg_chain_step (cell + lm_head top-k of the new states), and a
+        head-bootstrapped state comes from fg_medusa_propose with the root
+        logits."""
         B = st.B
         h = st.hidden
-        if self._fused_lm_head(cfg, B):
+        H = h.shape[-1]
+        fused = self._fused_chain(cfg) and len(rb.widths) > 0
+        idx = None
+        if fused and cfg.chain_bootstrap and len(self.heads) > 0 and 2 * B <= 256:
+            # root logits, head-0 state and its top-k in one call
+            if st.X.shape[0] >= 2 * B:
+                x2 = st.X[:2 * B]
+            else:
+                x2 = torch.empty((2 * B, H), dtype=h.dtype, device=self.device)
+                x2[:B].copy_(h)
+            k0 = rb.widths[0]
+            top = self._chain_topk_bufs(B, k0)
+            ops.medusa_propose(x2, B, self.heads.heads[:1], self.w.lm_head, root_logits=rb.logits, k=k0,
+                               topk_out=top, workspace=self._propose_ws(B, 1, k0))
+            state, idx = x2[B:], top[0]
+        elif self._fused_lm_head(cfg, B):
             ops.lm_head_topk(st.X[:B], self.w.lm_head, n_logit_rows=B, logits=rb.logits, topk_row0=B, k=1,
                              topk_out=None, workspace=self._lm_head_ws(B, B, 1))
         else:
@@ -460,28 +500,50 @@ class VerifyEngine:
         ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
                         top_p=cfg.top_p, forced=st.pending, out=rb.root)
-        if cfg.chain_bootstrap and len(self.heads) > 0:
-            hw = self.heads.heads[0]
-            ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
-            torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
-            state = ops.silu_residual(h, rb.fc)
-        else:
-            state = self._chain_cell(h, self.w.embed[rb.root.long()])
-        H = state.shape[-1]
-        states, n_par = state.view(B, 1, H), 1
+        if idx is None:  # the state was not bootstrapped together with the root logits
+            if cfg.chain_bootstrap and len(self.heads) > 0:
+                hw = self.heads.heads[0]
+                ops.layernorm(h, hw["norm_w"], hw["norm_b"], 1e-5, out=rb.ln)
+                torch.addmm(hw["fc_b"], rb.ln, hw["fc_w"].t(), out=rb.fc)
+                state = ops.silu_residual(h, rb.fc)
+            elif fused:
+                # the cell on the root token, with the depth-0 top-k
+                k0 = rb.widths[0]
+                state = torch.empty((B, H), dtype=h.dtype, device=self.device)
+                top = self._chain_topk_bufs(B, k0)
+                ops.chain_step(h, rb.root.view(B, 1), n_parent=1, fanout=1, n_child=1, embed=self.w.embed,
+                               cell=self.heads.chain, lm_head=self.w.lm_head, k=k0, state_out=state, topk_out=top,
+                               workspace=self._chain_ws(B, k0))
+                idx = top[0]
+            else:
+                state = self._chain_cell(h, self.w.embed[rb.root.long()])
+        states, n_par = state.reshape(B, 1, H), 1
         rb.chain_tokens = []
         for d, k in enumerate(rb.widths):
             n_ch = rb.level_count[d + 1] if d + 1 < len(rb.level_count) else 0
             if n_ch == 0:
                 break
-            idx = self._rows_topk(states.reshape(B * n_par, H), k, cfg)
+            if idx is None:
+                idx = self._rows_topk(states.reshape(B * n_par, H), k, cfg)
             tok = idx.view(B, n_par * k)[:, :n_ch]
             rb.chain_tokens.append((rb.level_off[d + 1], n_ch, tok))
             if d + 2 < len(rb.level_count) and rb.level_count[d + 2] > 0:
-                par = torch.arange(n_ch, device=self.device) // k
-                emb = self.w.embed[tok.reshape(-1).long()]
-                states = self._chain_cell(states[:, par].reshape(-1, H), emb).view(B, n_ch, H)
+                if fused and d + 1 < len(rb.widths):
+                    k1 = rb.widths[d + 1]
+                    new = torch.empty((B * n_ch, H), dtype=h.dtype, device=self.device)
+                    top = self._chain_topk_bufs(B * n_ch, k1)
+                    ops.chain_step(states.reshape(B * n_par, H), idx.view(B, n_par * k), n_parent=n_par, fanout=k,
+                                   n_child=n_ch, embed=self.w.embed, cell=self.heads.chain, lm_head=self.w.lm_head,
+                                   k=k1, state_out=new, topk_out=top, workspace=self._chain_ws(B * n_ch, k1))
+                    states, idx = new.view(B, n_ch, H), top[0]
+                else:
+                    par = torch.arange(n_ch, device=self.device) // k
+                    emb = self.w.embed[tok.reshape(-1).long()]
+                    states = self._chain_cell(states[:, par].reshape(-1, H), emb).view(B, n_ch, H)
+                    idx = None
                 n_par = n_ch
+            else:
+                idx = None
 
     def build_tree(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams):
         nh = rb.n_heads

@@ -160,6 +160,50 @@ def medusa_propose(x: torch.Tensor, B: int, heads: list[dict], lm_head: torch.Te
     return topk_out
 
 
+def chain_step_workspace_bytes(M: int, H: int, bottleneck: int, V: int, k: int) -> int:
+    return int(N.load().fg_chain_step_workspace_size(int(M), int(H), int(bottleneck), int(V), int(k)))
+
+
+def chain_step(state: torch.Tensor, tokens: torch.Tensor, *, n_parent: int, fanout: int, n_child: int,
+               embed: torch.Tensor, cell: dict, lm_head: torch.Tensor | None, k: int, state_out: torch.Tensor,
+               topk_out, workspace: torch.Tensor, eps: float = 1e-5):
+    """fg_chain_step (bf16): state [n_seq * n_parent, H]; tokens [n_seq, >=
+    n_child] int32 (row b's children's tokens, any row stride); cell: the
+    chain_cell.* tensors by their state-dict names.  Writes the n_seq *
+    n_child new states to state_out and, when k > 0, their lm_head top-k to
+    topk_out (idx, val, max, lse-or-None)."""
+    _need(state, "state")
+    _need(state_out, "state_out")
+    _need(embed, "embed", contiguous=False)
+    _need(tokens, "tokens", dtype=torch.int32, contiguous=False)
+    if tokens.dim() != 2 or tokens.stride(1) != 1 or embed.stride(1) != 1:
+        raise ValueError("tokens and embed need contiguous rows")
+    for t in (state, state_out, embed):
+        if t.dtype != torch.bfloat16:
+            raise ValueError("chain_step is the bf16 path")
+    H = state.shape[1]
+    n_seq = tokens.shape[0]
+    names = ("state_norm.weight", "state_norm.bias", "token_norm.weight", "token_norm.bias", "state_proj.weight",
+             "token_proj.weight", "out_proj.weight", "out_proj.bias", "gate")
+    for nm in names:
+        _need(cell[nm], nm)
+        if cell[nm].dtype != torch.bfloat16:
+            raise ValueError(f"chain cell {nm} must be bf16")
+    bn = cell["state_proj.weight"].shape[0]
+    c = N.ChainCell(*[_ptr(cell[nm]) for nm in names], int(bn))
+    idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
+    M = n_seq * n_child
+    # per pass of 256 rows: norms, 3 projections, mix, finish (+ lm_head and its top-k merge)
+    n_launch = (M + 255) // 256 * (6 + (2 if k > 0 else 0))
+    N.call("fg_chain_step", _ptr(state), _ptr(tokens), tokens.stride(0), n_seq, int(n_parent), int(fanout),
+           int(n_child), _ptr(embed), embed.stride(0), H, N.FG_DTYPE_BF16, ctypes.byref(c), float(eps),
+           _ptr(state_out), _ptr(lm_head), lm_head.stride(0) if lm_head is not None else 0,
+           lm_head.shape[0] if lm_head is not None else embed.shape[0], int(k), _ptr(idx), _ptr(val), _ptr(mx),
+           _ptr(lse), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(state),
+           n_launch=n_launch)
+    return state_out
+
+
 # ---------------------------------------------------------------- planning
 def plan_params(*, tree_mode: str, active_batch_size: int, num_medusa_heads: int, cpeak_nodes: int,
                 min_tree_nodes_per_seq: int, max_tree_nodes_per_seq: int, max_tree_depth: int,

@@ -70,6 +70,21 @@ def test_host_only_entry_points():
     need = lib.fg_medusa_propose_workspace_size(64, 1536, 151936, 2, 4)
     assert need >= 2 * 2 * 64 * 1536 * 2 + lib.fg_lm_head_topk_workspace_size(192, 151936, 64, 4)
     assert lib.fg_medusa_propose_workspace_size(64, 1536, 151936, 0, 4) == 256
+    # chain step: dtype, widths, row grouping, overlap and workspace are checked before any CUDA call
+    cell = _native.ChainCell(*([256] * 9), 192)
+    step = lambda dtype, H, c, n_par, fan, n_ch, out, ws_bytes: lib.fg_chain_step(
+        p, p, n_ch, 4, n_par, fan, n_ch, p, 2048, H, dtype, ctypes.byref(c), 1e-5, out, p, H, 1000, 4, p, p, p, None,
+        p, ws_bytes, None)
+    far = ctypes.c_void_p(1 << 40)
+    assert step(_native.FG_DTYPE_F32, 1536, cell, 1, 4, 4, far, big) == _native.FG_EUNSUPPORTED
+    assert step(_native.FG_DTYPE_BF16, 1536, cell, 1, 4, 5, far, big) == _native.FG_EINVAL      # 5 children > 1 x 4
+    assert step(_native.FG_DTYPE_BF16, 1500, cell, 1, 4, 4, far, big) == _native.FG_ECAPACITY   # H % 64
+    odd = _native.ChainCell(*([256] * 9), 100)
+    assert step(_native.FG_DTYPE_BF16, 1536, odd, 1, 4, 4, far, big) == _native.FG_ECAPACITY    # bottleneck % 64
+    assert step(_native.FG_DTYPE_BF16, 1536, cell, 1, 4, 4, p, big) == _native.FG_EINVAL        # state_out overlaps state
+    assert step(_native.FG_DTYPE_BF16, 1536, cell, 1, 4, 4, far, 1024) == _native.FG_ECAPACITY  # workspace too small
+    assert lib.fg_chain_step_workspace_size(512, 1536, 192, 151936, 4) == \
+        lib.fg_chain_step_workspace_size(256, 1536, 192, 151936, 4)                           # 256-row passes
 
 
 def test_plan_params_tables():
@@ -90,8 +105,8 @@ def test_plan_params_tables():
 
 
 def test_ctypes_structures_match_the_header(tmp_path):
-    """The ctypes mirrors of fg_plan_params, fg_kv_layer, fg_accept_args and
-    fg_medusa_head have the C structs' size and field offsets (compiled with gcc from the
+    """The ctypes mirrors of fg_plan_params, fg_kv_layer, fg_accept_args,
+    fg_medusa_head and fg_chain_cell have the C structs' size and field offsets (compiled with gcc from the
     header)."""
     import shutil
     import subprocess
@@ -102,7 +117,7 @@ def test_ctypes_structures_match_the_header(tmp_path):
     if cc is None:
         pytest.skip("no C compiler")
     structs = {"fg_plan_params": N.PlanParams, "fg_kv_layer": N.KvLayer, "fg_accept_args": N.AcceptArgs,
-               "fg_medusa_head": N.MedusaHead}
+               "fg_medusa_head": N.MedusaHead, "fg_chain_cell": N.ChainCell}
     lines = []
     for cname, py in structs.items():
         lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')

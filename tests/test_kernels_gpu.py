@@ -222,6 +222,106 @@ def test_medusa_propose_matches_torch_heads_then_lm_head(ops, B, H, V, n_heads, 
     assert err <= 1e-2 * root.float().abs().max().item() + 1e-3
 
 
+def _chain_case(n_seq, n_parent, fanout, n_child, H, V, seed):
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(seed)
+    bn = max(64, H // 8)
+    mk = lambda *shape, s=1.0, o=0.0: (torch.randn(*shape, generator=g) * s + o).to(bf).to(DEV)
+    state = mk(n_seq * n_parent, H, s=0.5)
+    tokens = torch.randint(0, V, (n_seq, n_parent * fanout), generator=g, dtype=torch.int32).to(DEV)
+    embed = mk(V, H, s=0.05)
+    cell = {"state_norm.weight": mk(H, s=0.1, o=1.0), "state_norm.bias": mk(H, s=0.1),
+            "token_norm.weight": mk(H, s=0.1, o=1.0), "token_norm.bias": mk(H, s=0.1),
+            "state_proj.weight": mk(bn, H, s=H ** -0.5), "token_proj.weight": mk(bn, H, s=H ** -0.5),
+            "out_proj.weight": mk(H, bn, s=bn ** -0.5), "out_proj.bias": mk(H, s=0.1),
+            "gate": torch.tensor(-1.0, dtype=bf, device=DEV)}
+    return state, tokens, embed, cell
+
+
+def _chain_ref(state, tokens, embed, cell, n_parent, fanout, n_child):
+    """ChainDraftCell.forward evaluated by torch in bf16 on the gathered rows."""
+    F = torch.nn.functional
+    H = state.shape[1]
+    M = tokens.shape[0] * n_child
+    r = torch.arange(M, device=DEV)
+    b, j = r // n_child, r % n_child
+    s = state[b * n_parent + j // fanout]
+    e = embed[tokens[b, j].long()]
+    c = cell
+    mixed = (F.linear(F.layer_norm(s, (H,), c["state_norm.weight"], c["state_norm.bias"], 1e-5),
+                      c["state_proj.weight"])
+             + F.linear(F.layer_norm(e, (H,), c["token_norm.weight"], c["token_norm.bias"], 1e-5),
+                        c["token_proj.weight"]))
+    delta = F.linear(F.silu(mixed), c["out_proj.weight"], c["out_proj.bias"])
+    return s, s + torch.sigmoid(c["gate"]) * delta
+
+
+@pytest.mark.parametrize("n_seq,n_parent,fanout,n_child,H,V,k", [
+    (64, 4, 2, 8, 1536, 151936, 2),   # config-2 width, 512 rows: two 256-row passes
+    (8, 1, 1, 1, 4096, 128256, 4),    # the cell on the root token, Llama-8B width (bottleneck 512)
+    (5, 3, 3, 7, 512, 3000, 0),       # ragged children per parent, no top-k
+])
+def test_chain_step_matches_torch_cell_then_lm_head(ops, n_seq, n_parent, fanout, n_child, H, V, k):
+    """fg_chain_step: the new states against torch's bf16 ChainDraftCell on
+    the same parents and tokens, and the top-k bit-identical to
+    fg_lm_head_topk on the states the call produced."""
+    state, tokens, embed, cell = _chain_case(n_seq, n_parent, fanout, n_child, H, V, seed=n_seq + H)
+    M = n_seq * n_child
+    bn = cell["state_proj.weight"].shape[0]
+    out = torch.full((M, H), float("nan"), dtype=torch.bfloat16, device=DEV)
+    mk = lambda: (torch.empty((M, k), dtype=torch.int32, device=DEV), torch.empty((M, k), device=DEV),
+                  torch.empty(M, device=DEV), torch.empty(M, device=DEV)) if k else None
+    got = mk()
+    ws = torch.empty(ops.chain_step_workspace_bytes(M, H, bn, V, k) // 4 + 64, dtype=torch.int32, device=DEV)
+    ops.chain_step(state, tokens, n_parent=n_parent, fanout=fanout, n_child=n_child, embed=embed, cell=cell,
+                   lm_head=embed if k else None, k=k, state_out=out, topk_out=got, workspace=ws)
+    torch.cuda.synchronize()
+    s, ref = _chain_ref(state, tokens, embed, cell, n_parent, fanout, n_child)
+    d = out.float() - ref.float()
+    # bf16 on both sides with different GEMM summation orders: the states
+    # within 1e-2 normwise (no element beyond 2e-2 of the largest), and the
+    # cell's update (state_out - parent) within 5e-2 normwise of torch's
+    assert (d.norm() / ref.float().norm()).item() <= 1e-2
+    assert d.abs().max().item() <= 2e-2 * ref.float().abs().max().item()
+    upd, ref_upd = out.float() - s.float(), ref.float() - s.float()
+    assert ((upd - ref_upd).norm() / ref_upd.norm()).item() <= 5e-2
+    if k:
+        want = mk()
+        ws2 = torch.empty(max(ops.lm_head_topk_workspace_bytes(256, V, 0, k), 16) // 4 + 4, dtype=torch.int32,
+                          device=DEV)
+        for r0 in range(0, M, 256):
+            r1 = min(M, r0 + 256)
+            ops.lm_head_topk(out[r0:r1], embed, n_logit_rows=0, logits=None, topk_row0=0, k=k,
+                             topk_out=tuple(t[r0:r1] for t in want), workspace=ws2)
+        torch.cuda.synchronize()
+        for a, b in zip(got[:3], want[:3]):
+            assert torch.equal(a, b)
+        assert torch.allclose(got[3], want[3])
+
+
+def test_chain_step_out_of_range_token_is_reported(ops):
+    """A token outside [0, V) records FG_EINVAL in the device error word and
+    reads embedding row 0 instead of memory outside the table."""
+    from flashgrpo_b200 import _native
+
+    state, tokens, embed, cell = _chain_case(2, 1, 2, 2, 256, 1000, seed=3)
+    bad = tokens.clone()
+    bad[1, 0] = 1000
+    zero = tokens.clone()
+    zero[1, 0] = 0
+    ws = torch.empty(ops.chain_step_workspace_bytes(4, 256, 64, 1000, 0) // 4 + 64, dtype=torch.int32, device=DEV)
+    outs = []
+    assert _native.read_device_error(clear=True) == 0
+    for t in (bad, zero):
+        out = torch.empty((4, 256), dtype=torch.bfloat16, device=DEV)
+        ops.chain_step(state, t, n_parent=1, fanout=2, n_child=2, embed=embed, cell=cell, lm_head=None, k=0,
+                       state_out=out, topk_out=None, workspace=ws)
+        torch.cuda.synchronize()
+        outs.append(out)
+        assert _native.read_device_error(clear=True) == (_native.FG_EINVAL if t is bad else 0)
+    assert torch.equal(outs[0], outs[1])
+
+
 # -------------------------------------------------------------- tree build
 def _check_tree(ops, *, tree_mode, B, cpeak, mx, depth, fixed, n_heads, V=300, adaptive=False, amin=(1, 1, 1),
                 metric="top1_prob", seed=0, dtype=torch.bfloat16):
