@@ -13,8 +13,13 @@
 
 namespace fg {
 
+// Chunks up to this length are searched by a warp (exponentials in
+// parallel, the running sum by one lane); longer ones by their own thread.
+constexpr int kFindWarpMax = 1024;
+
 struct SampleSmem {
     float P[FG_SAMPLE_LANES + 1];
+    float e[kFindWarpMax];  // the searched chunk's e_i
     float red[FG_SAMPLE_LANES / 32];
     int32_t redi[FG_SAMPLE_LANES / 32];
     int32_t result;
@@ -29,8 +34,10 @@ __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return _
 template <>
 __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
 
+// x / T (IEEE division) for T > 0.  Division by 1 is exact, so T == 1 skips
+// it and gives the same value.
 __device__ __forceinline__ float scale_t(float v, float temperature) {
-    return temperature > 0.0f ? __fdiv_rn(v, temperature) : v;
+    return temperature > 0.0f && temperature != 1.0f ? __fdiv_rn(v, temperature) : v;
 }
 
 // Block-wide (max value, lowest index) reduction; returns the index.
@@ -182,20 +189,56 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
     if (tid == 0) sm.result = -1;
     __syncthreads();
     if (tid == 0) {
+        // the specified sequential sum, its loads batched ahead of the adds
         float P = 0.0f;
         sm.P[0] = 0.0f;
-        for (int t = 0; t < FG_SAMPLE_LANES; ++t) {
-            P = __fadd_rn(P, sm.P[t + 1]);
-            sm.P[t + 1] = P;
+        for (int t0 = 0; t0 < FG_SAMPLE_LANES; t0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = sm.P[t0 + j + 1];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                P = __fadd_rn(P, v[j]);
+                sm.P[t0 + j + 1] = P;
+            }
         }
     }
     __syncthreads();
     const float target = __fmul_rn(u, sm.P[FG_SAMPLE_LANES]);
     const float P0 = sm.P[tid];
-    if (P0 <= target && target < sm.P[tid + 1]) {
-        int32_t found = -1;
-        chunk_scan<T, true>(row, lo, hi, m, temperature, vec, P0, target, &found);
-        sm.result = found;
+    const bool mine = P0 <= target && target < sm.P[tid + 1];
+    if (C > kFindWarpMax) {
+        if (mine) {
+            int32_t found = -1;
+            chunk_scan<T, true>(row, lo, hi, m, temperature, vec, P0, target, &found);
+            sm.result = found;
+        }
+    } else {
+        // the chunk holding the target: its e_i computed by warp 0, then the
+        // same left-to-right running sum by lane 0
+        if (mine) sm.redi[0] = tid;
+        if (tid == 0 && !(sm.P[0] <= target && target < sm.P[FG_SAMPLE_LANES])) sm.redi[0] = -1;
+        __syncthreads();
+        const int32_t t = sm.redi[0];
+        if (tid < 32 && t >= 0) {
+            const int32_t lo_t = min(t * C, V), hi_t = min(lo_t + C, V);
+            for (int32_t i = lo_t + tid; i < hi_t; i += 32)
+                sm.e[i - lo_t] = fg_exp(__fsub_rn(scale_t(to_f<T>(row[i]), temperature), m));
+            __syncwarp();
+            if (tid == 0) {
+                const float base = sm.P[t];
+                float c = 0.0f;
+                int32_t found = -1;
+                for (int32_t i = 0; i < hi_t - lo_t; ++i) {
+                    c = __fadd_rn(c, sm.e[i]);
+                    if (__fadd_rn(base, c) > target) {
+                        found = lo_t + i;
+                        break;
+                    }
+                }
+                sm.result = found;
+            }
+        }
     }
     __syncthreads();
     const int32_t r = sm.result;
