@@ -69,11 +69,17 @@ __device__ __forceinline__ float philox_uniform(uint64_t seed, uint32_t seq, uin
 // head and its fp32 tail so n * head is exact), degree-7 Taylor polynomial of
 // e^r by fused Horner steps with coefficients fp32(1/k!), scale by 2^n via the
 // exponent field.  Inputs below -86 (and NaN) give 0.
+// n = rint(t), ties to even, without the conversion units: for |t| < 2^22,
+// t + 1.5 * 2^23 lands where the float spacing is 1, so round-to-nearest-even
+// leaves the integer nearest t (ties to the even one, 1.5 * 2^23 being even)
+// in the low significand bits; subtracting the constant back is exact.  The
+// callers pass x - max <= 0, so t is in [-125, 0].
 __device__ __forceinline__ float fg_exp(float x) {
     if (!(x >= -86.0f)) return 0.0f;
     const float t = __fmul_rn(x, 1.44269502162933349609375f);
-    const int n = __float2int_rn(t);
-    const float nf = (float)n;
+    const float shifted = __fadd_rn(t, 12582912.0f);  // 1.5 * 2^23, bits 0x4B400000
+    const float nf = __fsub_rn(shifted, 12582912.0f);
+    const int n = __float_as_int(shifted) - 0x4B400000;
     float r = __fmaf_rn(-nf, 0.693145751953125f, x);
     r = __fmaf_rn(-nf, 1.42860676533018704503775e-06f, r);
     float p = 1.98412701138295233249664e-04f;

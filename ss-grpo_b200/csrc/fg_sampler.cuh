@@ -171,6 +171,9 @@ template <typename T>
 __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool do_sample, float u, SampleSmem& sm) {
     if (!do_sample || temperature == 0.0f) return block_argmax<T>(row, V, sm);
     const int tid = threadIdx.x;
+    const int32_t C = sample_chunk_len(V);
+    const int32_t lo = min(tid * C, V);
+    const int32_t hi = min(lo + C, V);
     // pass 1: maximum of the scaled logits.  x -> x / T is monotone for T > 0,
     // so the maximum of the raw values, divided once, is that maximum.
     float bv;
@@ -181,9 +184,6 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
     __syncthreads();
     // pass 2: left-to-right sum of this thread's chunk
     const bool vec = row_vectorizable<T>(row, V);
-    const int32_t C = sample_chunk_len(V);
-    const int32_t lo = min(tid * C, V);
-    const int32_t hi = min(lo + C, V);
     const float c = chunk_scan<T, false>(row, lo, hi, m, temperature, vec, 0.0f, 0.0f, nullptr);
     sm.P[tid + 1] = c;
     if (tid == 0) sm.result = -1;
