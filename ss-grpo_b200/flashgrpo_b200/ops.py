@@ -191,14 +191,16 @@ def chain_step(state: torch.Tensor, tokens: torch.Tensor, *, n_parent: int, fano
             raise ValueError(f"chain cell {nm} must be bf16")
     bn = cell["state_proj.weight"].shape[0]
     c = N.ChainCell(*[_ptr(cell[nm]) for nm in names], int(bn))
+    V = lm_head.shape[0] if lm_head is not None else embed.shape[0]
+    if embed.shape[0] < V:
+        raise ValueError("the embedding table needs the lm_head's V rows (tokens are checked against V)")
     idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
     M = n_seq * n_child
     # per pass of 256 rows: norms, 3 projections, mix, finish (+ lm_head and its top-k merge)
     n_launch = (M + 255) // 256 * (6 + (2 if k > 0 else 0))
     N.call("fg_chain_step", _ptr(state), _ptr(tokens), tokens.stride(0), n_seq, int(n_parent), int(fanout),
            int(n_child), _ptr(embed), embed.stride(0), H, N.FG_DTYPE_BF16, ctypes.byref(c), float(eps),
-           _ptr(state_out), _ptr(lm_head), lm_head.stride(0) if lm_head is not None else 0,
-           lm_head.shape[0] if lm_head is not None else embed.shape[0], int(k), _ptr(idx), _ptr(val), _ptr(mx),
+           _ptr(state_out), _ptr(lm_head), lm_head.stride(0) if lm_head is not None else 0, V, int(k), _ptr(idx), _ptr(val), _ptr(mx),
            _ptr(lse), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream(state),
            n_launch=n_launch)
     return state_out
