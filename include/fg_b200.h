@@ -413,6 +413,16 @@ fg_status fg_rmsnorm(const void *x, const void *weight, int32_t dtype, int32_t n
 /* y = layer_norm(x) * weight + bias per row (MEDUSA head norm, eps 1e-5). */
 fg_status fg_layernorm(const void *x, const void *weight, const void *bias, int32_t dtype, int32_t n_rows,
                        int32_t dim, float eps, void *y, void *stream);
+/* act[t, j] = bf16(bf16(silu(bf16(g))) * bf16(u)) with g = x[t] . w[j] and
+ * u = x[t] . w[I + j]: the MLP's act_fn(gate_proj(x)) * up_proj(x) on the
+ * tensor cores with SiLU-gating in the GEMM epilogue, so the [T, 2I]
+ * gate/up tensor of fg_silu_mul is never written.  x [T, H] and w_gate_up
+ * [2I, H] (gate_proj rows, then up_proj rows) bf16 with contiguous rows, act
+ * [T, I]; H a multiple of 64, I a multiple of 16; dtype FG_DTYPE_BF16 only.
+ * Replaces the gate/up GEMM and act_fn of the HF Qwen2/Llama MLP inside
+ * _forward_decoder (flashgrpo_b200/models/qwen_flashgrpo_wrapper.py:150-186). */
+fg_status fg_gate_up_silu(const void *x, int32_t dtype, int32_t T, int32_t H, const void *w_gate_up, int32_t I,
+                          void *act, void *stream);
 /* out[r, :I] = silu(gu[r, :I]) * gu[r, I:2I] (SwiGLU of the MLP). */
 fg_status fg_silu_mul(const void *gu, int32_t dtype, int32_t n_rows, int32_t inter, void *out, void *stream);
 /* out = x + silu(y) (residual of MedusaPredictionHead.project_hidden,

@@ -87,6 +87,7 @@ SIGNATURES = {
     "fg_chain_step": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32,
                               ctypes.POINTER(ChainCell), c_f32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp,
                               c_vp, c_vp, ctypes.c_size_t, c_vp]),
+    "fg_gate_up_silu": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                               c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
@@ -142,7 +143,7 @@ def load():
 LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree", "fg_rope_table",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
              "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows", "fg_medusa_propose",
-             "fg_chain_step"}
+             "fg_chain_step", "fg_gate_up_silu"}
 launches = 0
 
 

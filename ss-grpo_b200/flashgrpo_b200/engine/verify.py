@@ -10,8 +10,9 @@ reference, Reflex off) runs as one stream of work with no host sync:
   tree      fg_build_tree: plan, dense tree, ancestor bits, slots     (K2)
   verify    per layer: RMSNorm, QKV GEMM (+bias), fg_rope_kv_write (RoPE +
             tree K/V written at each row's cache tail), fg_tree_attention
-            (K3), O GEMM + residual, RMSNorm, gate/up GEMM, SwiGLU, down GEMM
-            + residual; final RMSNorm
+            (K3), O GEMM + residual, RMSNorm, fg_gate_up_silu (gate/up GEMM
+            with SwiGLU in the epilogue, tcgen05), down GEMM + residual;
+            final RMSNorm
   lm_head   internal (has-children) nodes only                        (cuBLAS)
   accept    fg_accept_extract: exact_target walk, clip/EOS/pending rules,
             KV compaction in every layer, next hidden state           (K4)
@@ -569,6 +570,8 @@ class VerifyEngine:
         # the tree positions are fixed for the round: one cos/sin table for all layers
         ops.rope_table(rb.tree["positions"], w.inv_freq, w.attention_scaling, sp.dtype, out=rb.rope_cs)
         ws = self._attn_workspace(rb, st, cfg.attn_splits)
+        # gate/up GEMM with SwiGLU in its epilogue (bf16); fp32 keeps cuBLAS + fg_silu_mul
+        fused_mlp = sp.dtype == torch.bfloat16 and sp.hidden % 64 == 0 and sp.inter % 16 == 0
         for l, lw in enumerate(w.layers):
             ops.rmsnorm(rb.h, lw["in_norm"], sp.eps, out=rb.xn)
             if lw["b_qkv"] is not None:
@@ -589,8 +592,11 @@ class VerifyEngine:
             if lw["b_o"] is not None:
                 rb.h.add_(lw["b_o"])
             ops.rmsnorm(rb.h, lw["post_norm"], sp.eps, out=rb.xn)
-            torch.mm(rb.xn, lw["w_gu"].t(), out=rb.gu)
-            ops.silu_mul(rb.gu, out=rb.act)
+            if fused_mlp:
+                ops.gate_up_silu(rb.xn, lw["w_gu"], out=rb.act)
+            else:
+                torch.mm(rb.xn, lw["w_gu"].t(), out=rb.gu)
+                ops.silu_mul(rb.gu, out=rb.act)
             torch.addmm(rb.h, rb.act, lw["w_down"].t(), out=rb.h)
         ops.rmsnorm(rb.h, w.final_norm, sp.eps, out=rb.tree_hidden.view(B * N_, -1))
 

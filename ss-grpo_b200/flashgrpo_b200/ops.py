@@ -409,6 +409,25 @@ def layernorm(x, weight, bias, eps, out=None):
     return out
 
 
+def gate_up_silu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fg_gate_up_silu (bf16): silu(x @ w_gate_up[:I].T) * (x @ w_gate_up[I:].T)
+    with the GEMM and the gating in one tcgen05 kernel; x [T, H], w_gate_up
+    [2I, H]; returns act [T, I]."""
+    _need(x, "x")
+    _need(w_gate_up, "w_gate_up")
+    if x.dtype != torch.bfloat16 or w_gate_up.dtype != torch.bfloat16:
+        raise ValueError("gate_up_silu is the bf16 path")
+    T, H = x.shape
+    I = w_gate_up.shape[0] // 2
+    if w_gate_up.shape != (2 * I, H):
+        raise ValueError("w_gate_up must be [2I, H]")
+    if out is None:
+        out = torch.empty((T, I), dtype=x.dtype, device=x.device)
+    _need(out, "out")
+    N.call("fg_gate_up_silu", _ptr(x), N.FG_DTYPE_BF16, T, H, _ptr(w_gate_up), I, _ptr(out), _stream(x))
+    return out
+
+
 def silu_mul(gu, out=None):
     inter = gu.shape[-1] // 2
     rows = gu.numel() // gu.shape[-1]

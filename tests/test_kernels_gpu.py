@@ -696,6 +696,32 @@ def test_row_map_matches_gathered_cache(ops, dtype):
         assert torch.equal(km_[others], kc[others]) and torch.equal(vm_[others], vc[others])
 
 
+@pytest.mark.parametrize("T,H,I", [
+    (832, 1536, 8960),   # config 2: 64 rows x 13 tree nodes, Qwen2.5-1.5B MLP
+    (100, 256, 384),     # one partial token tile
+    (300, 512, 1024),    # three token tiles, the last partial
+])
+def test_gate_up_silu_matches_gemm_then_silu_mul(ops, T, H, I):
+    """fg_gate_up_silu against torch's bf16 gate/up GEMM followed by
+    fg_silu_mul on the materialized [T, 2I] tensor (both round g and u to
+    bf16 before the gating; only the GEMM summation order differs)."""
+    g = torch.Generator().manual_seed(T + I)
+    x = (torch.randn(T, H, generator=g)).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(2 * I, H, generator=g) * H ** -0.5).to(torch.bfloat16).to(DEV)
+    out = torch.full((T, I), float("nan"), dtype=torch.bfloat16, device=DEV)
+    got = ops.gate_up_silu(x, w, out=out)
+    ref = ops.silu_mul(x @ w.t())
+    torch.cuda.synchronize()
+    assert torch.isfinite(got.float()).all()
+    d = got.float() - ref.float()
+    assert (d.norm() / ref.float().norm()).item() <= 1e-2
+    assert d.abs().max().item() <= 2e-2 * ref.float().abs().max().item()
+    # a second call into the same buffer gives the same bits
+    again = ops.gate_up_silu(x, w, out=torch.empty_like(out))
+    torch.cuda.synchronize()
+    assert torch.equal(again, got)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_norms_and_activations(ops, dtype):
     g = torch.Generator().manual_seed(7)
