@@ -40,6 +40,21 @@ def _need(t: torch.Tensor, name: str, dtype=None, contiguous=True):
         raise ValueError(f"{name} must be contiguous")
 
 
+def _out(t: torch.Tensor, name: str, dtype, n: int):
+    """An output the kernel writes as n contiguous elements of dtype."""
+    if t.dtype != dtype or not t.is_contiguous() or t.numel() < n:
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor of at least {n} elements")
+
+
+def _topk_out(topk_out, rows: int, k: int):
+    idx, val, mx, lse = topk_out
+    _out(idx, "top-k indices", torch.int32, rows * k)
+    _out(val, "top-k values", torch.float32, rows * k)
+    _out(mx, "row maxima", torch.float32, rows)
+    if lse is not None:
+        _out(lse, "row logsumexp", torch.float32, rows)
+
+
 def _rows(t: torch.Tensor, name: str) -> tuple[int, int]:
     """(row stride, vocab) of a 2-D tensor whose last dim is contiguous."""
     if t.dim() != 2 or t.stride(1) != 1:
@@ -149,6 +164,15 @@ def medusa_propose(x: torch.Tensor, B: int, heads: list[dict], lm_head: torch.Te
         if hw["fc_w"].shape != (H, H) or hw["fc_b"].shape != (H,):
             raise ValueError(f"head {i}: fc must be [H, H] with bias [H]")
         arr[i] = N.MedusaHead(_ptr(hw["norm_w"]), _ptr(hw["norm_b"]), _ptr(hw["fc_w"]), _ptr(hw["fc_b"]))
+    V = lm_head.shape[0]
+    if root_logits is not None and (root_logits.dtype != torch.bfloat16 or root_logits.dim() != 2
+                                    or root_logits.stride(1) != 1 or root_logits.shape[0] < B
+                                    or root_logits.shape[1] < V):
+        raise ValueError("root_logits must be bf16 [>= B, >= V] with contiguous rows")
+    if n > 0:
+        if topk_out is None:
+            raise ValueError("topk_out is required when there are heads")
+        _topk_out(topk_out, n * B, k)
     idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
     # LayerNorm and finishing pass per 8 heads, one fc GEMM per head, lm_head (+ top-k merge)
     n_launch = (2 * ((n + 7) // 8) + n if n > 0 else 0) + 1 + (n > 0)
@@ -194,6 +218,13 @@ def chain_step(state: torch.Tensor, tokens: torch.Tensor, *, n_parent: int, fano
     V = lm_head.shape[0] if lm_head is not None else embed.shape[0]
     if embed.shape[0] < V:
         raise ValueError("the embedding table needs the lm_head's V rows (tokens are checked against V)")
+    if state.shape[0] != n_seq * n_parent or tokens.shape[1] < n_child:
+        raise ValueError("state must have n_seq * n_parent rows and tokens n_child columns")
+    _out(state_out, "state_out", torch.bfloat16, n_seq * n_child * H)
+    if k > 0:
+        if topk_out is None or lm_head is None:
+            raise ValueError("k > 0 needs lm_head and topk_out")
+        _topk_out(topk_out, n_seq * n_child, k)
     idx, val, mx, lse = topk_out if topk_out is not None else (None, None, None, None)
     M = n_seq * n_child
     # per pass of 256 rows: norms, 3 projections, mix, finish (+ lm_head and its top-k merge)
@@ -424,6 +455,8 @@ def gate_up_silu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | N
     if out is None:
         out = torch.empty((T, I), dtype=x.dtype, device=x.device)
     _need(out, "out")
+    if out.shape != (T, I) or out.dtype != torch.bfloat16:
+        raise ValueError("out must be bf16 [T, I]")
     N.call("fg_gate_up_silu", _ptr(x), N.FG_DTYPE_BF16, T, H, _ptr(w_gate_up), I, _ptr(out), _stream(x))
     return out
 

@@ -105,3 +105,60 @@ def test_hf_plugin_registration_cache_and_ancestor_bits():
     bits = ancestor_bits(parents)
     assert bits[:5, 0].tolist() == [0b1, 0b11, 0b101, 0b1011, 0b10101]
     assert bits[40].tolist()[0] == 0b10101 and bits[40].tolist()[1] == 1 << (40 - 32)
+
+
+def test_new_entry_point_wrappers_check_their_buffers(monkeypatch):
+    """The ops wrappers of fg_medusa_propose, fg_chain_step and
+    fg_gate_up_silu hand the library well-sized outputs or raise: run on CPU
+    tensors with the device checks and the library call stubbed out."""
+    import pytest
+
+    from flashgrpo_b200 import ops
+
+    calls = []
+    monkeypatch.setattr(ops, "_need", lambda *a, **k: None)
+    monkeypatch.setattr(ops, "_stream", lambda t: 0)
+    monkeypatch.setattr(ops.N, "call", lambda name, *a, **k: calls.append((name, k.get("n_launch"))))
+    bf, i32, f32 = torch.bfloat16, torch.int32, torch.float32
+    B, H, V, k = 4, 128, 300, 3
+    heads = [dict(norm_w=torch.ones(H, dtype=bf), norm_b=torch.zeros(H, dtype=bf), fc_w=torch.zeros(H, H, dtype=bf),
+                  fc_b=torch.zeros(H, dtype=bf)) for _ in range(2)]
+    x = torch.zeros(3 * B, H, dtype=bf)
+    w = torch.zeros(V, H, dtype=bf)
+    top = lambda rows: (torch.zeros(rows, k, dtype=i32), torch.zeros(rows, k, dtype=f32), torch.zeros(rows, dtype=f32),
+                        None)
+    ws = torch.zeros(16, dtype=i32)
+    ops.medusa_propose(x, B, heads, w, root_logits=torch.zeros(B, V, dtype=bf), k=k, topk_out=top(2 * B), workspace=ws)
+    assert calls[-1] == ("fg_medusa_propose", 2 + 2 + 2)  # LayerNorm, 2 fc, finish, lm_head + merge
+    with pytest.raises(ValueError):
+        ops.medusa_propose(x, B, heads, w, root_logits=torch.zeros(B, V - 1, dtype=bf), k=k, topk_out=top(2 * B),
+                           workspace=ws)
+    with pytest.raises(ValueError):
+        ops.medusa_propose(x, B, heads, w, root_logits=None, k=k, topk_out=top(2 * B - 1), workspace=ws)
+    with pytest.raises(ValueError):
+        ops.medusa_propose(x, B, heads, w, root_logits=None, k=k, topk_out=None, workspace=ws)
+    # chain step: 2 sequences, 3 parents, fanout 2, 5 children each
+    cell = {n: torch.zeros(2, dtype=bf) for n in ("state_norm.weight", "state_norm.bias", "token_norm.weight",
+                                                  "token_norm.bias", "out_proj.bias", "gate")}
+    cell.update({"state_proj.weight": torch.zeros(64, H, dtype=bf), "token_proj.weight": torch.zeros(64, H, dtype=bf),
+                 "out_proj.weight": torch.zeros(H, 64, dtype=bf)})
+    state = torch.zeros(6, H, dtype=bf)
+    toks = torch.zeros(2, 6, dtype=i32)
+    kw = dict(n_parent=3, fanout=2, n_child=5, embed=w, cell=cell, lm_head=w, k=k, workspace=ws)
+    ops.chain_step(state, toks, state_out=torch.zeros(10, H, dtype=bf), topk_out=top(10), **kw)
+    assert calls[-1] == ("fg_chain_step", 6 + 2)
+    with pytest.raises(ValueError):
+        ops.chain_step(state, toks, state_out=torch.zeros(9, H, dtype=bf), topk_out=top(10), **kw)
+    with pytest.raises(ValueError):
+        ops.chain_step(state, toks, state_out=torch.zeros(10, H, dtype=bf), topk_out=top(9), **kw)
+    with pytest.raises(ValueError):
+        ops.chain_step(state[:5], toks, state_out=torch.zeros(10, H, dtype=bf), topk_out=top(10), **kw)
+    with pytest.raises(ValueError):
+        ops.chain_step(state, toks, state_out=torch.zeros(10, H, dtype=bf), topk_out=top(10),
+                       **{**kw, "embed": w[:V - 1]})
+    # fused MLP
+    xt, wgu = torch.zeros(7, H, dtype=bf), torch.zeros(2 * 256, H, dtype=bf)
+    ops.gate_up_silu(xt, wgu, out=torch.zeros(7, 256, dtype=bf))
+    assert calls[-1] == ("fg_gate_up_silu", None)
+    with pytest.raises(ValueError):
+        ops.gate_up_silu(xt, wgu, out=torch.zeros(7, 255, dtype=bf))
