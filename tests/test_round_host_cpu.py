@@ -156,6 +156,16 @@ def test_new_entry_point_wrappers_check_their_buffers(monkeypatch):
     with pytest.raises(ValueError):
         ops.chain_step(state, toks, state_out=torch.zeros(10, H, dtype=bf), topk_out=top(10),
                        **{**kw, "embed": w[:V - 1]})
+    # 9 heads: two LayerNorm and two finishing launches around the 9 fc GEMMs
+    heads9 = heads * 4 + heads[:1]
+    ops.medusa_propose(torch.zeros(10 * B, H, dtype=bf), B, heads9, w, root_logits=None, k=k, topk_out=top(9 * B),
+                       workspace=ws)
+    assert calls[-1] == ("fg_medusa_propose", 2 + 9 + 2 + 2)
+    # 600 chain rows run as three 256-row passes
+    ops.chain_step(torch.zeros(60 * 3, H, dtype=bf), torch.zeros(60, 10, dtype=i32), n_parent=3, fanout=4,
+                   n_child=10, embed=w, cell=cell, lm_head=None, k=0, state_out=torch.zeros(600, H, dtype=bf),
+                   topk_out=None, workspace=ws)
+    assert calls[-1] == ("fg_chain_step", 3 * 6)
     # fused MLP
     xt, wgu = torch.zeros(7, H, dtype=bf), torch.zeros(2 * 256, H, dtype=bf)
     ops.gate_up_silu(xt, wgu, out=torch.zeros(7, 256, dtype=bf))
