@@ -534,6 +534,12 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
     logical = full_mask.sum(-1)
     stats = dict(total_acc_length=0, total_decoded_token_num=0, total_verify_rounds=0, total_correction_tokens=0,
                  total_accepted_medusa_tokens=0, total_proposed_medusa_tokens=0)
+    # tree / acceptance statistics of the result dict (decoder :1617-1638,
+    # accumulated at :2185-2205, :2220, :2250, :2320-2322, :2860)
+    nodes_by_head = [0] * min(cfg.num_medusa_heads, len(heads))
+    tstat = dict(active_batch_sum=0, tree_node_sum=0.0, tree_sample_count=0, tree_budget_unused=0,
+                 tree_query_rows=0, tree_lm_head_rows=0)
+    accept_hist, accept_by_depth, proposed_by_depth, layout_counts = {}, {}, {}, {}
     round_idx = 0
     prefill_time = time.perf_counter() - t_start
     while active_ids:
@@ -583,13 +589,27 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
             trees = build_dense_trees(root, head_logits, plan)
         for t in trees:
             stats["total_proposed_medusa_tokens"] += t.node_count - 1
+        layout_counts["configured"] = layout_counts.get("configured", 0) + B
+        tstat["active_batch_sum"] += B
+        tstat["tree_node_sum"] += sum(t.node_count for t in trees) / max(B, 1)
+        tstat["tree_sample_count"] += 1
+        for t in trees:
+            # CandidateTree.nodes_by_head (medusa_tree.py:38-45): nodes per depth >= 2
+            for dpt in t.depths:
+                if dpt >= 2 and dpt - 2 < len(nodes_by_head):
+                    nodes_by_head[dpt - 2] += 1
+                if dpt >= 2:
+                    proposed_by_depth[dpt] = proposed_by_depth.get(dpt, 0) + 1
+            tstat["tree_budget_unused"] += max(0, plan.node_budget_per_seq - t.node_count)
         tree_logits = slots = tree_hidden = None
         if plan.active_heads > 0 and max(t.node_count for t in trees) > 1:
             ids, mask4d, tpos, _ = tree_attention_inputs(trees, full_mask, logical, pad_token_id=pad_token_id,
                                                          dtype=torch.float32)
+            tstat["tree_query_rows"] += int(ids.shape[0] * ids.shape[1])
             tcache = _cache_from_layers(model, layers)
             tree_hidden, tcache = _run_model(model, ids, mask4d, tpos, tcache)
             rows, nodes, slots = internal_logit_layout(trees)
+            tstat["tree_lm_head_rows"] += len(rows)
             tree_logits = torch.nn.functional.linear(tree_hidden[rows, nodes], lm_w)
             tree_layers = _cache_layers(tcache)
         if tree_logits is None:
@@ -615,6 +635,9 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
             stats["total_acc_length"] += len(tk)
             stats["total_decoded_token_num"] += 1
             stats["total_accepted_medusa_tokens"] += max(len(tk) - 1, 0)
+            accept_hist[len(tk)] = accept_hist.get(len(tk), 0) + 1
+            for dpt in range(2, len(tk) + 1):
+                accept_by_depth[dpt] = accept_by_depth.get(dpt, 0) + 1
             acc.append(tk)
             acc_nodes.append(nd)
             fin.append(done)
@@ -636,6 +659,7 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
                 tree_logits[slots[r][n]] if slots[r][n] >= 0 else torch.nn.functional.linear(cur_hidden[r], lm_w)
                 for r, n in enumerate(last)
             ])
+            tstat["tree_lm_head_rows"] += sum(1 for r, n in enumerate(last) if slots[r][n] < 0)
         else:
             ids = torch.full((B, max_acc), int(pad_token_id), dtype=torch.long)
             apos = torch.zeros((B, max_acc), dtype=torch.long)
@@ -663,6 +687,40 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
             active_ids = [active_ids[r] for r in keep]
         round_idx += 1
         round_times.append((time.perf_counter() - t_round, sum(len(t) for t in acc)))
-    stats["average_accept_length"] = stats["total_acc_length"] / max(stats["total_decoded_token_num"], 1)
+    decoded = max(stats["total_decoded_token_num"], 1)
+    rounds = max(stats["total_verify_rounds"], 1)
+    proposed = max(stats["total_proposed_medusa_tokens"], 1)
+    stats["average_accept_length"] = stats["total_acc_length"] / decoded
+    # the deterministic entries of the reference's result dict (:3039-3117)
+    stats.update(
+        max_sequence_length=max((len(g) for g in generated), default=0),
+        accepted_tokens_per_medusa_step=stats["average_accept_length"],
+        total_accepted_draft_tokens=stats["total_accepted_medusa_tokens"],
+        total_proposed_draft_tokens=stats["total_proposed_medusa_tokens"],
+        correction_token_rate=stats["total_correction_tokens"] / decoded,
+        draft_acceptance_rate=stats["total_accepted_medusa_tokens"] / proposed,
+        medusa_acceptance_rate=stats["total_accepted_medusa_tokens"] / proposed,
+        average_active_batch_size=tstat["active_batch_sum"] / rounds,
+        average_tree_nodes_per_seq=tstat["tree_node_sum"] / max(tstat["tree_sample_count"], 1),
+        tree_active_heads=max((i + 1 for i, c in enumerate(nodes_by_head) if c > 0), default=0),
+        tree_nodes_head1=nodes_by_head[0] if nodes_by_head else 0,
+        tree_nodes_head2=nodes_by_head[1] if len(nodes_by_head) > 1 else 0,
+        tree_nodes_head3=nodes_by_head[2] if len(nodes_by_head) > 2 else 0,
+        tree_total_nodes=sum(nodes_by_head) + stats["total_decoded_token_num"],
+        tree_budget_unused=tstat["tree_budget_unused"],
+        tree_query_rows=tstat["tree_query_rows"],
+        tree_lm_head_rows=tstat["tree_lm_head_rows"],
+        tree_lm_head_row_ratio=tstat["tree_lm_head_rows"] / max(tstat["tree_query_rows"], 1),
+        accept_length_histogram=accept_hist,
+        medusa_accept_by_depth=accept_by_depth,
+        medusa_proposed_by_depth=proposed_by_depth,
+        actual_tree_layout_counts=layout_counts,
+        head3_conditional_path_acceptance=0.0,
+        head3_conditional_path_success=0,
+        head3_conditional_path_opportunities=0,
+        cache_update_mode="extract_path",
+        oom_count=0,
+        timing_sample_count=0,
+    )
     return {"generated_token_ids": generated, **stats, "prefill_time": prefill_time,
             "round_times": round_times}

@@ -10,9 +10,19 @@ CUDA graph and reads back the accepted tokens.
 Sampling: draws come from Philox uniforms indexed by (sequence id, round,
 draw) and the fg-icdf-v1 inverse CDF, so a seeded run is reproducible bit for
 bit.  Nucleus sampling (``top_p < 1``), adaptive trees and chain proposals
-are supported; ``top_k`` sampling, the sparse tree layouts, adaptive widths
-with chain proposals and the Reflex/HRDCR machinery are not on this path and
-are rejected explicitly.
+are supported; ``top_k`` sampling, ``cache_update_mode="recompute_accepted"``,
+the sparse tree layouts, adaptive widths with chain proposals and the
+Reflex/HRDCR machinery are not on this path and are rejected explicitly.
+
+Result timings.  A round is one CUDA graph, so the reference's per-phase host
+timers (proposal, tree verify, cache update) become CUDA events at the phase
+boundaries inside the graph: proposal + tree build | verify forward +
+internal-node lm_head | acceptance + extract_path.  Every
+``metrics_timing_sample_interval``-th round is timed that way (the sampled
+``*_cuda_time_s`` keys, as the reference samples, :1816-1822, :2940-2946);
+with ``statistical_time=True`` every round is, and the ``*_time_cost`` keys
+are the sums of the measured phase times.  Without it they split the rounds'
+host-measured wall time by the phase shares of the sampled rounds.
 """
 from __future__ import annotations
 
@@ -80,6 +90,9 @@ class FlashMedusaDecoder:
             raise NotImplementedError("Only exact_target acceptance is implemented in the main FlashGRPO path")
         if config.cache_update_mode not in {"extract_path", "recompute_accepted"}:
             raise ValueError(f"Unsupported cache_update_mode={config.cache_update_mode}")
+        if config.cache_update_mode != "extract_path":
+            raise NotImplementedError("cache_update_mode='recompute_accepted' is not on the B200 path: the accepted "
+                                      "K/V are compacted from the tree cache (extract_path) on the device")
         if config.proposal_mode not in {"medusa", "chain"}:
             raise ValueError(f"Unsupported proposal_mode={config.proposal_mode}")
         if config.proposal_mode == "chain" and config.adaptive_tree_enabled:
@@ -171,37 +184,24 @@ class FlashMedusaDecoder:
         generated = [[] for _ in range(B)]
         active_host = [True] * B
         row_len_host = st.row_len.tolist()
-        stats = dict(total_acc_length=0, total_decoded_token_num=0, total_verify_rounds=0,
-                     total_correction_tokens=0, total_accepted_medusa_tokens=0, total_proposed_medusa_tokens=0)
-        accept_hist: dict[int, int] = {}
-        accept_by_depth: dict[int, int] = {}
-        active_batch_sum = 0
-        tree_node_sum = 0.0
-        tree_plan_last = {}
+        acc = RolloutStats(min(cfg.num_medusa_heads, len(eng.heads)))
         pending_host = [-1] * B
         graphs, seen = self._graphs, self._seen
         pinned = None
-        verify_time = 0.0
         rcfg_key = dataclasses.astuple(rcfg)
         setups: dict = {}
         flat_bufs: dict = {}
+        interval = max(1, int(cfg.metrics_timing_sample_interval))
+        timer = self._phase_events(dev)
+        use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
 
         def account(d):
             """Host bookkeeping of a finished round (tokens, statistics); runs
             while the next round executes on the device."""
-            rows_d, acc_d, toks_d, dcap_d, n_tree_d, pend_before = d
+            rows_d, acc_d, toks_d, dcap_d, pend_before = d
             for i, r in enumerate(rows_d):
-                if pend_before[i] >= 0:
-                    stats["total_correction_tokens"] += 1
-                a = acc_d[i]
-                generated[r].extend(toks_d[i * dcap_d: i * dcap_d + a])
-                stats["total_acc_length"] += a
-                stats["total_decoded_token_num"] += 1
-                stats["total_accepted_medusa_tokens"] += max(a - 1, 0)
-                stats["total_proposed_medusa_tokens"] += max(n_tree_d - 1, 0)
-                accept_hist[a] = accept_hist.get(a, 0) + 1
-                for d_ in range(2, a + 1):
-                    accept_by_depth[d_] = accept_by_depth.get(d_, 0) + 1
+                generated[r].extend(toks_d[i * dcap_d: i * dcap_d + acc_d[i]])
+            acc.rows(acc_d, pend_before)
 
         deferred = None
         while any(active_host):
@@ -212,7 +212,6 @@ class FlashMedusaDecoder:
             n_active = len(act_rows)
             setup = setups.get(n_active)
             if setup is None:
-                use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
                 plan = self._plan(n_active)
                 if not use_tree:
                     plan.topk_by_depth, plan.active_heads = [], 0
@@ -233,17 +232,23 @@ class FlashMedusaDecoder:
             else:
                 rs = st
             rb = eng.buffers(n_active, plan, nh, dcap, adaptive=adaptive)
-            key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive, rcfg_key)
+            # CUDA events at the phase boundaries on sampled rounds (every
+            # round with statistical_time)
+            timed = bool(statistical_time) or acc.rounds % interval == 0
+            ev = timer if timed else None
+            key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive, rcfg_key,
+                   timed)
             tv = time.time()
             if cfg.use_cuda_graphs and key in seen:
                 if key not in graphs:
-                    graphs[key] = (eng.graph_round(rs, rb, params, rcfg), params)
+                    graphs[key] = (eng.graph_round(rs, rb, params, rcfg, phase_events=ev), params)
                 graphs[key][0].replay()
             else:
-                eng.run_round(rs, rb, params, rcfg)
+                eng.run_round(rs, rb, params, rcfg, phase_events=ev)
                 seen.add(key)
             out = rb.out
-            parts = [out["acc_len"], out["finished"], rs.pending, rb.tree["plan"], out["acc_tokens"].view(-1)]
+            parts = [out["acc_len"], out["finished"], rs.pending, out["last_node"], rb.tree["plan"],
+                     out["acc_tokens"].view(-1)]
             fb = flat_bufs.get((id(rb), id(rs)))
             if fb is None:
                 fb = flat_bufs[(id(rb), id(rs))] = torch.empty(sum(t.numel() for t in parts), dtype=torch.int32,
@@ -257,23 +262,28 @@ class FlashMedusaDecoder:
                 account(deferred)
                 deferred = None
             torch.cuda.current_stream(dev).synchronize()
-            verify_time += time.time() - tv
+            wall = time.time() - tv
+            phases = [timer[i].elapsed_time(timer[i + 1]) / 1000.0 for i in range(3)] if timed else None
             vals = host.tolist()
             Br = n_active  # outputs are per round row: round row i is state row act_rows[i]
             acc_len = vals[:Br]
             fin = vals[Br:2 * Br]
             pend = vals[2 * Br:3 * Br]
-            plan_dev = vals[3 * Br:3 * Br + 16]
-            toks = vals[3 * Br + 16:]
+            last = vals[3 * Br:4 * Br]
+            plan_dev = vals[4 * Br:4 * Br + 16]
+            toks = vals[4 * Br + 16:]
             # the round's tree as built on the device (adaptive rounds may be smaller)
-            n_tree = plan_dev[10] if nh > 0 else 1
             topk_round = plan_dev[2:2 + plan_dev[1]] if nh > 0 else []
-            stats["total_verify_rounds"] += 1
-            active_batch_sum += n_active
-            tree_node_sum += n_tree
-            tree_plan_last = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
-                              "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
-                              "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa"}
+            n_tree = plan_dev[10] if nh > 0 else 1
+            if nh > 0 and n_tree <= 1 and not cfg.allow_recompute_fallback:
+                # the reference's verify needs a tree cache to extract from (:2881-2882)
+                raise RuntimeError("KV extraction was requested but no tree cache was available")
+            acc.round(n_active, plan.node_budget_per_seq, topk_round, n_tree, last, use_tree, nh, wall, phases)
+            acc.last_plan = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
+                             "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
+                             "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa",
+                             "adaptive_tree": {"topk": list(topk_round)} if adaptive else {},
+                             "nodes_by_head": tree_level_counts(topk_round, n_tree)}
             # what the next round's shape depends on now; the rest after its launch
             pend_before = [pending_host[r] for r in act_rows]
             for i, r in enumerate(act_rows):
@@ -281,39 +291,191 @@ class FlashMedusaDecoder:
                 if fin[i]:
                     active_host[r] = False
                 pending_host[r] = pend[i]
-            deferred = (act_rows, acc_len, toks, dcap, n_tree, pend_before)
+            deferred = (act_rows, acc_len, toks, dcap, pend_before)
         if deferred is not None:
             account(deferred)
-        total_time = time.time() - total_start
-        rounds = max(stats["total_verify_rounds"], 1)
-        decoded = max(stats["total_decoded_token_num"], 1)
-        proposed = max(stats["total_proposed_medusa_tokens"], 1)
-        avg_accept = stats["total_acc_length"] / decoded
+        return acc.result(generated, prefill_time=prefill_time, total_time=time.time() - total_start,
+                          statistical_time=bool(statistical_time), cache_update_mode=cfg.cache_update_mode)
+
+    def _phase_events(self, dev):
+        """Four timing events (graph-capturable) at the round's phase boundaries."""
+        ev = getattr(self, "_timer", None)
+        if ev is None:
+            ev = self._timer = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
+        return ev
+
+
+def tree_level_counts(topk_by_depth, n_nodes: int) -> list[int]:
+    """Nodes per depth below the root of the dense tree with these widths,
+    expanded breadth first and cut at n_nodes (CandidateTree.nodes_by_head,
+    medusa_tree.py:38-45, for the shared topology of a round)."""
+    counts, total, width = [], 1, 1
+    for k in topk_by_depth:
+        width *= int(k)
+        c = min(width, n_nodes - total)
+        if c <= 0:
+            break
+        counts.append(c)
+        total += c
+        width = c
+    return counts
+
+
+def tree_internal_nodes(topk_by_depth, n_nodes: int) -> set[int]:
+    """Node ids with children in that tree (BFS order: a level's nodes with
+    children are its first ceil(children / width) nodes)."""
+    counts = tree_level_counts(topk_by_depth, n_nodes)
+    internal, start = set(), 0
+    level = [1] + counts
+    for d, k in enumerate(topk_by_depth[: len(counts)]):
+        n_par = -(-counts[d] // int(k))
+        internal.update(range(start, start + n_par))
+        start += level[d]
+    return internal
+
+
+class RolloutStats:
+    """The statistics of the reference's generate result dict
+    (flash_medusa_decoder.py:1617-1638 accumulated at :2185-2205, :2220,
+    :2250, :2316-2326, :2860; assembled at :3039-3117), from the per-round
+    outputs the engine reads back: every row of a round shares the tree's
+    topology, so per-tree counts are per-round counts times the active rows."""
+
+    def __init__(self, n_stat_heads: int):
+        self.nodes_by_head = [0] * n_stat_heads
+        self.rounds = 0
+        self.c = dict(total_acc_length=0, total_decoded_token_num=0, total_verify_rounds=0,
+                      total_correction_tokens=0, total_accepted_medusa_tokens=0, total_proposed_medusa_tokens=0)
+        self.active_batch_sum = 0
+        self.tree_node_sum = 0.0
+        self.tree_budget_unused = 0
+        self.tree_query_rows = 0
+        self.tree_lm_head_rows = 0
+        self.extract_ok = 0
+        self.extract_fallback = 0
+        self.accept_hist: dict[int, int] = {}
+        self.accept_by_depth: dict[int, int] = {}
+        self.proposed_by_depth: dict[int, int] = {}
+        self.layouts: dict[str, int] = {}
+        self.last_plan: dict = {}
+        self.n_tree_round: list[int] = []
+        # timings: host wall time of every round, device phase times of the timed ones
+        self.wall = 0.0
+        self.wall_timed = 0.0
+        self.phase = [0.0, 0.0, 0.0]
+        self.sampled = [0.0, 0.0, 0.0]
+        self.samples = 0
+
+    def round(self, n_active, budget, topk_round, n_tree, last_nodes, use_tree, nh, wall, phases):
+        self.rounds += 1
+        self.c["total_verify_rounds"] += 1
+        self.active_batch_sum += n_active
+        self.tree_node_sum += n_tree
+        self.n_tree_round.append(n_tree)
+        if use_tree:
+            self.layouts["configured"] = self.layouts.get("configured", 0) + n_active
+        counts = tree_level_counts(topk_round, n_tree)
+        for h, c in enumerate(counts[: len(self.nodes_by_head)]):
+            self.nodes_by_head[h] += c * n_active
+        for d, c in enumerate(counts):
+            self.proposed_by_depth[d + 2] = self.proposed_by_depth.get(d + 2, 0) + c * n_active
+        self.tree_budget_unused += max(0, int(budget) - n_tree) * n_active
+        if nh > 0 and n_tree > 1:
+            # a tree verify ran: query rows, packed internal-node logits and
+            # the leaf rows whose next logits the lm_head recomputes
+            internal = tree_internal_nodes(topk_round, n_tree)
+            self.tree_query_rows += n_active * n_tree
+            self.tree_lm_head_rows += n_active * len(internal) + sum(1 for n in last_nodes if n not in internal)
+            self.extract_ok += 1
+        elif nh > 0:
+            self.extract_fallback += 1
+        self.wall += wall
+        if phases is not None:
+            self.samples += 1
+            self.wall_timed += wall
+            for i in range(3):
+                self.sampled[i] += phases[i]
+
+    def rows(self, acc_len, pend_before):
+        n_tree = self.n_tree_round.pop(0)
+        for a, p in zip(acc_len, pend_before):
+            if p >= 0:
+                self.c["total_correction_tokens"] += 1
+            self.c["total_acc_length"] += a
+            self.c["total_decoded_token_num"] += 1
+            self.c["total_accepted_medusa_tokens"] += max(a - 1, 0)
+            self.c["total_proposed_medusa_tokens"] += max(n_tree - 1, 0)
+            self.accept_hist[a] = self.accept_hist.get(a, 0) + 1
+            for d in range(2, a + 1):
+                self.accept_by_depth[d] = self.accept_by_depth.get(d, 0) + 1
+
+    def result(self, generated, *, prefill_time, total_time, statistical_time, cache_update_mode) -> dict:
+        c = self.c
+        rounds = max(c["total_verify_rounds"], 1)
+        decoded = max(c["total_decoded_token_num"], 1)
+        proposed = max(c["total_proposed_medusa_tokens"], 1)
+        avg_accept = c["total_acc_length"] / decoded
+        if statistical_time:
+            head_t, verify_t, update_t = self.sampled
+        else:
+            # the rounds' wall time, split by the sampled rounds' phase shares
+            tot = sum(self.sampled)
+            share = [x / tot for x in self.sampled] if tot > 0 else [0.0, 1.0, 0.0]
+            head_t, verify_t, update_t = (self.wall * x for x in share)
+        nbh = self.nodes_by_head
         total_tokens = sum(len(g) for g in generated)
         return {
             "generated_token_ids": generated,
             "max_sequence_length": max((len(g) for g in generated), default=0),
-            **stats,
+            **c,
             "average_accept_length": float(avg_accept),
             "accepted_tokens_per_medusa_step": float(avg_accept),
-            "total_accepted_draft_tokens": stats["total_accepted_medusa_tokens"],
-            "total_proposed_draft_tokens": stats["total_proposed_medusa_tokens"],
-            "correction_token_rate": stats["total_correction_tokens"] / decoded,
-            "draft_acceptance_rate": stats["total_accepted_medusa_tokens"] / proposed,
-            "medusa_acceptance_rate": stats["total_accepted_medusa_tokens"] / proposed,
-            "average_active_batch_size": active_batch_sum / rounds,
-            "average_tree_nodes_per_seq": tree_node_sum / rounds,
-            "accept_length_histogram": accept_hist,
-            "medusa_accept_by_depth": accept_by_depth,
-            "last_tree_plan": tree_plan_last,
-            "cache_update_mode": cfg.cache_update_mode,
-            "kv_extraction_success_count": stats["total_verify_rounds"],
-            "kv_extraction_fallback_count": 0,
+            "total_accepted_draft_tokens": c["total_accepted_medusa_tokens"],
+            "total_proposed_draft_tokens": c["total_proposed_medusa_tokens"],
+            "correction_token_rate": c["total_correction_tokens"] / decoded,
+            "draft_acceptance_rate": c["total_accepted_medusa_tokens"] / proposed,
+            "medusa_acceptance_rate": c["total_accepted_medusa_tokens"] / proposed,
+            "average_active_batch_size": self.active_batch_sum / rounds,
+            "average_tree_nodes_per_seq": self.tree_node_sum / rounds,
+            "tree_active_heads": max((i + 1 for i, n in enumerate(nbh) if n > 0), default=0),
+            "tree_nodes_head1": nbh[0] if nbh else 0,
+            "tree_nodes_head2": nbh[1] if len(nbh) > 1 else 0,
+            "tree_nodes_head3": nbh[2] if len(nbh) > 2 else 0,
+            "tree_total_nodes": sum(nbh) + c["total_decoded_token_num"],
+            "tree_budget_unused": self.tree_budget_unused,
+            "tree_query_rows": self.tree_query_rows,
+            "tree_lm_head_rows": self.tree_lm_head_rows,
+            "tree_lm_head_row_ratio": self.tree_lm_head_rows / max(self.tree_query_rows, 1),
+            "accept_length_histogram": self.accept_hist,
+            "medusa_accept_by_depth": self.accept_by_depth,
+            "medusa_proposed_by_depth": self.proposed_by_depth,
+            "last_tree_plan": self.last_plan,
+            "actual_tree_layout_counts": self.layouts,
+            # the head-3 gate statistics exist only with the Reflex/HRDCR manager
+            "head3_conditional_path_acceptance": 0.0,
+            "head3_conditional_path_success": 0,
+            "head3_conditional_path_opportunities": 0,
+            "cache_update_mode": cache_update_mode,
+            "kv_extraction_success_count": self.extract_ok,
+            "kv_extraction_fallback_count": self.extract_fallback,
+            "kv_extraction_time": update_t,
+            "recompute_fallback_time": 0.0,
             "oom_count": 0,
             "total_time_cost": total_time,
             "prefill_time_cost": prefill_time,
-            "tree_verify_time_cost": verify_time,
-            "target_time_cost": prefill_time + verify_time,
+            "target_time_cost": prefill_time + verify_t + update_t,
+            "tree_verify_time_cost": verify_t,
+            "cache_update_time_cost": update_t,
+            "medusa_head_time_cost": head_t,
+            "sampled_medusa_head_cuda_time_s": self.sampled[0],
+            "sampled_tree_verify_cuda_time_s": self.sampled[1],
+            "timing_sample_count": self.samples,
+            "draft_time_cost": head_t,
+            "check_time_cost": 0.0,
             "tokens_per_sec_generation": total_tokens / max(total_time, 1e-9),
             "reflex_metrics": {"enabled": False},
+            "reflex_head_metrics": {},
+            "reflex_aux_records": {},
+            "persistent_memory_feedback": {},
+            "motivation_trace": [],
         }

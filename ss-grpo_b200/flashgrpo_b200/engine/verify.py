@@ -600,7 +600,9 @@ class VerifyEngine:
             torch.addmm(rb.h, rb.act, lw["w_down"].t(), out=rb.h)
         ops.rmsnorm(rb.h, w.final_norm, sp.eps, out=rb.tree_hidden.view(B * N_, -1))
 
-    def accept(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig):
+    def accept(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig, phase_event=None):
+        """Internal-node logits, then K4.  phase_event (optional) is recorded
+        between the two: the end of the verify phase."""
         B = st.B
         if rb.n_int > 0:
             if rb.adaptive:
@@ -612,6 +614,8 @@ class VerifyEngine:
                 torch.where(rb.j_int < B * ni, idx, torch.zeros_like(idx), out=rb.int_idx)
             ops.gather_rows(rb.tree_hidden.view(B * rb.N, -1), rb.int_idx, out=rb.hid_int)
             torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
+        if phase_event is not None:
+            phase_event.record()
         rb.corr_used += (st.pending >= 0).sum()
         outs = dict(rb.out)
         outs["pending"] = st.pending
@@ -635,17 +639,25 @@ class VerifyEngine:
             self._graphs[key] = v
         return v
 
-    def run_round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None):
+    def run_round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None,
+                  phase_events=None):
         """All device work of one round, enqueued on the current stream.  st is
-        a DecodeState or a RoundView (gathered before, scattered after)."""
+        a DecodeState or a RoundView (gathered before, scattered after).
+        phase_events (optional): four timing events recorded at the start,
+        after the proposal and tree build, after the verify forward and the
+        internal-node lm_head, and after acceptance + extraction."""
         if isinstance(st, RoundView):
             st.gather()
-            self._round(st, rb, params, cfg, attn_events)
+            self._round(st, rb, params, cfg, attn_events, phase_events)
             st.scatter()
         else:
-            self._round(st, rb, params, cfg, attn_events)
+            self._round(st, rb, params, cfg, attn_events, phase_events)
 
-    def _round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None):
+    def _round(self, st, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig, attn_events=None,
+               phase_events=None):
+        ev = phase_events or [None] * 4
+        if ev[0] is not None:
+            ev[0].record()
         if cfg.chain:
             self.propose_chain(st, rb, cfg)
             self.build_tree(st, rb, params)
@@ -654,19 +666,24 @@ class VerifyEngine:
         else:
             self.propose(st, rb, cfg)
             self.build_tree(st, rb, params)
+        if ev[1] is not None:
+            ev[1].record()
         self.verify_forward(st, rb, cfg, attn_events)
-        self.accept(st, rb, cfg)
+        self.accept(st, rb, cfg, phase_event=ev[2])
+        if ev[3] is not None:
+            ev[3].record()
 
     # --------------------------------------------------------------- graphs
     def graph_round(self, st: DecodeState, rb: RoundBuffers, params: N.PlanParams, cfg: RoundConfig,
-                    pool=None, attn_events=None) -> torch.cuda.CUDAGraph:
+                    pool=None, attn_events=None, phase_events=None) -> torch.cuda.CUDAGraph:
         """Captures run_round for this (state, buffers, plan); replay() runs it.
-        attn_events must be created with external=True to be captured."""
+        attn_events / phase_events must be created with external=True to be
+        captured."""
         self._attn_workspace(rb, st, cfg.attn_splits)
         M = (rb.n_heads + 1) * st.B
         if self._fused_lm_head(cfg, M):
             self._lm_head_ws(M, st.B, rb.kmax)  # allocated outside the capture
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, pool=pool):
-            self.run_round(st, rb, params, cfg, attn_events)
+            self.run_round(st, rb, params, cfg, attn_events, phase_events)
         return g

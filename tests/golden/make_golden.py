@@ -30,7 +30,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("FG_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("FG_REFERENCE_ROOT"):
+    sys.exit("set FG_REFERENCE_ROOT to the root of the ihbkaiser/ss-GRPO source tree")
+REF = Path(os.environ["FG_REFERENCE_ROOT"])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REPO))
 
@@ -62,6 +64,9 @@ class _StableTorch:
 
 
 ref_tree.torch = _StableTorch()
+# the chain proposal's per-parent top-k (flash_medusa_decoder.py:1203) takes
+# the same stable rule; the decoder's only other topk (:1028) reads values only
+ref_dec.torch = _StableTorch()
 
 
 def _bf16_logits(g, shape, scale=1.0):
@@ -265,11 +270,14 @@ class _CallOrderRefSampler:
         self.calls = 0
 
     def __call__(self, logits, *, do_sample=True, temperature=1.0, top_p=1.0, top_k=None, nucleus_topk_hint=2048):
-        assert top_k is None and (top_p is None or top_p >= 1.0)
+        assert top_k is None
         x = logits.detach().float().numpy()
         u = np.array([native.uniform(self.seed, k, self.calls, 0) for k in range(x.shape[0])], dtype=np.float32)
         self.calls += 1
-        return torch.from_numpy(native.sample_rows(x, u, do_sample=do_sample, temperature=temperature).astype(np.int64))
+        # top_p < 1: the fg-icdf-v1n draw from the nucleus kept set
+        p = 1.0 if top_p is None else float(top_p)
+        return torch.from_numpy(native.sample_rows(x, u, do_sample=do_sample, temperature=temperature,
+                                                   top_p=p).astype(np.int64))
 
 
 def gen_generate():
@@ -282,20 +290,37 @@ def gen_generate():
         "adaptive": dict(tree_mode="concurrency_aware", cpeak_nodes=128, fixed_tree_topk_by_depth=(8, 8, 8),
                          max_tree_nodes_per_seq=32, max_tree_depth=4, repeats=1, max_new=16, seed=5,
                          adaptive_tree_enabled=True, adaptive_min_topk_by_depth=(2, 2, 2)),
+        # nucleus draws at the reference's default top_p
+        "nucleus_095": dict(tree_mode="fixed", fixed_tree_topk_by_depth=(4, 2, 2), max_tree_nodes_per_seq=16,
+                            max_tree_depth=4, repeats=1, max_new=20, seed=5, top_p=0.95),
+        # chain proposals (_build_chain_batch_trees, :1141-1261) through the
+        # ChainDraftCell, with the first state from MEDUSA head 1 and from the cell
+        "chain_boot": dict(tree_mode="fixed", fixed_tree_topk_by_depth=(3, 2, 2), max_tree_nodes_per_seq=16,
+                           max_tree_depth=4, repeats=1, max_new=20, seed=13, proposal_mode="chain",
+                           chain_bootstrap_from_medusa=True),
+        "chain_noboot": dict(tree_mode="fixed", fixed_tree_topk_by_depth=(2, 2), max_tree_nodes_per_seq=7,
+                             max_tree_depth=3, repeats=2, max_new=16, seed=17, proposal_mode="chain",
+                             chain_bootstrap_from_medusa=False),
+        "chain_conc_p09": dict(tree_mode="concurrency_aware", cpeak_nodes=64, fixed_tree_topk_by_depth=(4, 3, 2),
+                               max_tree_nodes_per_seq=16, max_tree_depth=4, repeats=2, max_new=16, seed=19,
+                               proposal_mode="chain", chain_bootstrap_from_medusa=True, top_p=0.9),
     }
     model = synth.build_model(1)
-    head_state = synth.medusa_head_tensors(1)
-    heads = MedusaHeads(256, 4096, 3, tie_lm_head=True)
-    missing = heads.load_state_dict(head_state, strict=False)
-    assert not missing.unexpected_keys
     ids, mask = synth.random_prompts(4, 128, 4096, seed=0)
     for name, r in runs.items():
+        chain = r.get("proposal_mode", "medusa") == "chain"
+        head_state = synth.medusa_head_tensors(1, chain=chain)
+        heads = MedusaHeads(256, 4096, 3, tie_lm_head=True)
+        missing = heads.load_state_dict(head_state, strict=False)
+        assert not missing.unexpected_keys
         cfg = ref_dec.FlashMedusaConfig(
             num_medusa_heads=3, tree_mode=r["tree_mode"], cpeak_nodes=r.get("cpeak_nodes", 512),
             max_tree_nodes_per_seq=r["max_tree_nodes_per_seq"], max_tree_depth=r["max_tree_depth"],
-            fixed_tree_topk_by_depth=r["fixed_tree_topk_by_depth"], temperature=1.0, top_p=1.0,
+            fixed_tree_topk_by_depth=r["fixed_tree_topk_by_depth"], temperature=1.0, top_p=r.get("top_p", 1.0),
             adaptive_tree_enabled=r.get("adaptive_tree_enabled", False),
             adaptive_min_topk_by_depth=r.get("adaptive_min_topk_by_depth", (1, 1, 1)),
+            proposal_mode=r.get("proposal_mode", "medusa"),
+            chain_bootstrap_from_medusa=r.get("chain_bootstrap_from_medusa", True),
             allow_recompute_fallback=False,
         )
         sampler = _CallOrderRefSampler(r["seed"])
@@ -311,8 +336,13 @@ def gen_generate():
         keep = ("generated_token_ids", "total_acc_length", "average_accept_length", "total_decoded_token_num",
                 "total_verify_rounds", "total_correction_tokens", "total_accepted_medusa_tokens",
                 "total_proposed_medusa_tokens", "kv_extraction_success_count", "kv_extraction_fallback_count")
+        # every deterministic statistic (counts, histograms, plans; not the
+        # timings) and the full key set, which the drop-in's result must cover
+        stats = {k: v for k, v in res.items() if k not in keep and "time" not in k and not k.startswith("sampled_")
+                 and k not in ("reflex_metrics", "reflex_head_metrics", "reflex_aux_records", "motivation_trace",
+                               "persistent_memory_feedback", "last_tree_plan")}
         results[name] = {"run": {k: (list(v) if isinstance(v, tuple) else v) for k, v in r.items()},
-                         **{k: res[k] for k in keep}}
+                         **{k: res[k] for k in keep}, "stats": stats, "result_keys": sorted(res)}
     (HERE / "generate_cfg1.json").write_text(json.dumps(results))
 
 

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import cuda_available
+from conftest import compare_stats, cuda_available
 from oracle import native as orc
 from oracle import reference_path as rp
 
@@ -81,6 +81,11 @@ def test_generate_config1_matches_oracle(run):
     for k in ("total_acc_length", "total_decoded_token_num", "total_verify_rounds", "total_correction_tokens",
               "total_accepted_medusa_tokens", "total_proposed_medusa_tokens"):
         assert res[k] == ref[k], k
+    # the rest of the reference's result statistics (tree rows, histograms, rates)
+    want = {k: v for k, v in ref.items() if k not in ("generated_token_ids", "prefill_time", "round_times")}
+    compare_stats(res, want)
+    assert res["timing_sample_count"] >= 1 and res["sampled_tree_verify_cuda_time_s"] > 0
+    assert res["kv_extraction_success_count"] == res["total_verify_rounds"]
     if run.get("adaptive"):
         # the confidences did shrink some trees below the base plan
         base = rp.plan_tree(active_batch_size=ids.shape[0] * run["repeats"], num_medusa_heads=3,

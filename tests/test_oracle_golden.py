@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 import torch
 
+from conftest import compare_stats
 from oracle import native
 from oracle import reference_path as rp
 
@@ -368,28 +369,46 @@ def test_planner_matches_reference_fixture(golden_dir):
 
 
 # --------------------------------------------------------------- generate
-@pytest.mark.parametrize("name", ["fixed_422", "conc_rep2", "adaptive"])
-def test_generate_matches_reference_config1(golden_dir, name):
+GENERATE_RUNS = ["fixed_422", "conc_rep2", "adaptive", "nucleus_095", "chain_boot", "chain_noboot",
+                 "chain_conc_p09"]
+
+
+def oracle_generate_run(r: dict):
+    """The oracle's generate on config 1 for a fixture run description."""
     from flashgrpo_b200.utils import synthetic
 
-    d = json.loads((golden_dir / "generate_cfg1.json").read_text())[name]
-    r = d["run"]
+    chain = r.get("proposal_mode", "medusa") == "chain"
     model = synthetic.build_model(1)
-    st = synthetic.medusa_head_tensors(1)
+    st = synthetic.medusa_head_tensors(1, chain=chain)
     heads = [{"norm_w": st[f"heads.{i}.norm.weight"], "norm_b": st[f"heads.{i}.norm.bias"],
               "fc_w": st[f"heads.{i}.fc.weight"], "fc_b": st[f"heads.{i}.fc.bias"]} for i in range(3)]
+    cell = {k[len("chain_cell."):]: v for k, v in st.items() if k.startswith("chain_cell.")} if chain else None
     ids, mask = synthetic.random_prompts(4, 128, 4096, seed=0)
     if r["repeats"] > 1:
         ids, mask = ids[:2], mask[:2]
     cfg = rp.OracleConfig(tree_mode=r["tree_mode"], cpeak_nodes=r.get("cpeak_nodes", 512),
                           max_tree_nodes_per_seq=r["max_tree_nodes_per_seq"], max_tree_depth=r["max_tree_depth"],
                           fixed_tree_topk_by_depth=tuple(r["fixed_tree_topk_by_depth"]),
+                          top_p=r.get("top_p", 1.0),
                           adaptive_tree_enabled=r.get("adaptive_tree_enabled", False),
-                          adaptive_min_topk_by_depth=tuple(r.get("adaptive_min_topk_by_depth", (1, 1, 1))))
-    res = rp.generate(model, heads, ids, mask, cfg, rp.CallOrderSampler(r["seed"]), repeats=r["repeats"],
-                      max_length=128 + r["max_new"])
+                          adaptive_min_topk_by_depth=tuple(r.get("adaptive_min_topk_by_depth", (1, 1, 1))),
+                          proposal_mode=r.get("proposal_mode", "medusa"), chain_cell=cell,
+                          chain_bootstrap_from_medusa=r.get("chain_bootstrap_from_medusa", True))
+    return rp.generate(model, heads, ids, mask, cfg, rp.CallOrderSampler(r["seed"]), repeats=r["repeats"],
+                       max_length=128 + r["max_new"])
+
+
+@pytest.mark.parametrize("name", GENERATE_RUNS)
+def test_generate_matches_reference_config1(golden_dir, name):
+    """The oracle's generate loop against the reference's own
+    FlashMedusaDecoder.generate (stable top-k, fg-icdf-v1/v1n draws
+    substituted), for MEDUSA and chain proposals, nucleus draws and adaptive
+    widths: tokens and every deterministic statistic of the result dict."""
+    d = json.loads((golden_dir / "generate_cfg1.json").read_text())[name]
+    res = oracle_generate_run(d["run"])
     assert res["generated_token_ids"] == d["generated_token_ids"]
     for k in ("total_acc_length", "total_decoded_token_num", "total_verify_rounds", "total_correction_tokens",
               "total_accepted_medusa_tokens", "total_proposed_medusa_tokens"):
         assert res[k] == d[k], k
     assert math.isclose(res["average_accept_length"], d["average_accept_length"])
+    compare_stats(res, d["stats"])

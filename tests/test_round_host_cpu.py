@@ -172,3 +172,54 @@ def test_new_entry_point_wrappers_check_their_buffers(monkeypatch):
     assert calls[-1] == ("fg_gate_up_silu", None)
     with pytest.raises(ValueError):
         ops.gate_up_silu(xt, wgu, out=torch.zeros(7, 255, dtype=bf))
+
+
+def test_round_tree_statistics_match_dense_topology():
+    """The per-round tree counts the decoder derives from the device plan
+    (widths, node count) equal those of the BFS tree itself: nodes per depth
+    (CandidateTree.nodes_by_head) and the nodes that have children."""
+    from flashgrpo_b200.decoding.flash_medusa_decoder import tree_internal_nodes, tree_level_counts
+
+    for widths in ([4, 2], [4, 3, 2], [3, 2, 2], [8], [2, 2, 2, 2, 2], [1, 1, 1], [5, 4], [4, 1, 3]):
+        for budget in range(1, 70):
+            plan = TreePlan(budget, len(widths), list(widths), budget, "fixed")
+            parents, depths = dense_topology(plan)
+            n = len(parents)
+            want_counts = [sum(1 for d in depths if d == dd) for dd in range(2, max(depths) + 1)]
+            assert tree_level_counts(widths, n) == want_counts, (widths, budget)
+            assert tree_internal_nodes(widths, n) == set(internal_nodes(parents)), (widths, budget)
+
+
+def test_result_dict_covers_the_reference_keys(golden_dir):
+    """generate()'s result carries every key the reference's result dict has
+    (flash_medusa_decoder.py:3039-3117, recorded in the generate fixtures),
+    assembled here from synthetic per-round outputs without a GPU."""
+    import json
+
+    from flashgrpo_b200.decoding.flash_medusa_decoder import RolloutStats
+
+    ref_keys = set()
+    for run in json.loads((golden_dir / "generate_cfg1.json").read_text()).values():
+        ref_keys |= set(run["result_keys"])
+    acc = RolloutStats(3)
+    acc.round(4, 16, [4, 2], 13, [0, 1, 5, 0], True, 2, 0.01, [0.001, 0.006, 0.002])
+    acc.rows([1, 2, 3, 1], [-1, 7, -1, -1])
+    acc.round(4, 16, [4, 2], 13, [0, 0, 0, 0], True, 2, 0.01, None)
+    acc.rows([1, 1, 1, 1], [-1, -1, 3, -1])
+    res = acc.result([[1], [2, 3], [4, 5, 6], [7]], prefill_time=0.5, total_time=1.0, statistical_time=False,
+                     cache_update_mode="extract_path")
+    assert ref_keys - set(res) == set()
+    assert res["tree_query_rows"] == 2 * 4 * 13
+    # 5 internal nodes per tree; row 3's last node (5) is a leaf in round 1
+    assert res["tree_lm_head_rows"] == 2 * 4 * 5 + 1
+    assert res["tree_nodes_head1"] == 2 * 4 * 4 and res["tree_nodes_head2"] == 2 * 4 * 8
+    assert res["tree_total_nodes"] == 2 * 4 * 12 + 8
+    assert res["medusa_proposed_by_depth"] == {2: 32, 3: 64}
+    assert res["accept_length_histogram"] == {1: 6, 2: 1, 3: 1}
+    assert res["medusa_accept_by_depth"] == {2: 2, 3: 1}
+    assert res["total_correction_tokens"] == 2 and res["timing_sample_count"] == 1
+    assert res["actual_tree_layout_counts"] == {"configured": 8}
+    # without statistical_time the wall time (0.02 s) is split by the sampled shares
+    assert abs(res["tree_verify_time_cost"] - 0.02 * 6 / 9) < 1e-12
+    assert abs(res["medusa_head_time_cost"] + res["tree_verify_time_cost"] + res["cache_update_time_cost"]
+               - 0.02) < 1e-12
