@@ -57,8 +57,11 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-splits", type=int, default=0)
-    ap.add_argument("--lm-head", choices=["fused", "separate"], default="fused",
+    ap.add_argument("--lm-head", choices=["fused", "separate"], default="separate",
                     help="proposal lm_head: tcgen05 GEMM with fused top-k, or cuBLAS + row top-k")
+    ap.add_argument("--dense", choices=["auto", "native", "cublas"], default="auto",
+                    help="verify projections + internal lm_head: per shape the faster of fg_linear and cuBLAS, "
+                         "fg_linear (tcgen05) always, or cuBLAS")
     return ap.parse_args()
 
 
@@ -90,14 +93,17 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
+        import tempfile
+
         self.gpu = gpu_index
         self.proc = None
         self.window = None
-        self.path = REPO / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+        fd, name = tempfile.mkstemp(prefix=f"fg_clocks_gpu{gpu_index}_", suffix=".csv")
+        os.close(fd)
+        self.path = Path(name)
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.fh,
@@ -151,7 +157,26 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- workload
-def config2_decoder(device, layers=None, attn_splits=0, lm_head="fused"):
+def config2_plan(rows: int):
+    """The config-2 tree plan for `rows` rollouts on one GPU (host planner)."""
+    from flashgrpo_b200.decoding.medusa_tree import dense_topology, plan_tree
+
+    plan = plan_tree(active_batch_size=rows, num_medusa_heads=3, tree_mode="concurrency_aware", cpeak_nodes=1024,
+                     min_tree_nodes_per_seq=1, max_tree_nodes_per_seq=16, max_tree_depth=4,
+                     fixed_tree_topk_by_depth=[4, 3, 2])
+    return plan, len(dense_topology(plan)[0])
+
+
+def workload_config(rows: int, prefix: int, layers: int, world: int) -> dict:
+    """The `config` object both arms print: the workload, not the engine."""
+    plan, n_nodes = config2_plan(rows)
+    return {"workload": WORKLOAD, "rollouts_per_gpu": rows, "prompts_per_gpu": max(1, rows // 8),
+            "samples_per_prompt": 8, "prefix_tokens": prefix, "tree": list(plan.topk_by_depth),
+            "tree_nodes": n_nodes, "layers": layers, "medusa_heads": 3, "active_heads": plan.active_heads,
+            "temperature": 1.0, "top_p": 1.0, "parallelism": f"dp{world} (rollouts sharded by prompt group)"}
+
+
+def config2_decoder(device, layers=None, attn_splits=0, lm_head="separate", dense="auto"):
     import torch
 
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -168,7 +193,7 @@ def config2_decoder(device, layers=None, attn_splits=0, lm_head="fused"):
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode="concurrency_aware", cpeak_nodes=1024,
                             max_tree_nodes_per_seq=16, max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2),
                             temperature=1.0, top_p=1.0, sampling_seed=1234, attention_splits=attn_splits,
-                            lm_head_kernel=lm_head)
+                            lm_head_kernel=lm_head, dense_kernel=dense)
     torch.cuda.synchronize()
     return FlashMedusaDecoder(model, heads, Tok(), cfg)
 
@@ -215,7 +240,7 @@ def run_ours(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     torch.manual_seed(0)
-    dec = config2_decoder(device, args.layers, args.attn_splits, args.lm_head)
+    dec = config2_decoder(device, args.layers, args.attn_splits, args.lm_head, args.dense)
     eng = dec.engine
     spec = eng.spec
     # the global batch is world x prompts prompt groups; this rank owns a
@@ -324,7 +349,7 @@ def run_ours(args, rank, world, local_rank):
                 tok += res["total_acc_length"]
                 rounds_total += res["total_verify_rounds"]
                 pre_s += res["prefill_time_cost"]
-                ver_s += res["tree_verify_time_cost"]
+                ver_s += res["total_time_cost"] - res["prefill_time_cost"]
             torch.cuda.synchronize()
             e_s = shard.reduce_scalar(time.perf_counter() - t0, "max", device)
             tok = int(shard.reduce_scalar(tok, "sum", device))
@@ -340,11 +365,10 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": accepted_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids",
-        "config": {"workload": WORKLOAD, "rollouts_per_gpu": rows, "prompts_per_gpu": prompts,
-                   "samples_per_prompt": 8, "prefix_tokens": args.prefix, "tree": plan.topk_by_depth,
-                   "tree_nodes": rb.N, "layers": spec.n_layers, "medusa_heads": 3, "active_heads": plan.active_heads,
-                   "temperature": 1.0, "top_p": 1.0, "lm_head": args.lm_head,
-                   "parallelism": f"dp{world} (rollouts sharded by prompt group)",
+        "config": workload_config(rows, args.prefix, spec.n_layers, world),
+        "engine": {"lm_head": args.lm_head, "dense": args.dense,
+                   "dense_shapes": {f"{k[0]}x{k[1]}x{k[2]}/{['store', 'resid', 'swiglu'][k[3]]}": v
+                                    for k, v in eng.tile_report.items()},
                    "l2": "inputs larger than L2: 3.1 GB weights + KV cache re-read every step",
                    "graphs": "each step replays a captured CUDA graph of the round"},
         "accepted_tokens": accepted_all, "average_accept_length": accepted_all / (K * rows * world),
@@ -371,34 +395,57 @@ def run_ours(args, rank, world, local_rank):
 
 
 # ------------------------------------------------------------- CPU oracle
-def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 8, prefix: int = 256):
-    """The oracle's restatement of the reference generate loop, on the host
-    cores, on a bounded sample of the config-2 workload (fp32, `rows` rollouts
-    of `prefix`-token prompts)."""
+def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 64, prefix: int = 1024):
+    """The oracle's restatement of the reference generate loop on the host
+    cores, on config 2's own shape (fp32): `rows` rollouts (rows / 8 prompts x
+    8 samples) of `prefix`-token uniform-random prompts, the same tree plan
+    (cpeak 1024, at most 16 nodes), HF eager attention with the dense tree
+    mask.  The prefill is not timed; `timed_rounds` verify rounds after
+    `warm_rounds` are."""
     import torch
 
     from oracle import reference_path as rp
     from flashgrpo_b200.utils import synthetic
 
     torch.set_num_threads(os.cpu_count() or 1)
-    model = synthetic.build_model(2, device="cpu", dtype=torch.float32, attn_implementation="eager")
+    model = synthetic.build_model(2, device="cpu", dtype=torch.float32, attn_implementation="eager",
+                                  fast_host_init=True)
     st = synthetic.medusa_head_tensors(2, dtype=torch.float32)
+
+    def synthetic_prefill(model, ids, mask, pos, cache):
+        """The prefix's K/V and hidden states at their shapes (N(0, 1)): the
+        timed verify rounds read them like a prefilled cache, without the
+        minutes a CPU prefill of 8 x 1024 tokens takes."""
+        conf = model.config
+        P, S = ids.shape
+        hkv, D = conf.num_key_value_heads, conf.head_dim
+        g = torch.Generator().manual_seed(5)
+        for layer in range(conf.num_hidden_layers):
+            k = torch.randn(P, hkv, S, D, generator=g)
+            v = torch.randn(P, hkv, S, D, generator=g)
+            cache.update(k, v, layer)
+        return torch.randn(P, S, conf.hidden_size, generator=g), cache
+
     heads = [{"norm_w": st[f"heads.{i}.norm.weight"], "norm_b": st[f"heads.{i}.norm.bias"],
               "fc_w": st[f"heads.{i}.fc.weight"], "fc_b": st[f"heads.{i}.fc.bias"]} for i in range(3)]
-    prompts = max(1, rows // 2)
-    ids, mask = synthetic.random_prompts(prompts, prefix, 151936, seed=7)
-    cfg = rp.OracleConfig(tree_mode="concurrency_aware", cpeak_nodes=1024 * rows // 64, max_tree_nodes_per_seq=16,
-                          max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2))
-    res = rp.generate(model, heads, ids, mask, cfg, rp.SeqRoundSampler(1234), repeats=2,
-                      max_length=prefix + warm_rounds + timed_rounds + 2)
+    prompts = max(1, rows // 8)
+    ids, mask = synthetic.random_prompts(prompts, prefix, 151936, seed=100)
+    cfg = rp.OracleConfig(tree_mode="concurrency_aware", cpeak_nodes=1024, max_tree_nodes_per_seq=16,
+                          max_tree_depth=4, fixed_tree_topk_by_depth=(4, 3, 2), top_p=1.0)
+    t0 = time.perf_counter()
+    res = rp.generate(model, heads, ids, mask, cfg, rp.SeqRoundSampler(1234), repeats=8,
+                      max_length=prefix + warm_rounds + timed_rounds + 2, prefill_fn=synthetic_prefill)
+    wall = time.perf_counter() - t0
     times = res["round_times"][warm_rounds:warm_rounds + timed_rounds]
     sec = sum(t for t, _ in times)
     tok = sum(n for _, n in times)
     return {"value": tok / sec, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{len(times)} verify rounds of {rows} rollouts ({prompts} prompts x 2 samples) with "
-                      f"{prefix}-token prefixes, fp32 on the host; oracle/reference_path.py restatement of the "
-                      "reference generate loop with HF eager attention and the dense tree mask",
-            "seconds": sec}
+            "sample": f"{len(times)} verify rounds (after {warm_rounds} untimed) of config 2's full shape: "
+                      f"{rows} rollouts ({prompts} prompts x 8 samples) with {prefix}-token prefixes, 28 layers, "
+                      "fp32 on the host; oracle/reference_path.py restatement of the reference generate loop "
+                      "with HF eager attention and the dense tree mask; the prefix K/V are synthesized at their "
+                      "shapes instead of a CPU prefill, which no arm times",
+            "seconds": sec, "prefill_s": res["prefill_time"], "wall_s": wall}
 
 
 def main():
@@ -409,12 +456,15 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        W, K = max(args.warmup, 3), max(args.steps, 1)
-        base = cpu_oracle_round_rate(W, K)
+        # config 2's shape on the host, a bounded number of rounds: each
+        # round of 64 rollouts is seconds of fp32 CPU work
+        W, K = min(max(args.warmup, 3), 3), min(max(args.steps, 1), 8)
+        base = cpu_oracle_round_rate(W, K, rows=args.rows, prefix=args.prefix)
         line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
-                "steps": K, "warmup": W, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "steps": K, "warmup": W, "ms_per_step": 1e3 * base["seconds"] / K, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic: random-init weights N(0,0.02), uniform-random prompt ids",
-                "config": {"workload": WORKLOAD, "sample": base["sample"]},
+                "config": workload_config(args.rows, args.prefix, 28, args.gpus),
                 "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
@@ -433,7 +483,7 @@ def main():
             dist.barrier()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_oracle_round_rate(2, 30)
+            result["cpu_baseline"] = cpu_oracle_round_rate(1, 3, rows=args.rows, prefix=args.prefix)
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()

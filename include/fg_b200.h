@@ -307,9 +307,12 @@ fg_status fg_tree_attention(const void *q, int32_t dtype, const fg_kv_layer *kv,
  * reference.  The split-K scratch comes from one fixed array inside the
  * library (FG_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the
  * library until exit); needs beyond it return FG_ECAPACITY.  The first call
- * on a device looks the array up (make it before any stream capture); calls
- * share the array, so calls that overlap on the GPU race.  Allocates
- * nothing. */
+ * on a device looks the array up (make it before any stream capture; after a
+ * cudaDeviceReset of that device the looked-up address is stale); calls
+ * share the array, so calls that overlap on the GPU race.  A bf16 call that
+ * splits the KV range clears the split counters with a memset on the stream
+ * first, so it does not overlap the preceding kernel the way
+ * fg_tree_attention does; fp32 calls need no scratch.  Allocates nothing. */
 #define FG_NOALLOC_SCRATCH_BYTES (32u << 20)
 fg_status fg_tree_attention_noalloc(const void *q, int32_t dtype, const fg_kv_layer *kv, const int32_t *kv_len,
                                     const uint32_t *anc_bits, int32_t B, int32_t n_nodes, int32_t n_q_heads,
@@ -368,6 +371,18 @@ typedef struct fg_accept_args {
      * kv_rows[b] of kv_batch rows; NULL = identity */
     const int32_t *kv_rows;
     int32_t kv_batch;
+    /* Parallel draws (drawn != NULL; shared topology only): before the walk,
+     * one CTA per packed logits row j < internal_rows draws the target token
+     * at internal node internal[j % n_int] of row j / n_int with uniform
+     * u[b][depths[node] - 1] -- the draw the walk would make there -- into
+     * drawn[j]; the walk then reads them.  n_int = plan_out[11] (fg_build_tree's
+     * plan) when plan_out != NULL, else internal_rows / B.  Same tokens as the
+     * sequential walk, with every internal node's draw done at once. */
+    const int32_t *internal;   /* [nmax] node ids with children (fg_build_tree) */
+    const int32_t *depths;     /* [nmax] */
+    const int32_t *plan_out;   /* [16] or NULL */
+    int32_t internal_rows;     /* packed logits rows = grid of the draws */
+    int32_t *drawn;            /* [internal_rows] int32 scratch, or NULL */
 } fg_accept_args;
 
 /* One CTA per row: the exact_target walk of exact_accept_paths_batch
@@ -375,7 +390,9 @@ typedef struct fg_accept_args {
  * EOS / pending-correction rules (flash_medusa_decoder.py:2289-2343), the
  * extract_path compaction of the accepted slots in every layer
  * (flashgrpo_b200/decoding/kv_extraction.py:34-218, on per-row lengths), and
- * current_hidden = tree_hidden[row, last node] (flash_medusa_decoder.py:2829-2835). */
+ * current_hidden = tree_hidden[row, last node] (flash_medusa_decoder.py:2829-2835).
+ * With args->drawn set, a first kernel makes every internal node's draw in
+ * parallel (see fg_accept_args) and the walk reads them. */
 fg_status fg_accept_extract(const fg_accept_args *args, void *stream);
 
 /* Compaction alone, for callers that keep their own tree walk:
@@ -423,6 +440,39 @@ fg_status fg_layernorm(const void *x, const void *weight, const void *bias, int3
  * _forward_decoder (flashgrpo_b200/models/qwen_flashgrpo_wrapper.py:150-186). */
 fg_status fg_gate_up_silu(const void *x, int32_t dtype, int32_t T, int32_t H, const void *w_gate_up, int32_t I,
                           void *act, void *stream);
+/* The verify forward's dense projections on the tensor cores with their
+ * consumer fused into the epilogue: D = x w^T for x [M, K] (tokens) and
+ * w [N, K] (nn.Linear layout), bf16 with contiguous rows, fp32 accumulation:
+ *   FG_EPI_STORE   out = bf16(D + bias)           (bias nullable)
+ *   FG_EPI_RESID   out = bf16(resid + D + bias)   (resid may equal out)
+ *   FG_EPI_SWIGLU  out = bf16(bf16(silu(bf16(g))) * bf16(u)) with g, u the
+ *                  rows j and N + j of w ([2N, K]); no bias
+ * out / resid rows are ld_out / ld_resid elements apart (multiples of 8).
+ * Replaces the addmm / mm projections of the HF Qwen2 / Llama layers inside
+ * _forward_decoder (flashgrpo_b200/models/qwen_flashgrpo_wrapper.py:150-186:
+ * q/k/v_proj with bias, o_proj + residual, gate/up + act_fn, down_proj +
+ * residual) and the lm_head of the packed internal tree nodes
+ * (_project_packed_tree_logits, flashgrpo_b200/decoding/flash_medusa_decoder.py:
+ * 1120-1139).  Tiles of bm tokens (128, or 256 as two 128-token MMAs
+ * sharing each weight box) x bn outputs (a multiple of 16, at most 256; the
+ * epilogue's TMEM reads must fit the tile's accumulator, FG_EINVAL
+ * otherwise) with the k range cut into `splits` parts (split-K), through a
+ * ring of `stages` 64-wide k chunks; any of bm / bn / splits / stages <= 0 is
+ * chosen from the shape.  splits > 1 writes fp32 partials to workspace
+ * (fg_linear_workspace_size bytes for the same bm / bn / splits: splits x M x
+ * N floats, 2N for SwiGLU) and a second kernel adds them in k order and
+ * applies the epilogue.  K a multiple of 64, N a multiple of 8 (of bn for
+ * SwiGLU); dtype FG_DTYPE_BF16 only.  Launched as a programmatic dependent
+ * of the preceding kernel: it fetches weights before waiting for it. */
+#define FG_EPI_STORE 0
+#define FG_EPI_RESID 1
+#define FG_EPI_SWIGLU 2
+size_t fg_linear_workspace_size(int32_t M, int32_t N, int32_t K, int32_t epilogue, int32_t bm, int32_t bn,
+                                int32_t splits);
+fg_status fg_linear(const void *x, int32_t dtype, int32_t M, int32_t K, const void *w, int32_t N, const void *bias,
+                    const void *resid, int64_t ld_resid, void *out, int64_t ld_out, int32_t epilogue, int32_t bm,
+                    int32_t bn, int32_t splits, int32_t stages, void *workspace, size_t workspace_bytes,
+                    void *stream);
 /* out[r, :I] = silu(gu[r, :I]) * gu[r, I:2I] (SwiGLU of the MLP). */
 fg_status fg_silu_mul(const void *gu, int32_t dtype, int32_t n_rows, int32_t inter, void *out, void *stream);
 /* out = x + silu(y) (residual of MedusaPredictionHead.project_hidden,

@@ -498,12 +498,15 @@ def project_heads(heads, hidden, n_heads):
 
 @torch.no_grad()
 def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler, *, repeats=1, max_length=2048,
-             pad_token_id=0, eos_token_id=1, record=None):
+             pad_token_id=0, eos_token_id=1, record=None, prefill_fn=None):
     """Restatement of FlashMedusaDecoder.generate (Reflex off, MEDUSA proposal,
     exact_target acceptance, extract_path cache update, CPU fp32).
 
     ``heads`` is a list of dicts with norm_w, norm_b, fc_w, fc_b tensors.
     ``record`` (a list) receives one RoundRecord per verify round.
+    ``prefill_fn(model, input_ids, attention_mask, pos, cache) -> (hidden,
+    cache)`` replaces the model's prefill forward (host timing runs that only
+    need the prefix's shape use it to skip a long CPU prefill).
     """
     import time
 
@@ -512,7 +515,7 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
     lm_w = model.lm_head.weight
     # prefill (wrapper.py:189-199): positions from the mask, fresh cache
     pos = (attention_mask.long().cumsum(-1) - 1).masked_fill(attention_mask == 0, 0)
-    hid, cache = _run_model(model, input_ids, attention_mask, pos, _new_cache(model))
+    hid, cache = (prefill_fn or _run_model)(model, input_ids, attention_mask, pos, _new_cache(model))
     if bool((attention_mask[:, -1] == 1).all()):
         cur_hidden = hid[:, -1, :]
     else:

@@ -67,6 +67,7 @@ struct AcceptParams {
     int32_t hidden_elem_bytes;
     const int32_t* kv_rows;  // row -> cache row for the compaction (NULL = identity)
     int32_t kv_batch;
+    const int32_t* drawn;    // parallel draws per packed logits row (NULL = draw during the walk)
 };
 
 // g_fg_error_word is defined in fg_abi.cu (same translation unit).
@@ -155,11 +156,17 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
             __syncthreads();
             break;
         }
-        const T* row = static_cast<const T*>(p.logits) + (int64_t)srow * p.logits_row_stride;
-        const float u = p.uniforms[(int64_t)b * p.u_stride + step];
-        const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
-        const int32_t drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
-                                      : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+        int32_t drawn;
+        if (p.drawn) {
+            // drawn by draw_internal_kernel at this node with this step's uniform
+            drawn = p.drawn[srow];
+        } else {
+            const T* row = static_cast<const T*>(p.logits) + (int64_t)srow * p.logits_row_stride;
+            const float u = p.uniforms[(int64_t)b * p.u_stride + step];
+            const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
+            drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
+                            : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+        }
         if (tid == 0) s_match = 0x7fffffff;
         __syncthreads();
         for (int32_t j = s_child + tid; j < n; j += blockDim.x)
@@ -226,6 +233,44 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
         if (p.update_len) p.row_len[b] = len0 + a;
         if (fin && p.active != nullptr) p.active[b] = 0;
     }
+}
+
+// The walk's target draws, all at once: the draw at internal node n of row b
+// uses logits row slot[b][n] and uniform u[b][depth(n) - 1] -- the step at
+// which the walk stands on n -- so every internal node's draw is fixed
+// before the walk and they run in parallel, one CTA per packed logits row
+// (row j = b * n_int + rank, node internal[rank]; n_int from the tree's plan
+// on the device when plan_out is set).  The walk then only reads them.
+template <typename T>
+__global__ void __launch_bounds__(FG_SAMPLE_LANES) draw_internal_kernel(AcceptParams p, int32_t B,
+                                                                        const int32_t* internal, const int32_t* depths,
+                                                                        const int32_t* plan_out, int32_t n_int_static,
+                                                                        int32_t* drawn) {
+    __shared__ SampleSmem sm;
+    __shared__ NucleusSmem ns;
+    const int32_t n_int = plan_out ? plan_out[11] : n_int_static;
+    const int32_t j = blockIdx.x;
+    if (n_int <= 0 || j >= B * n_int) return;
+    const int32_t b = j / n_int, rank = j - b * n_int;
+    const int32_t node = internal[rank];
+    if (p.active != nullptr && p.active[b] == 0) {
+        if (threadIdx.x == 0) drawn[j] = -1;
+        return;
+    }
+    const int32_t step = depths[node] - 1;
+    if (node < 0 || node >= p.nmax || p.slot[(int64_t)b * p.nmax + node] != j || step < 0 || step >= p.u_stride) {
+        if (threadIdx.x == 0) {
+            drawn[j] = -1;
+            record_error(FG_EINVAL);
+        }
+        return;
+    }
+    const T* row = static_cast<const T*>(p.logits) + (int64_t)j * p.logits_row_stride;
+    const float u = p.uniforms[(int64_t)b * p.u_stride + step];
+    const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
+    const int32_t t = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
+                              : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+    if (threadIdx.x == 0) drawn[j] = t;
 }
 
 __global__ void extract_path_kernel(KvPtrs kv, int32_t n_layers, int32_t elem_bytes, int32_t n_heads,
@@ -308,12 +353,37 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     p.hidden_elem_bytes = a->hidden_elem_bytes;
     p.kv_rows = a->kv_rows;
     p.kv_batch = a->kv_batch;
+    p.drawn = nullptr;
+    const bool parallel = a->drawn != nullptr;
+    if (parallel && (!a->internal || !a->depths || a->internal_rows <= 0 || a->parent_stride != 0)) return FG_EINVAL;
     KvPtrs kv;
     for (int l = 0; l < FG_MAX_LAYERS; ++l) {
         kv.k[l] = l < a->n_layers ? a->k_layers[l] : 0;
         kv.v[l] = l < a->n_layers ? a->v_layers[l] : 0;
     }
     cudaStream_t st = (cudaStream_t)stream;
+    if (parallel) {
+        const int32_t n_static = a->internal_rows / a->B;
+        switch (a->logits_dtype) {
+            case FG_DTYPE_F32:
+                draw_internal_kernel<float><<<a->internal_rows, FG_SAMPLE_LANES, 0, st>>>(
+                    p, a->B, a->internal, a->depths, a->plan_out, n_static, a->drawn);
+                break;
+            case FG_DTYPE_BF16:
+                draw_internal_kernel<__nv_bfloat16><<<a->internal_rows, FG_SAMPLE_LANES, 0, st>>>(
+                    p, a->B, a->internal, a->depths, a->plan_out, n_static, a->drawn);
+                break;
+            case FG_DTYPE_F16:
+                draw_internal_kernel<__half><<<a->internal_rows, FG_SAMPLE_LANES, 0, st>>>(
+                    p, a->B, a->internal, a->depths, a->plan_out, n_static, a->drawn);
+                break;
+            default:
+                return FG_EINVAL;
+        }
+        const int32_t s = launch_status();
+        if (s != FG_OK) return s;
+        p.drawn = a->drawn;
+    }
     switch (a->logits_dtype) {
         case FG_DTYPE_F32:
             accept_extract_kernel<float><<<a->B, FG_SAMPLE_LANES, 0, st>>>(p, kv);

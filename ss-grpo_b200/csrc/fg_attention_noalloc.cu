@@ -17,7 +17,17 @@
 //    streams, or two host threads on one device) race; serialize them.
 //  * A call whose scratch need exceeds FG_NOALLOC_SCRATCH_BYTES is rejected
 //    with FG_ECAPACITY (ask fewer splits, or use fg_tree_attention).
+//  * A bf16 call that splits the KV range clears the split counters with a
+//    cudaMemsetAsync on the stream first (the previous call may have used the
+//    array with another layout), so unlike fg_tree_attention it does not start
+//    early under the kernel before it (programmatic dependent launch).  fp32
+//    calls use no scratch at all.
+//  * The device address is cached per device ordinal; after cudaDeviceReset
+//    the cached address is stale, so a process that resets a device must not
+//    call this entry point on it again.
 //  * No cudaMalloc, cudaFree or allocating library routine is called.
+#include <atomic>
+
 #include "fg_common.cuh"
 
 // The shared scratch.  In host code this name is only a host-side stand-in
@@ -26,20 +36,23 @@ static __device__ __align__(256) uint8_t g_fg_noalloc_scratch[FG_NOALLOC_SCRATCH
 
 namespace fg {
 
+// Per-device address cache.  Host threads may race on a device's first call:
+// each then looks the address up itself and stores the same value, and the
+// atomics make those reads and writes well defined.
 static void* noalloc_scratch_ptr() {
-    static void* ptrs[64] = {};
+    static std::atomic<void*> ptrs[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (ptrs[dev] == nullptr) {
-        void* p = nullptr;
+    void* p = ptrs[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
         const cudaError_t e = cudaGetSymbolAddress(&p, g_fg_noalloc_scratch);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             return nullptr;
         }
-        ptrs[dev] = p;
+        ptrs[dev].store(p, std::memory_order_release);
     }
-    return ptrs[dev];
+    return p;
 }
 
 }  // namespace fg
@@ -52,6 +65,9 @@ extern "C" fg_status fg_tree_attention_noalloc(const void* q, int32_t dtype, con
     if (B == 0) return FG_OK;
     if (!kv || B < 0 || n_nodes <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads) return FG_EINVAL;
     const int32_t kv_max = max_kv_len > 0 ? max_kv_len : kv->capacity;
+    if (dtype == FG_DTYPE_F32)  // the fp32 kernel keeps no split-K partials
+        return fg_tree_attention(q, dtype, kv, kv_len, anc_bits, B, n_nodes, n_q_heads, n_kv_heads, head_dim, scale,
+                                 out, nullptr, 0, num_splits, kv_max, stream);
     const size_t need = fg_tree_attention_workspace_size(B, n_nodes, n_q_heads, n_kv_heads, head_dim, num_splits,
                                                          kv_max);
     if (need > (size_t)FG_NOALLOC_SCRATCH_BYTES) return FG_ECAPACITY;

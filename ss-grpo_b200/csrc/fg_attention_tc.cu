@@ -375,8 +375,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     // Q and this round's tree K/V slots are written by the preceding kernel:
-    // every thread waits for it (a no-op without programmatic launch)
+    // every thread waits for it (a no-op without programmatic launch); the
+    // projection after this kernel may then start fetching its weights
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0)
         for (int i = 0; i < min(kStages, nmine); ++i)
             if ((c0 + i + 1) * kBlk > kv_len) {

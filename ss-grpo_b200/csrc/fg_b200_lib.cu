@@ -13,4 +13,4 @@
 #include "fg_lmhead_tc.cu"
 #include "fg_propose.cu"
 #include "fg_chain.cu"
-#include "fg_mlp_tc.cu"
+#include "fg_gemm_tc.cu"

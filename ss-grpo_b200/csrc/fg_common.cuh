@@ -32,6 +32,34 @@ inline int32_t launch_status() {
     return FG_OK;
 }
 
+// Launch as a programmatic dependent of the preceding kernel on the stream:
+// the grid may start while that kernel finishes, so the kernel itself must
+// execute griddepcontrol.wait before it reads anything the preceding kernels
+// wrote (every kernel launched this way does so first, then lets its own
+// dependents launch).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// The grid dependency of a kernel launched with launch_pdl: wait for the
+// preceding kernel, then let the next one launch.
+__device__ __forceinline__ void pdl_wait_then_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float load_elem(const void* p, int32_t dtype, int64_t i) {
     if (dtype == FG_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
     if (dtype == FG_DTYPE_F16) return __half2float(static_cast<const __half*>(p)[i]);

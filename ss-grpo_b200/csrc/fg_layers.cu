@@ -126,7 +126,9 @@ __global__ void __launch_bounds__(128) rope_kv_table_kernel(
     const T* __restrict__ qkv, const T* __restrict__ cs, int32_t n_tokens, int32_t n_nodes, int32_t Hq, int32_t Hkv,
     int32_t D, const int32_t* __restrict__ kv_len, T* __restrict__ kc, T* __restrict__ vc, int64_t sb, int64_t sh,
     int64_t ss, int32_t cap, const int32_t* __restrict__ kv_rows, int32_t kv_batch, T* __restrict__ q_out) {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // qkv comes from the projection before; the tree attention after may then
+    // start (its prefix loads), waiting for this grid before reading Q or the tree K/V
+    pdl_wait_then_release();
     constexpr int NV = 16 / sizeof(T);
     const int32_t tokn = blockIdx.x;
     const int32_t b = tokn / n_nodes, node = tokn % n_nodes;
@@ -191,6 +193,7 @@ __device__ float block_sum(float v, float* red) {
 template <typename T>
 __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                           int32_t dim, float eps, T* __restrict__ y) {
+    pdl_wait_then_release();
     constexpr int NV = 16 / sizeof(T);
     __shared__ float red[32];
     const int32_t nvec = dim / NV;
@@ -309,6 +312,7 @@ __global__ void silu_residual_kernel(const T* __restrict__ x, const T* __restric
 
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, int64_t src_stride, const int32_t* __restrict__ idx,
                                    int64_t row_bytes, uint8_t* __restrict__ out, int64_t out_stride) {
+    pdl_wait_then_release();
     const int32_t r = blockIdx.x;
     const uint8_t* s = src + (int64_t)idx[r] * src_stride;
     uint8_t* d = out + (int64_t)r * out_stride;
@@ -358,10 +362,16 @@ extern "C" fg_status fg_rope_kv_write(const void* qkv, int32_t dtype, const int3
                      ((uintptr_t)kv->v % 16) == 0 && (kv->stride_s * esz) % 16 == 0 && (kv->stride_h * esz) % 16 == 0 &&
                      (kv->stride_b * esz) % 16 == 0;
     if (vec) {
-        FG_DISPATCH(dtype, (rope_kv_table_kernel<T><<<B * n_nodes, 128, 0, st>>>(
-                                (const T*)qkv, (const T*)cos_sin, B * n_nodes, n_nodes, n_q_heads, n_kv_heads,
-                                head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b, kv->stride_h, kv->stride_s,
-                                kv->capacity, kv->rows, kv->batch, (T*)q_out)));
+        cudaError_t e = cudaSuccess;
+        FG_DISPATCH(dtype, (e = launch_pdl(rope_kv_table_kernel<T>, dim3(B * n_nodes), dim3(128), 0, st,
+                                           (const T*)qkv, (const T*)cos_sin, B * n_nodes, n_nodes, n_q_heads,
+                                           n_kv_heads, head_dim, kv_len, (T*)kv->k, (T*)kv->v, kv->stride_b,
+                                           kv->stride_h, kv->stride_s, kv->capacity, kv->rows, kv->batch,
+                                           (T*)q_out)));
+        if (e != cudaSuccess) {
+            set_cuda_error(e);
+            return FG_ECUDA;
+        }
         return launch_status();
     }
     FG_DISPATCH(dtype, (rope_kv_kernel<T><<<B * n_nodes, 128, 0, st>>>(
@@ -380,8 +390,13 @@ extern "C" fg_status fg_rmsnorm(const void* x, const void* weight, int32_t dtype
     const bool vec = (dim * esz) % 16 == 0 && dim * esz <= 128 * 4 * 16 && ((uintptr_t)x % 16) == 0 &&
                      ((uintptr_t)y % 16) == 0 && ((uintptr_t)weight % 16) == 0;
     if (vec) {
-        FG_DISPATCH(dtype, (rmsnorm_vec_kernel<T><<<n_rows, 128, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
-                                                                         (T*)y)));
+        cudaError_t e = cudaSuccess;
+        FG_DISPATCH(dtype, (e = launch_pdl(rmsnorm_vec_kernel<T>, dim3(n_rows), dim3(128), 0, st, (const T*)x,
+                                           (const T*)weight, dim, eps, (T*)y)));
+        if (e != cudaSuccess) {
+            set_cuda_error(e);
+            return FG_ECUDA;
+        }
     } else {
         FG_DISPATCH(dtype, (rmsnorm_kernel<T><<<n_rows, 256, 0, st>>>((const T*)x, (const T*)weight, dim, eps,
                                                                       (T*)y)));
@@ -428,7 +443,12 @@ extern "C" fg_status fg_gather_rows(const void* src, int64_t src_row_stride_byte
     if (row_bytes % 16 || src_row_stride_bytes % 16 || out_row_stride_bytes % 16 || ((uintptr_t)src % 16) ||
         ((uintptr_t)out % 16))
         return FG_EINVAL;
-    gather_rows_kernel<<<n_rows, 128, 0, (cudaStream_t)stream>>>((const uint8_t*)src, src_row_stride_bytes, idx,
-                                                                 row_bytes, (uint8_t*)out, out_row_stride_bytes);
+    const cudaError_t e = launch_pdl(gather_rows_kernel, dim3(n_rows), dim3(128), 0, (cudaStream_t)stream,
+                                     (const uint8_t*)src, src_row_stride_bytes, idx, row_bytes, (uint8_t*)out,
+                                     out_row_stride_bytes);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return FG_ECUDA;
+    }
     return launch_status();
 }

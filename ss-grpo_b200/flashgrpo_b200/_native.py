@@ -63,6 +63,7 @@ class AcceptArgs(ctypes.Structure):
         ("kv_elem_bytes", c_i32), ("n_kv_heads", c_i32), ("head_dim", c_i32), ("kv_stride_b", c_i64),
         ("kv_stride_h", c_i64), ("kv_stride_s", c_i64), ("tree_hidden", c_vp), ("hidden_out", c_vp),
         ("hidden_dim", c_i32), ("hidden_elem_bytes", c_i32), ("kv_rows", c_vp), ("kv_batch", c_i32),
+        ("internal", c_vp), ("depths", c_vp), ("plan_out", c_vp), ("internal_rows", c_i32), ("drawn", c_vp),
     ]
 
 
@@ -88,6 +89,9 @@ SIGNATURES = {
                               ctypes.POINTER(ChainCell), c_f32, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp,
                               c_vp, c_vp, ctypes.c_size_t, c_vp]),
     "fg_gate_up_silu": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp]),
+    "fg_linear_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "fg_linear": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_vp, c_i64, c_i32, c_i32, c_i32,
+                          c_i32, c_i32, c_vp, ctypes.c_size_t, c_vp]),
     "fg_build_tree": (c_i32, [ctypes.POINTER(PlanParams), c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
                               c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_tree_attention_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
@@ -143,7 +147,7 @@ def load():
 LAUNCHING = {"fg_wait_flag", "fg_philox_uniforms", "fg_sample_rows", "fg_row_topk", "fg_lm_head_topk", "fg_build_tree", "fg_rope_table",
              "fg_tree_attention", "fg_tree_attention_noalloc", "fg_accept_extract", "fg_extract_path", "fg_rope_kv_write", "fg_rmsnorm",
              "fg_layernorm", "fg_silu_mul", "fg_silu_residual", "fg_gather_rows", "fg_medusa_propose",
-             "fg_chain_step", "fg_gate_up_silu"}
+             "fg_chain_step", "fg_gate_up_silu", "fg_linear"}
 launches = 0
 
 

@@ -77,7 +77,13 @@ class FlashMedusaConfig:
     sampling_seed: int = 0
     use_cuda_graphs: bool = True
     attention_splits: int = 0
-    lm_head_kernel: str = "fused"  # "fused" (tcgen05 + top-k epilogue) or "separate" (cuBLAS + fg_row_topk)
+    # proposal lm_head: "separate" (cuBLAS + fg_row_topk; measured faster on B200, 3.60 vs 3.66 ms per
+    # config-2 round) or "fused" (tcgen05 GEMM with the top-k in its epilogue)
+    lm_head_kernel: str = "separate"
+    # verify projections + internal lm_head: "auto" (per shape, fg_linear or cuBLAS, whichever
+    # measured faster), "native" (fg_linear, tcgen05, always) or "cublas"
+    dense_kernel: str = "auto"
+    autotune_dense: bool = True    # time fg_linear's tilings once per projection shape
 
 
 class FlashMedusaDecoder:
@@ -105,6 +111,8 @@ class FlashMedusaDecoder:
             raise NotImplementedError("top_k sampling is not on the B200 path yet")
         if config.lm_head_kernel not in {"fused", "separate"}:
             raise ValueError(f"Unsupported lm_head_kernel={config.lm_head_kernel}")
+        if config.dense_kernel not in {"auto", "native", "cublas"}:
+            raise ValueError(f"Unsupported dense_kernel={config.dense_kernel}")
         self._engine: VerifyEngine | None = None
         # captured round graphs, keyed by (state, round shape, round config);
         # a shape is run eagerly once before it is captured
@@ -115,7 +123,8 @@ class FlashMedusaDecoder:
     @property
     def engine(self) -> VerifyEngine:
         if self._engine is None:
-            self._engine = VerifyEngine(self.target_model, self.medusa_heads)
+            self._engine = VerifyEngine(self.target_model, self.medusa_heads,
+                                        autotune=bool(self.config.autotune_dense), dense=self.config.dense_kernel)
         return self._engine
 
     def _plan(self, active: int):
@@ -155,7 +164,8 @@ class FlashMedusaDecoder:
         return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), top_p=top_p,
                            eos_id=int(eos),
                            max_length=int(max_length), seed=int(cfg.sampling_seed),
-                           attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel), chain=chain,
+                           attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel),
+                           dense=str(cfg.dense_kernel), chain=chain,
                            chain_bootstrap=bool(cfg.chain_bootstrap_from_medusa))
 
     def max_heads(self) -> int:

@@ -10,10 +10,11 @@ reference, Reflex off) runs as one stream of work with no host sync:
   tree      fg_build_tree: plan, dense tree, ancestor bits, slots     (K2)
   verify    per layer: RMSNorm, QKV GEMM (+bias), fg_rope_kv_write (RoPE +
             tree K/V written at each row's cache tail), fg_tree_attention
-            (K3), O GEMM + residual, RMSNorm, fg_gate_up_silu (gate/up GEMM
-            with SwiGLU in the epilogue, tcgen05), down GEMM + residual;
+            (K3), O GEMM + residual, RMSNorm, gate/up GEMM with SwiGLU in
+            the epilogue, down GEMM + residual (bf16: every GEMM is
+            fg_linear, tcgen05 with the bias / residual / SwiGLU fused);
             final RMSNorm
-  lm_head   internal (has-children) nodes only                        (cuBLAS)
+  lm_head   internal (has-children) nodes only                  (fg_linear)
   accept    fg_accept_extract: exact_target walk, clip/EOS/pending rules,
             KV compaction in every layer, next hidden state           (K4)
 
@@ -148,7 +149,17 @@ class RoundConfig:
     # proposal lm_head: "fused" = tcgen05 GEMM with the top-k in its epilogue
     # (bf16, hidden a multiple of 64, <= 256 rows), "separate" = cuBLAS GEMM
     # then fg_row_topk
-    lm_head: str = "fused"
+    lm_head: str = "separate"
+    # acceptance: every internal node's draw before the walk (one CTA per
+    # packed logits row) instead of one draw per walk step; faster once the
+    # walk visits more nodes than one wave of those CTAs covers
+    parallel_draws: bool = False
+    # verify-forward projections and the internal-node lm_head: "native" =
+    # fg_linear (tcgen05, fused bias / residual / SwiGLU epilogues, bf16),
+    # "cublas" = torch addmm / mm (+ fg_silu_mul), "auto" = per projection
+    # shape whichever of the two measured faster on this GPU (fp32 always
+    # uses cuBLAS)
+    dense: str = "auto"
 
 
 class DecodeState:
@@ -282,6 +293,8 @@ class RoundBuffers:
         self.hid_int = torch.empty((max(n_rows, 1), H), dtype=spec.dtype, **f)
         self.tree_logits = torch.empty((max(n_rows, 1), V), dtype=spec.dtype, **f)
         self.dcap = dcap
+        # the acceptance walk's draws, one per packed internal-node logits row
+        self.drawn = torch.empty(max(n_rows, 1), **i32)
         self.out = {k: torch.empty((B, dcap), **i32) for k in ("acc_tokens", "acc_nodes")}
         for k in ("acc_len", "correction", "last_node", "finished"):
             self.out[k] = torch.empty(B, **i32)
@@ -295,8 +308,13 @@ class RoundBuffers:
 
 # ------------------------------------------------------------------- engine
 class VerifyEngine:
-    def __init__(self, causal_lm, medusa_heads, *, device=None):
+    def __init__(self, causal_lm, medusa_heads, *, device=None, autotune: bool = True, dense: str = "auto"):
         self.model = causal_lm
+        # time fg_linear's tilings once per projection shape (else the library's choice)
+        self.autotune = autotune
+        # "auto": per shape, fg_linear or cuBLAS, whichever the tuning measured faster
+        self.dense_mode = dense
+        self.tile_report: dict = {}
         self.w = TargetWeights(causal_lm)
         self.spec = self.w.spec
         self.device = device or self.w.embed.device
@@ -384,6 +402,172 @@ class VerifyEngine:
         if need and (rb.attn_ws is None or rb.attn_ws.numel() * 4 < need):
             rb.attn_ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=self.device)
         return rb.attn_ws
+
+    def _native_dense(self, cfg: RoundConfig) -> bool:
+        """fg_linear can run this model's projections (bf16, K multiples of 64)
+        and the round asks for it ("native", or "auto" per shape)."""
+        sp = self.spec
+        return (cfg.dense in ("native", "auto") and sp.dtype == torch.bfloat16 and sp.hidden % 64 == 0
+                and sp.inter % 64 == 0 and (sp.n_q_heads * sp.head_dim) % 64 == 0 and self.w.lm_head.stride(1) == 1
+                and self.w.lm_head.stride(0) == sp.hidden)
+
+    # ---------------------------------------------------- dense projections
+    @staticmethod
+    def _tile_ok(pair: bool, bn: int, epi: int) -> bool:
+        """fg_linear's tile rule: the epilogue's 32-column TMEM reads stay in
+        the tile's 256-column accumulator; an SM pair splits the weight rows
+        in two 8-row-aligned halves."""
+        nb = 2 * bn if epi == ops.EPI_SWIGLU else bn
+        if bn % 16 or nb > 256 or (pair and (nb // 2) % 8):
+            return False
+        return bn // 2 + (bn // 2 + 31) // 32 * 32 + (bn if epi == ops.EPI_SWIGLU else 0) <= 256
+
+    def _tune_linear(self, M: int, n_out: int, K: int, epi: int):
+        """The fastest fg_linear tiling (token rows, outputs, k ranges) of one
+        projection shape, timed with CUDA events on random
+        operands whose weights rotate through more copies than L2 holds (the
+        round reads every layer's weights from HBM).  Runs once per shape,
+        outside any stream capture."""
+        dev = self.device
+        rows = 2 * n_out if epi == ops.EPI_SWIGLU else n_out
+        nk = K // 64
+        cands = []
+        for pair in (False, True):
+            for bn in range(48, 257, 16):
+                if not self._tile_ok(pair, bn, epi) or (epi == ops.EPI_SWIGLU and n_out % bn):
+                    continue
+                n_units = -(-M // (256 if pair else 128)) * -(-n_out // bn)
+                for sp in (1, 2, 3, 4, 6, 8):
+                    if sp > 1 and nk // sp < 4:
+                        break
+                    if n_units * sp > 24 * 148:
+                        continue
+                    nb = 2 * bn if epi == ops.EPI_SWIGLU else bn
+                    stage = 128 * 128 + (nb // 2 if pair else nb) * 128
+                    for st in ((6,) if pair else (4, 6, 8)):
+                        if st * stage <= 227 * 1024 - 2048:
+                            cands.append((256 if pair else 128, bn, sp, st))
+        if not cands:
+            return (0, 0, 0, 0)
+        g = torch.Generator(device=dev).manual_seed(1)
+        copies = max(1, min(16, -(-(256 << 20) // (rows * K * 2))))
+        ws_ = [torch.randn(rows, K, generator=g, device=dev, dtype=torch.bfloat16) * 0.02 for _ in range(copies)]
+        x = torch.randn(M, K, generator=g, device=dev, dtype=torch.bfloat16)
+        b = torch.zeros(n_out, device=dev, dtype=torch.bfloat16) if epi == ops.EPI_STORE else None
+        h = torch.zeros(M, n_out, device=dev, dtype=torch.bfloat16)
+        need = max(ops.linear_workspace_bytes(M, n_out, K, epi, bn, sp, bm) for bm, bn, sp, _ in cands)
+        wsp = torch.zeros(need // 4 + 64, dtype=torch.int32, device=dev) if need else None
+
+        def timed(c, reps=8):
+            # the launches are replayed from a CUDA graph, so the device time
+            # is measured, not the host's launch rate
+            bm, bn, sp, st = c
+            run = lambda i: ops.linear(x, ws_[i % copies], bias=b, resid=h if epi == ops.EPI_RESID else None, out=h,
+                                       epilogue=epi, bm=bm, bn=bn, splits=sp, stages=st, workspace=wsp)
+            run(0)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(reps):
+                    run(i + 1)
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1) / reps
+
+        res = sorted((timed(c), c) for c in cands)
+        best = res[0][1]
+        self.tile_report[(M, n_out, K, epi)] = {"fg_linear_us": 1e3 * res[0][0], "tile": list(best)}
+        if self.dense_mode == "auto":
+            # the library GEMM with the same epilogue, timed the same way
+            gu = torch.empty(M, 2 * n_out, device=dev, dtype=torch.bfloat16) if epi == ops.EPI_SWIGLU else None
+
+            def cublas(i):
+                w_ = ws_[i % copies]
+                if epi == ops.EPI_SWIGLU:
+                    torch.mm(x, w_.t(), out=gu)
+                    ops.silu_mul(gu, out=h)
+                elif epi == ops.EPI_RESID:
+                    torch.addmm(h, x, w_.t(), out=h)
+                else:
+                    torch.addmm(b, x, w_.t(), out=h) if b is not None else torch.mm(x, w_.t(), out=h)
+
+            cublas(0)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(8):
+                    cublas(i + 1)
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            t_cub = e0.elapsed_time(e1) / 8
+            self.tile_report[(M, n_out, K, epi)]["cublas_us"] = 1e3 * t_cub
+            if t_cub < res[0][0]:
+                best = None
+        self.tile_report[(M, n_out, K, epi)]["uses"] = "fg_linear" if best is not None else "cublas"
+        del ws_, x, h, wsp
+        return best
+
+    def _tile(self, M: int, n_out: int, K: int, epi: int):
+        """The fg_linear tiling of a projection shape, or None where the
+        round runs that shape on cuBLAS ("auto" measured it faster)."""
+        key = ("tile", M, n_out, K, epi)
+        if key not in self._graphs:
+            self._graphs[key] = self._tune_linear(M, n_out, K, epi) if self.autotune else (0, 0, 0, 0)
+        return self._graphs[key]
+
+    def _linear(self, x, w, *, epi, bias=None, resid=None, out=None, gu=None):
+        """One projection: fg_linear with this shape's tuned tiling and
+        workspace, or the cuBLAS form of the same epilogue."""
+        M, K = x.shape
+        n_out = w.shape[0] // 2 if epi == ops.EPI_SWIGLU else w.shape[0]
+        tile = self._tile(M, n_out, K, epi)
+        if tile is None:
+            if epi == ops.EPI_SWIGLU:
+                torch.mm(x, w.t(), out=gu)
+                return ops.silu_mul(gu, out=out)
+            if epi == ops.EPI_RESID:
+                torch.addmm(resid, x, w.t(), out=out)
+                if bias is not None:
+                    out.add_(bias)
+                return out
+            return torch.addmm(bias, x, w.t(), out=out) if bias is not None else torch.mm(x, w.t(), out=out)
+        bm, bn, sp, st = tile
+        return ops.linear(x, w, bias=bias, resid=resid, out=out, epilogue=epi, bm=bm, bn=bn, splits=sp, stages=st,
+                          workspace=self._linear_ws(M, n_out, K, epi))
+
+    def _linear_ws(self, M: int, n_out: int, K: int, epi: int):
+        """Zero-filled split-K workspace of one projection shape (None when its
+        tiling needs none); one per shape, reused by every layer in turn."""
+        tile = self._tile(M, n_out, K, epi)
+        if tile is None:
+            return None
+        bm, bn, sp, _ = tile
+        need = ops.linear_workspace_bytes(M, n_out, K, epi, bn, sp, bm)
+        if not need:
+            return None
+        key = ("linws", M, n_out, K, epi)
+        ws = self._graphs.get(key)
+        if ws is None or ws.numel() * 4 < need:
+            ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=self.device)
+            self._graphs[key] = ws
+        return ws
+
+    def _prepare_linear(self, rb: "RoundBuffers", B: int):
+        """Allocates the round's projection workspaces (before any capture)."""
+        sp = self.spec
+        T = B * rb.N
+        qkv = (sp.n_q_heads + 2 * sp.n_kv_heads) * sp.head_dim
+        self._linear_ws(T, qkv, sp.hidden, ops.EPI_STORE)
+        self._linear_ws(T, sp.hidden, sp.n_q_heads * sp.head_dim, ops.EPI_RESID)
+        self._linear_ws(T, sp.inter, sp.hidden, ops.EPI_SWIGLU)
+        self._linear_ws(T, sp.hidden, sp.inter, ops.EPI_RESID)
+        self._linear_ws(rb.hid_int.shape[0], sp.vocab, sp.hidden, ops.EPI_STORE)
 
     def _propose_ws(self, B: int, nh: int, k: int) -> torch.Tensor:
         need = ops.medusa_propose_workspace_bytes(B, self.spec.hidden, self.spec.vocab, nh, k)
@@ -570,11 +754,17 @@ class VerifyEngine:
         # the tree positions are fixed for the round: one cos/sin table for all layers
         ops.rope_table(rb.tree["positions"], w.inv_freq, w.attention_scaling, sp.dtype, out=rb.rope_cs)
         ws = self._attn_workspace(rb, st, cfg.attn_splits)
-        # gate/up GEMM with SwiGLU in its epilogue (bf16); fp32 keeps cuBLAS + fg_silu_mul
-        fused_mlp = sp.dtype == torch.bfloat16 and sp.hidden % 64 == 0 and sp.inter % 16 == 0
+        # bf16: every projection on fg_linear with its consumer in the
+        # epilogue (bias, residual add, SwiGLU); fp32 keeps cuBLAS
+        native = self._native_dense(cfg)
+        T = B * N_
+        if native:
+            self._prepare_linear(rb, B)
         for l, lw in enumerate(w.layers):
             ops.rmsnorm(rb.h, lw["in_norm"], sp.eps, out=rb.xn)
-            if lw["b_qkv"] is not None:
+            if native:
+                self._linear(rb.xn, lw["w_qkv"], epi=ops.EPI_STORE, bias=lw["b_qkv"], out=rb.qkv)
+            elif lw["b_qkv"] is not None:
                 torch.addmm(lw["b_qkv"], rb.xn, lw["w_qkv"].t(), out=rb.qkv)
             else:
                 torch.mm(rb.xn, lw["w_qkv"].t(), out=rb.qkv)
@@ -588,16 +778,20 @@ class VerifyEngine:
                                workspace=ws, num_splits=cfg.attn_splits, max_kv_len=st.capacity, kv=kv)
             if attn_events is not None and attn_events[l] is not None:
                 attn_events[l][1].record()
-            torch.addmm(rb.h, rb.attn.view(B * N_, -1), lw["w_o"].t(), out=rb.h)
-            if lw["b_o"] is not None:
-                rb.h.add_(lw["b_o"])
+            if native:
+                self._linear(rb.attn.view(T, -1), lw["w_o"], epi=ops.EPI_RESID, bias=lw["b_o"], resid=rb.h, out=rb.h)
+            else:
+                torch.addmm(rb.h, rb.attn.view(T, -1), lw["w_o"].t(), out=rb.h)
+                if lw["b_o"] is not None:
+                    rb.h.add_(lw["b_o"])
             ops.rmsnorm(rb.h, lw["post_norm"], sp.eps, out=rb.xn)
-            if fused_mlp:
-                ops.gate_up_silu(rb.xn, lw["w_gu"], out=rb.act)
+            if native:
+                self._linear(rb.xn, lw["w_gu"], epi=ops.EPI_SWIGLU, out=rb.act, gu=rb.gu)
+                self._linear(rb.act, lw["w_down"], epi=ops.EPI_RESID, resid=rb.h, out=rb.h)
             else:
                 torch.mm(rb.xn, lw["w_gu"].t(), out=rb.gu)
                 ops.silu_mul(rb.gu, out=rb.act)
-            torch.addmm(rb.h, rb.act, lw["w_down"].t(), out=rb.h)
+                torch.addmm(rb.h, rb.act, lw["w_down"].t(), out=rb.h)
         ops.rmsnorm(rb.h, w.final_norm, sp.eps, out=rb.tree_hidden.view(B * N_, -1))
 
     def accept(self, st: DecodeState, rb: RoundBuffers, cfg: RoundConfig, phase_event=None):
@@ -613,7 +807,10 @@ class VerifyEngine:
                 idx = b * rb.N + rb.tree["internal"][r.long()]
                 torch.where(rb.j_int < B * ni, idx, torch.zeros_like(idx), out=rb.int_idx)
             ops.gather_rows(rb.tree_hidden.view(B * rb.N, -1), rb.int_idx, out=rb.hid_int)
-            torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
+            if self._native_dense(cfg):
+                self._linear(rb.hid_int, self.w.lm_head, epi=ops.EPI_STORE, out=rb.tree_logits)
+            else:
+                torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
         if phase_event is not None:
             phase_event.record()
         rb.corr_used += (st.pending >= 0).sum()
@@ -625,7 +822,9 @@ class VerifyEngine:
                            max_length=cfg.max_length, row_len=st.row_len, outputs=outs, dcap=rb.dcap,
                            update_len=True, active=st.active, k_layers=[st.k[l] for l in range(self.spec.n_layers)],
                            v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,
-                           hidden_out=st.hidden, kv_rows=st.rows if isinstance(st, RoundView) else None)
+                           hidden_out=st.hidden, kv_rows=st.rows if isinstance(st, RoundView) else None,
+                           parallel=(rb.tree["internal"], rb.tree["depths"], rb.tree["plan"], rb.drawn)
+                           if rb.n_int > 0 and cfg.parallel_draws else None)
         rb.acc_sum += rb.out["acc_len"].sum()
         st.round_dev += 1
 
@@ -680,6 +879,8 @@ class VerifyEngine:
         attn_events / phase_events must be created with external=True to be
         captured."""
         self._attn_workspace(rb, st, cfg.attn_splits)
+        if self._native_dense(cfg):
+            self._prepare_linear(rb, st.B)
         M = (rb.n_heads + 1) * st.B
         if self._fused_lm_head(cfg, M):
             self._lm_head_ws(M, st.B, rb.kmax)  # allocated outside the capture

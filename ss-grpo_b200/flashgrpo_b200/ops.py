@@ -352,10 +352,13 @@ def layer_pointer_arrays(k_layers, v_layers):
 def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
                    row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
                    tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0,
-                   top_p: float = 1.0, kv_rows=None):
+                   top_p: float = 1.0, kv_rows=None, parallel=None):
     """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
     acc_len/correction/pending/last_node/finished [B]; kv_rows (int32 [B],
-    optional): row b compacts cache row kv_rows[b] of k_layers/v_layers."""
+    optional): row b compacts cache row kv_rows[b] of k_layers/v_layers.
+    parallel (optional, shared topology): (internal [nmax], depths [nmax],
+    plan_out [16] or None, drawn int32 [logits rows]) -- every internal
+    node's draw in parallel before the walk (the same tokens)."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     for name, t in (("slot", slot), ("tokens", tokens), ("parents", parents), ("row_len", row_len)):
@@ -391,7 +394,17 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
     if hidden_out is not None:
         a.tree_hidden, a.hidden_out = tree_hidden.data_ptr(), hidden_out.data_ptr()
         a.hidden_dim, a.hidden_elem_bytes = hidden_out.shape[-1], hidden_out.element_size()
-    N.call("fg_accept_extract", ctypes.byref(a), _stream(tokens))
+    n_launch = 1
+    if parallel is not None:
+        internal, depths, plan_out, drawn = parallel
+        for name, t in (("internal", internal), ("depths", depths), ("drawn", drawn)):
+            _need(t, name, torch.int32)
+        if drawn.numel() < logits.shape[0]:
+            raise ValueError("drawn needs one entry per logits row")
+        a.internal, a.depths, a.plan_out = internal.data_ptr(), depths.data_ptr(), _ptr(plan_out)
+        a.internal_rows, a.drawn = logits.shape[0], drawn.data_ptr()
+        n_launch = 2
+    N.call("fg_accept_extract", ctypes.byref(a), _stream(tokens), n_launch=n_launch)
     return outputs
 
 
@@ -458,6 +471,63 @@ def gate_up_silu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | N
     if out.shape != (T, I) or out.dtype != torch.bfloat16:
         raise ValueError("out must be bf16 [T, I]")
     N.call("fg_gate_up_silu", _ptr(x), N.FG_DTYPE_BF16, T, H, _ptr(w_gate_up), I, _ptr(out), _stream(x))
+    return out
+
+
+EPI_STORE, EPI_RESID, EPI_SWIGLU = 0, 1, 2
+
+
+def linear_workspace_bytes(M: int, N_out: int, K: int, epilogue: int = EPI_STORE, bn: int = 0, splits: int = 0,
+                           bm: int = 0) -> int:
+    return int(N.load().fg_linear_workspace_size(M, N_out, K, epilogue, bm, bn, splits))
+
+
+def _row_stride(t: torch.Tensor, name: str):
+    """A 2-D bf16 CUDA tensor with contiguous rows; returns its row stride."""
+    _need(t, name, torch.bfloat16, contiguous=False)
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with contiguous rows")
+    return t.stride(0)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, bias: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+           out: torch.Tensor | None = None, epilogue: int | None = None, bn: int = 0, splits: int = 0,
+           bm: int = 0, stages: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """fg_linear (bf16, tcgen05): out = x @ w.T + bias (EPI_STORE), resid +
+    x @ w.T + bias (EPI_RESID, the default when resid is given; resid may be
+    out), or the SwiGLU of the gate rows w[:I] and up rows w[I:] (EPI_SWIGLU).
+    x [M, K], w [N, K] (or [2I, K]); tile tokens bm (128 / 256), outputs bn,
+    k ranges `splits` and ring `stages`, 0 = chosen by the library; split-K
+    tiles need `workspace` (linear_workspace_bytes, zero-filled once)."""
+    if epilogue is None:
+        epilogue = EPI_RESID if resid is not None else EPI_STORE
+    ldx = _row_stride(x, "x")
+    ldw = _row_stride(w, "w")
+    M, K = x.shape
+    if ldx != K or ldw != K or w.shape[1] != K:
+        raise ValueError("x and w need densely packed rows of the same K")
+    n_out = w.shape[0] // 2 if epilogue == EPI_SWIGLU else w.shape[0]
+    if out is None:
+        out = torch.empty((M, n_out), dtype=x.dtype, device=x.device)
+    ldo = _row_stride(out, "out")
+    if out.shape != (M, n_out):
+        raise ValueError(f"out must be [{M}, {n_out}]")
+    ldr = 0
+    if resid is not None:
+        ldr = _row_stride(resid, "resid")
+        if resid.shape != (M, n_out):
+            raise ValueError("resid must have out's shape")
+    if bias is not None:
+        _need(bias, "bias", torch.bfloat16)
+        if bias.shape != (n_out,):
+            raise ValueError("bias must be [N]")
+    need = linear_workspace_bytes(M, n_out, K, epilogue, bn, splits, bm)
+    if need:
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            raise ValueError(f"this tiling needs a zero-filled workspace of {need} bytes")
+        _need(workspace, "workspace", contiguous=True)
+    N.call("fg_linear", _ptr(x), N.FG_DTYPE_BF16, M, K, _ptr(w), n_out, _ptr(bias), _ptr(resid), ldr, _ptr(out), ldo,
+           epilogue, bm, bn, splits, stages, _ptr(workspace) if need else None, need, _stream(x))
     return out
 
 

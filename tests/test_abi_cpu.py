@@ -85,6 +85,24 @@ def test_host_only_entry_points():
     assert step(_native.FG_DTYPE_BF16, 1536, cell, 1, 4, 4, far, 1024) == _native.FG_ECAPACITY  # workspace too small
     assert lib.fg_chain_step_workspace_size(512, 1536, 192, 151936, 4) == \
         lib.fg_chain_step_workspace_size(256, 1536, 192, 151936, 4)                           # 256-row passes
+    # dense projections: dtype, K, N, tile and epilogue checks before any CUDA call
+    lin = lambda dtype, M, K, N, bias, resid, ld, epi, bn, sp: lib.fg_linear(
+        p, dtype, M, K, p, N, bias, resid, ld, p, ld, epi, 128, bn, sp, 0, None, 0, None)
+    assert lin(_native.FG_DTYPE_F32, 64, 128, 64, None, None, 64, 0, 0, 0) == _native.FG_EUNSUPPORTED
+    assert lin(_native.FG_DTYPE_BF16, 64, 100, 64, None, None, 64, 0, 0, 0) == _native.FG_ECAPACITY  # K % 64
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 60, None, None, 60, 0, 0, 0) == _native.FG_EINVAL     # N % 8
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 64, None, None, 64, 1, 0, 0) == _native.FG_EINVAL     # RESID needs resid
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 64, p, None, 64, 2, 0, 0) == _native.FG_EINVAL        # no bias with SwiGLU
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 64, None, None, 64, 0, 24, 1) == _native.FG_EINVAL    # bn % 16
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 64, None, None, 64, 0, 16, 2) == _native.FG_ECAPACITY # split-K, no workspace
+    assert lin(_native.FG_DTYPE_BF16, 64, 128, 64, None, None, 64, 7, 0, 0) == _native.FG_EINVAL     # epilogue
+    assert lib.fg_linear(p, _native.FG_DTYPE_BF16, 64, 128, p, 64, None, None, 64, p, 64, 0, 192, 64, 1, 0, None, 0,
+                         None) == _native.FG_EINVAL                                              # bm 128 or 256
+    assert lib.fg_linear(p, _native.FG_DTYPE_BF16, 64, 128, p, 64, None, None, 64, p, 64, 0, 128, 64, 1, 9, None, 0,
+                         None) == _native.FG_EINVAL                                              # ring stages
+    assert lib.fg_linear_workspace_size(832, 1536, 8960, 1, 128, 256, 5) == 5 * 832 * 1536 * 4
+    assert lib.fg_linear_workspace_size(832, 1536, 8960, 2, 256, 128, 3) == 3 * 832 * 2 * 1536 * 4
+    assert lib.fg_linear_workspace_size(832, 1536, 8960, 1, 128, 256, 1) == 0
 
 
 def test_plan_params_tables():

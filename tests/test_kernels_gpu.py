@@ -400,7 +400,7 @@ def test_build_tree_matches_oracle(ops, case):
 # ------------------------------------------------ acceptance + compaction
 def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sample, temperature, row_len,
                 max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None,
-                top_p=1.0, kv_rows=None):
+                top_p=1.0, kv_rows=None, parallel=None):
     B = tokens.shape[0]
     outs = {k: torch.full((B, dcap), -9, dtype=torch.int32, device=DEV) for k in ("acc_tokens", "acc_nodes")}
     for k in ("acc_len", "correction", "pending", "last_node", "finished"):
@@ -408,9 +408,9 @@ def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sa
     rl = row_len.clone()
     ops.accept_extract(logits=logits, slot=slots, tokens=tokens, parents=parents, n_nodes=n_nodes,
                        uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
-                       max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=False,
+                       max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=parallel is not None,
                        k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out,
-                       top_p=top_p, kv_rows=kv_rows)
+                       top_p=top_p, kv_rows=kv_rows, parallel=parallel)
     torch.cuda.synchronize()
     return outs, rl
 
@@ -430,10 +430,14 @@ def test_accept_matches_reference_fixture(ops, golden_dir):
         assert np.array_equal(outs["last_node"].cpu().numpy(), g[c + "_parent"]), c
 
 
+@pytest.mark.parametrize("parallel", [False, True])
 @pytest.mark.parametrize("dtype,V,B,peak,top_p", [(torch.bfloat16, 151936, 64, 6.0, 1.0), (torch.float32, 4096, 12, 8.0, 1.0),
                                                   (torch.float16, 1000, 33, 5.0, 1.0), (torch.bfloat16, 151936, 64, 6.0, 0.9),
                                                   (torch.float32, 4096, 12, 2.0, 0.5)])
-def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p):
+def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p, parallel):
+    """K4 against the oracle walk, bit for bit: drawing during the walk, and
+    (parallel) every internal node's draw made before the walk on the shared
+    topology."""
     g = torch.Generator().manual_seed(V + B)
     plan = rp.Plan(16, 3, [4, 2, 2], 0, "fixed")
     heads = [(torch.randn(B, V, generator=g) * peak).to(dtype).float() for _ in range(3)]
@@ -457,10 +461,20 @@ def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p):
     v_np = [v.view(torch.int16).cpu().numpy().copy() for v in vl]
     hidden = torch.randn(B, n, 64, generator=g).to(DEV)
     hout = torch.zeros(B, 64, device=DEV)
+    par_arg, par_in = par.to(DEV), None
+    if parallel:
+        # dense trees of one plan share their topology
+        assert all(t.parents == trees[0].parents for t in trees)
+        internal = [i for i in range(n) if trees[0].children.get(i)]
+        par_arg = par[0].contiguous().to(DEV)
+        par_in = (torch.tensor(internal, dtype=torch.int32, device=DEV),
+                  torch.tensor(trees[0].depths, dtype=torch.int32, device=DEV), None,
+                  torch.full((packed.shape[0],), -9, dtype=torch.int32, device=DEV))
     outs, rl = _run_accept(ops, packed.to(DEV), torch.tensor(slots, dtype=torch.int32).to(DEV), tok.to(DEV),
-                           par.to(DEV), torch.full((B,), n, dtype=torch.int32, device=DEV), U.to(DEV),
+                           par_arg, torch.full((B,), n, dtype=torch.int32, device=DEV), U.to(DEV),
                            do_sample=True, temperature=1.0, row_len=row_len.to(DEV), max_length=max_length, eos=eos,
-                           dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout, top_p=top_p)
+                           dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout, top_p=top_p,
+                           parallel=par_in)
     ref = orc.accept_walk(packed.float().numpy(), np.array(slots), tok.numpy(), par.numpy(), np.full(B, n), U.numpy(),
                           do_sample=True, temperature=1.0, eos_id=eos, max_length=max_length,
                           row_len=row_len.numpy(), dcap=8, top_p=top_p)
@@ -720,6 +734,109 @@ def test_gate_up_silu_matches_gemm_then_silu_mul(ops, T, H, I):
     again = ops.gate_up_silu(x, w, out=torch.empty_like(out))
     torch.cuda.synchronize()
     assert torch.equal(again, got)
+
+
+def _linear_ref(x, w, epi, bias=None, resid=None):
+    """fp32 reference of fg_linear's epilogues (SwiGLU rounds g and u to bf16
+    as the HF MLP's bf16 linears do before act_fn)."""
+    d = x.float() @ w.float().t()
+    if epi == 2:
+        n = w.shape[0] // 2
+        gb, ub = d[:, :n].bfloat16().float(), d[:, n:].bfloat16().float()
+        return torch.nn.functional.silu(gb) * ub
+    if bias is not None:
+        d = d + bias.float()
+    if resid is not None:
+        d = d + resid.float()
+    return d
+
+
+@pytest.mark.parametrize("M,K,N,epi,bias,bm,bn,splits", [
+    (832, 1536, 2048, 0, True, 0, 0, 0),         # config 2 QKV with bias
+    (832, 1536, 1536, 1, False, 0, 0, 0),        # O projection + residual, in place
+    (832, 8960, 1536, 1, False, 0, 0, 0),        # down projection + residual
+    (832, 1536, 8960, 2, False, 0, 0, 0),        # gate/up + SwiGLU
+    (320, 1536, 151936, 0, False, 0, 0, 0),      # internal-node lm_head (5 x 64 rows)
+    (77, 256, 200, 1, True, 128, 48, 2),         # partial token and output tiles, split-K
+    (300, 512, 1024, 2, False, 128, 64, 4),      # SwiGLU with split-K
+    (130, 1024, 512, 0, True, 128, 256, 3),      # widest tile, split-K, two token tiles
+    (832, 8960, 1536, 1, False, 128, 256, 5),    # down projection, explicit split-K
+    # 256-token tiles on SM pairs (cta_group::2): gate on the even CTA, up on the odd one
+    (832, 1536, 8960, 2, False, 256, 128, 1),
+    (300, 1536, 1536, 1, True, 256, 256, 3),     # split-K, the odd CTA's rows partly past M
+    (100, 512, 640, 0, False, 256, 160, 1),      # the odd CTA's rows all past M
+    (832, 8960, 1536, 1, False, 256, 192, 6),    # down projection, split-K
+    (832, 1536, 2048, 0, True, 256, 128, 1),     # QKV with bias
+    (320, 1536, 151936, 0, False, 256, 256, 1),  # internal-node lm_head
+    (300, 512, 1024, 2, False, 256, 64, 2),      # SwiGLU split-K on a pair
+])
+def test_linear_epilogues_match_fp32(ops, M, K, N, epi, bias, bm, bn, splits):
+    """fg_linear against an fp32 torch reference of the same projection and
+    epilogue, within the bf16 tolerance (2e-2 of the largest magnitude, 1e-2
+    normwise); a second call gives the same bits (split-K adds its partials
+    in a fixed order)."""
+    g = torch.Generator().manual_seed(M + N + K + 7 * epi)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    rows = 2 * N if epi == 2 else N
+    w = (torch.randn(rows, K, generator=g) * K ** -0.5).to(torch.bfloat16).to(DEV)
+    b = torch.randn(N, generator=g).to(torch.bfloat16).to(DEV) if bias else None
+    resid = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV) if epi == 1 else None
+    ref = _linear_ref(x, w, epi, b, resid)
+    need = ops.linear_workspace_bytes(M, N, K, epi, bn, splits, bm)
+    ws = torch.zeros(need // 4 + 16, dtype=torch.int32, device=DEV) if need else None
+    outs = []
+    for _ in range(2):
+        if epi == 1:
+            out = resid.clone()  # the residual add in place, as the verify forward runs it
+            got = ops.linear(x, w, bias=b, resid=out, out=out, bm=bm, bn=bn, splits=splits, workspace=ws)
+        else:
+            out = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=DEV)
+            got = ops.linear(x, w, bias=b, out=out, epilogue=epi, bm=bm, bn=bn, splits=splits, workspace=ws)
+        outs.append(got)
+    torch.cuda.synchronize()
+    got = outs[0]
+    assert torch.isfinite(got.float()).all()
+    d = got.float() - ref
+    assert (d.norm() / ref.norm()).item() <= 1e-2
+    assert d.abs().max().item() <= 2e-2 * ref.abs().max().item()
+    assert torch.equal(outs[1], got)
+
+
+def test_linear_ring_depths_give_the_same_bits(ops):
+    """The ring depth only changes how many k chunks are in flight: 4, 6 and
+    8 stages give identical outputs (the k order of the accumulation is the
+    same), for a fused epilogue and a split-K tile."""
+    g = torch.Generator().manual_seed(3)
+    M, K, N = 300, 1024, 512
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(N, K, generator=g) * K ** -0.5).to(torch.bfloat16).to(DEV)
+    r = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV)
+    for bn, splits in ((64, 1), (64, 2)):  # 24 KB stages: 8 of them fit
+        need = ops.linear_workspace_bytes(M, N, K, 1, bn, splits, 128)
+        ws = torch.zeros(need // 4 + 16, dtype=torch.int32, device=DEV) if need else None
+        outs = [ops.linear(x, w, resid=r, out=r.clone(), bm=128, bn=bn, splits=splits, stages=st, workspace=ws)
+                for st in (4, 6, 8)]
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2]), (bn, splits)
+        ref = _linear_ref(x, w, 1, None, r)
+        assert (outs[0].float() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+
+
+def test_linear_rejects_bad_shapes(ops):
+    from flashgrpo_b200 import _native
+
+    x = torch.zeros(8, 100, dtype=torch.bfloat16, device=DEV)  # K not a multiple of 64
+    w = torch.zeros(16, 100, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(_native.NativeError):
+        ops.linear(x, w)
+    x = torch.zeros(8, 128, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(16, 128, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(_native.NativeError):
+        ops.linear(x, w, bm=128, bn=24, splits=1)  # bn must be a multiple of 16
+    need = ops.linear_workspace_bytes(8, 16, 128, 0, 16, 2, 128)
+    assert need > 0
+    with pytest.raises(ValueError):
+        ops.linear(x, w, bm=128, bn=16, splits=2)  # split-K without its workspace
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
