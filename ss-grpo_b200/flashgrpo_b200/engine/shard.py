@@ -62,3 +62,39 @@ def reduce_scalar(value: float, op: str, device, group=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "sum": dist.ReduceOp.SUM}[op], group=group)
     return float(t.item())
+
+
+def gather_rollouts(local: torch.Tensor, counts: list[int], extras=(), group=None):
+    """The round's one collective: a single all-gather of every rank's
+    per-rollout values together with a few per-rank numbers (device time,
+    token counts), the per-rank row counts known from the shard plan
+    (``counts[r] = len(rollout_rows(prompt_shard(...)))``).
+
+    Every rank sends ``max(counts) + len(extras)`` float64 slots (integers
+    below 2**53 round-trip exactly).  Returns ``(values, per_rank)``: the
+    per-rollout values in global rollout order, in ``local``'s dtype, and a
+    ``[world, len(extras)]`` float64 tensor of every rank's numbers.  With one
+    process no collective runs."""
+    import torch.distributed as dist
+
+    if local.dim() != 1:
+        raise ValueError("gather_rollouts expects a 1-D tensor")
+    extras = [float(x) for x in extras]
+    ne = len(extras)
+    if not dist.is_available() or not dist.is_initialized():
+        if len(counts) != 1 or counts[0] != local.numel():
+            raise ValueError(f"shard plan {counts} does not match one rank holding {local.numel()} rollouts")
+        return local.clone(), torch.tensor([extras], dtype=torch.float64).reshape(1, ne)
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if len(counts) != world or counts[rank] != local.numel():
+        raise ValueError(f"shard plan {counts} does not match rank {rank} holding {local.numel()} rollouts")
+    width = max(counts) + ne
+    send = torch.zeros(width, dtype=torch.float64, device=local.device)
+    send[: local.numel()] = local.to(torch.float64)
+    if ne:
+        send[width - ne:] = torch.tensor(extras, dtype=torch.float64, device=local.device)
+    recv = torch.empty(world * width, dtype=torch.float64, device=local.device)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    recv = recv.view(world, width)
+    values = torch.cat([recv[r, : counts[r]] for r in range(world)]).to(local.dtype)
+    return values, recv[:, width - ne:].cpu()

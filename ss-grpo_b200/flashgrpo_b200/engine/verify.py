@@ -515,10 +515,15 @@ class VerifyEngine:
 
     def _tile(self, M: int, n_out: int, K: int, epi: int):
         """The fg_linear tiling of a projection shape, or None where the
-        round runs that shape on cuBLAS ("auto" measured it faster)."""
-        key = ("tile", M, n_out, K, epi)
+        round runs that shape on cuBLAS ("auto" measured it faster).  Shapes
+        are tuned per 128-row bucket of M (the tile grid is the same for
+        every M of a bucket, for 128- and 256-row tiles alike), so a round
+        whose active rows shrink by a few retired rows reuses the decision
+        instead of timing the candidates again."""
+        Mb = -(-M // 128) * 128
+        key = ("tile", Mb, n_out, K, epi)
         if key not in self._graphs:
-            self._graphs[key] = self._tune_linear(M, n_out, K, epi) if self.autotune else (0, 0, 0, 0)
+            self._graphs[key] = self._tune_linear(Mb, n_out, K, epi) if self.autotune else (0, 0, 0, 0)
         return self._graphs[key]
 
     def _linear(self, x, w, *, epi, bias=None, resid=None, out=None, gu=None):

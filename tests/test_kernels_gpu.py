@@ -201,11 +201,21 @@ def test_medusa_propose_matches_torch_heads_then_lm_head(ops, B, H, V, n_heads, 
     ops.medusa_propose(x, B, heads, w, root_logits=root, k=k, topk_out=got, workspace=ws)
     torch.cuda.synchronize()
     h = x[:B]
+    h32 = h.float()
     for i, hw in enumerate(heads):
+        got_i = x[(i + 1) * B:(i + 2) * B].float()
+        # fp32 reference on the same bf16 inputs: the bf16 kernel within
+        # 1e-2 relative in norm and no element further than 2e-2 of the
+        # largest magnitude (the 2e-2 bf16 bound)
+        w32 = {n: t.float() for n, t in hw.items()}
+        ref32 = h32 + F.silu(F.linear(F.layer_norm(h32, (H,), w32["norm_w"], w32["norm_b"], 1e-5), w32["fc_w"],
+                                      w32["fc_b"]))
+        d32 = got_i - ref32
+        assert (d32.norm() / ref32.norm()).item() <= 1e-2, i
+        assert d32.abs().max().item() <= 2e-2 * ref32.abs().max().item(), i
+        # and torch's own bf16 evaluation of the head within the same bounds
         ref = h + F.silu(F.linear(F.layer_norm(h, (H,), hw["norm_w"], hw["norm_b"], 1e-5), hw["fc_w"], hw["fc_b"]))
-        d = x[(i + 1) * B:(i + 2) * B].float() - ref.float()
-        # bf16 on both sides, different GEMM summation orders: 1e-2 relative
-        # in norm, no element further than 2e-2 of the largest magnitude
+        d = got_i - ref.float()
         assert (d.norm() / ref.float().norm()).item() <= 1e-2, i
         assert d.abs().max().item() <= 2e-2 * ref.float().abs().max().item(), i
     want_root = torch.full((B, V), float("nan"), dtype=bf, device=DEV)
@@ -238,9 +248,13 @@ def _chain_case(n_seq, n_parent, fanout, n_child, H, V, seed):
     return state, tokens, embed, cell
 
 
-def _chain_ref(state, tokens, embed, cell, n_parent, fanout, n_child):
-    """ChainDraftCell.forward evaluated by torch in bf16 on the gathered rows."""
+def _chain_ref(state, tokens, embed, cell, n_parent, fanout, n_child, fp32=False):
+    """ChainDraftCell.forward evaluated by torch on the gathered rows, in
+    bf16 (the inputs' dtype) or in fp32 on the same bf16 inputs."""
     F = torch.nn.functional
+    if fp32:
+        state, embed = state.float(), embed.float()
+        cell = {n: t.float() for n, t in cell.items()}
     H = state.shape[1]
     M = tokens.shape[0] * n_child
     r = torch.arange(M, device=DEV)
@@ -285,6 +299,12 @@ def test_chain_step_matches_torch_cell_then_lm_head(ops, n_seq, n_parent, fanout
     assert d.abs().max().item() <= 2e-2 * ref.float().abs().max().item()
     upd, ref_upd = out.float() - s.float(), ref.float() - s.float()
     assert ((upd - ref_upd).norm() / ref_upd.norm()).item() <= 5e-2
+    # the fp32 reference on the same bf16 inputs, within the same bounds
+    s32, ref32 = _chain_ref(state, tokens, embed, cell, n_parent, fanout, n_child, fp32=True)
+    d32 = out.float() - ref32
+    assert (d32.norm() / ref32.norm()).item() <= 1e-2
+    assert d32.abs().max().item() <= 2e-2 * ref32.abs().max().item()
+    assert (((out.float() - s32) - (ref32 - s32)).norm() / (ref32 - s32).norm()).item() <= 5e-2
     if k:
         want = mk()
         ws2 = torch.empty(max(ops.lm_head_topk_workspace_bytes(256, V, 0, k), 16) // 4 + 4, dtype=torch.int32,
@@ -553,6 +573,9 @@ def _attn_reference(q, k, v, kv_len, tree, scale):
     (8, 13, 12, 2, 1024, 0), (8, 13, 12, 2, 1024, 1), (4, 13, 12, 2, 700, 3), (6, 32, 28, 4, 517, 0),
     (2, 64, 32, 8, 300, 2), (3, 128, 32, 8, 129, 0), (1, 16, 32, 8, 4000, 0), (5, 1, 12, 2, 63, 0),
     (2, 8, 8, 8, 0, 0), (64, 13, 12, 2, 1024, 0), (1, 16, 32, 8, 4000, 24), (2, 13, 12, 2, 1500, 64),
+    # config-5 sweep corners: the longest prefix with the fewest nodes, a long
+    # prefix with 4 query-row groups per KV head
+    (1, 8, 32, 8, 32768, 0), (2, 128, 32, 8, 16384, 0),
 ])
 def test_tree_attention_bf16(ops, B, n, hq, hkv, L, splits):
     g = torch.Generator().manual_seed(B * 1000 + n)

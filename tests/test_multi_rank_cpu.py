@@ -57,6 +57,16 @@ def _worker(rank: int, world: int, port: int, n_prompts: int, samples: int):
         # slowest rank's time and total tokens, as bench.py reports them
         assert shard.reduce_scalar(1.5 + rank, "max", "cpu") == 1.5 + world - 1
         assert shard.reduce_scalar(float(local.sum()), "sum", "cpu") == float(want.sum())
+        # the single all-gather bench.py runs: sizes from the shard plan, the
+        # per-rank time and token count riding in the same buffer
+        counts = [len(shard.rollout_rows(shard.prompt_shard(n_prompts, world, r), samples)) for r in range(world)]
+        got2, per_rank = shard.gather_rollouts(local, counts, extras=(1.5 + rank, float(local.sum())))
+        assert torch.equal(got2, want), (rank, got2, want)
+        assert per_rank.shape == (world, 2)
+        assert per_rank[:, 0].max().item() == 1.5 + world - 1
+        assert per_rank[:, 1].sum().item() == float(want.sum())
+        with pytest.raises(ValueError):
+            shard.gather_rollouts(local, [c + 1 for c in counts])
     finally:
         dist.destroy_process_group()
 
@@ -71,3 +81,5 @@ def test_single_process_gather_is_identity():
     x = torch.arange(5, dtype=torch.int32)
     assert torch.equal(shard.gather_rollout_values(x), x)
     assert shard.reduce_scalar(3.0, "max", "cpu") == 3.0
+    vals, per_rank = shard.gather_rollouts(x, [5], extras=(2.0, 7.0))
+    assert torch.equal(vals, x) and per_rank.tolist() == [[2.0, 7.0]]
