@@ -70,16 +70,60 @@ struct AcceptParams {
     const int32_t* drawn;    // parallel draws per packed logits row (NULL = draw during the walk)
 };
 
+// CTAs per row and threads per CTA of the clustered walk
+constexpr int kAcceptCtas = 8;
+constexpr int kAcceptClusterThreads = 256;
+
 // g_fg_error_word is defined in fg_abi.cu (same translation unit).
 __device__ __forceinline__ void record_error(int32_t code) { atomicCAS(&g_fg_error_word, 0, code); }
 
+// The clustered walk's compaction: the same moves in path order, four
+// entries at a time (their loads before their stores).  A walk path is
+// strictly increasing (every accepted node is a child of the previous one
+// and follows it in node order, which the walk checks), so path[j] >= j:
+// every later source slot lies past every destination written before it,
+// and only one batch of values is held in registers.
+__device__ void compact_row_in_order(const KvPtrs& kv, int32_t n_layers, int32_t elem_bytes, int32_t n_heads,
+                                     int32_t head_dim, int64_t sb, int64_t sh, int64_t ss, int32_t b, int32_t base,
+                                     const int32_t* path, int32_t a, int32_t part, int32_t parts) {
+    const int32_t cols = head_dim * elem_bytes / 16;
+    const int64_t items = (int64_t)n_layers * 2 * n_heads * cols;
+    for (int64_t it = (int64_t)part * blockDim.x + threadIdx.x; it < items; it += (int64_t)parts * blockDim.x) {
+        const int32_t c = (int32_t)(it % cols);
+        int64_t g = it / cols;
+        const int32_t h = (int32_t)(g % n_heads);
+        g /= n_heads;
+        const int32_t which = (int32_t)(g % 2);
+        const int32_t l = (int32_t)(g / 2);
+        uint8_t* rowp = reinterpret_cast<uint8_t*>(which == 0 ? kv.k[l] : kv.v[l]) +
+                        ((int64_t)b * sb + (int64_t)h * sh) * elem_bytes + (int64_t)c * 16;
+        for (int32_t j0 = 0; j0 < a; j0 += 4) {
+            uint4 vals[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int32_t j = j0 + q;
+                if (j < a && path[j] != j)
+                    vals[q] = *reinterpret_cast<const uint4*>(rowp + (int64_t)(base + path[j]) * ss * elem_bytes);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int32_t j = j0 + q;
+                if (j < a && path[j] != j)
+                    *reinterpret_cast<uint4*>(rowp + (int64_t)(base + j) * ss * elem_bytes) = vals[q];
+            }
+        }
+    }
+}
+
 // Moves row b's accepted slots in every layer.  path[j] < FG_MAX_PATH nodes.
+// The (layer, K|V, head, column) items are dealt to `parts` CTAs (part =
+// this CTA's index among them); an item is one thread's alone.
 __device__ void compact_row(const KvPtrs& kv, int32_t n_layers, int32_t elem_bytes, int32_t n_heads,
                             int32_t head_dim, int64_t sb, int64_t sh, int64_t ss, int32_t b, int32_t base,
-                            const int32_t* path, int32_t a) {
+                            const int32_t* path, int32_t a, int32_t part = 0, int32_t parts = 1) {
     const int32_t cols = head_dim * elem_bytes / 16;  // 16-byte columns per vector
     const int64_t items = (int64_t)n_layers * 2 * n_heads * cols;
-    for (int64_t it = threadIdx.x; it < items; it += blockDim.x) {
+    for (int64_t it = (int64_t)part * blockDim.x + threadIdx.x; it < items; it += (int64_t)parts * blockDim.x) {
         const int32_t c = (int32_t)(it % cols);
         int64_t g = it / cols;
         const int32_t h = (int32_t)(g % n_heads);
@@ -98,23 +142,31 @@ __device__ void compact_row(const KvPtrs& kv, int32_t n_layers, int32_t elem_byt
     }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptParams p, KvPtrs kv) {
-    __shared__ SampleSmem sm;
-    __shared__ NucleusSmem ns;
+// S == 1: one CTA of 512 threads per row.  S > 1: a cluster of S CTAs of
+// kAcceptClusterThreads threads per row, for fg-icdf-v1 draws (no nucleus,
+// T > 0, no parallel draws): every CTA walks the tree redundantly on the
+// same draws (cluster_sample, its e_i buffer in dynamic shared memory), CTA 0
+// writes the row's outputs, the compaction and the hidden copy are dealt
+// over the S CTAs, and the lengths / active flags change only after a
+// cluster barrier (every CTA has read them by then).
+template <typename T, int S>
+__global__ void __launch_bounds__(S > 1 ? kAcceptClusterThreads : FG_SAMPLE_LANES, S > 1 ? 4 : 1)
+    accept_extract_kernel(AcceptParams p, KvPtrs kv) {
     __shared__ int32_t s_child;
     __shared__ int32_t s_match;
     __shared__ int32_t s_path[FG_MAX_PATH];
     __shared__ int32_t s_tok[FG_MAX_PATH];
     __shared__ int32_t s_a, s_corr, s_err;
-    const int32_t b = blockIdx.x;
+    const int32_t b = blockIdx.x / S;
     const int tid = threadIdx.x;
+    const uint32_t rank = S > 1 ? cl_rank() : 0;
     const int32_t* tk = p.tokens + (int64_t)b * p.nmax;
     const int32_t* pa = p.parents + (int64_t)b * p.parent_stride;
     const int32_t* sl = p.slot + (int64_t)b * p.nmax;
     const int32_t n = p.n_nodes ? p.n_nodes[b] : p.n_nodes_shared;
     const bool row_active = p.active == nullptr || p.active[b] != 0;
     if (!row_active) {
+        if (rank != 0) return;
         if (tid < p.dcap) {
             p.acc_tokens[(int64_t)b * p.dcap + tid] = -1;
             p.acc_nodes[(int64_t)b * p.dcap + tid] = -1;
@@ -163,9 +215,17 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
         } else {
             const T* row = static_cast<const T*>(p.logits) + (int64_t)srow * p.logits_row_stride;
             const float u = p.uniforms[(int64_t)b * p.u_stride + step];
-            const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
-            drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
-                            : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+            if constexpr (S == 1) {
+                __shared__ SampleSmem sm;
+                __shared__ NucleusSmem ns;
+                const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
+                drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
+                                : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+            } else {
+                __shared__ ClusterSampleSmem<S, kAcceptClusterThreads> cs;
+                extern __shared__ __align__(16) float ebuf[];
+                drawn = cluster_sample<T, S, kAcceptClusterThreads>(row, p.vocab, p.temperature, u, cs, ebuf);
+            }
         }
         if (tid == 0) s_match = 0x7fffffff;
         __syncthreads();
@@ -178,6 +238,11 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
             __syncthreads();
             break;
         }
+        if (match <= parent) {  // children follow their parent in node order
+            if (tid == 0) s_err = FG_EINVAL;
+            __syncthreads();
+            break;
+        }
         if (tid == 0) {
             s_path[s_a] = match;
             s_tok[s_a] = drawn;
@@ -187,7 +252,7 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
         __syncthreads();
     }
     if (s_err != 0) {
-        if (tid == 0) record_error(s_err);
+        if (tid == 0 && rank == 0) record_error(s_err);
         return;
     }
     // post-accept rules
@@ -204,11 +269,11 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
             break;
         }
     const bool fin = eos_seen || (len0 + a >= p.max_length);
-    if (tid < p.dcap) {
+    if (rank == 0 && tid < p.dcap) {
         p.acc_tokens[(int64_t)b * p.dcap + tid] = tid < a ? s_tok[tid] : -1;
         p.acc_nodes[(int64_t)b * p.dcap + tid] = tid < a ? s_path[tid] : -1;
     }
-    if (tid == 0) {
+    if (rank == 0 && tid == 0) {
         p.acc_len[b] = a;
         p.correction[b] = s_corr;
         p.pending[b] = (s_corr >= 0 && a == raw && !fin) ? s_corr : -1;
@@ -217,19 +282,27 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) accept_extract_kernel(AcceptP
     }
     // extract_path compaction of the accepted slots (in the row's cache row)
     const int32_t bk = cache_row(p.kv_rows, p.kv_batch, b);
-    if (p.n_layers > 0 && bk >= 0)
-        compact_row(kv, p.n_layers, p.kv_elem_bytes, p.n_kv_heads, p.head_dim, p.kv_stride_b, p.kv_stride_h,
-                    p.kv_stride_s, bk, len0, s_path, a);
+    if (p.n_layers > 0 && bk >= 0) {
+        if constexpr (S > 1)
+            compact_row_in_order(kv, p.n_layers, p.kv_elem_bytes, p.n_kv_heads, p.head_dim, p.kv_stride_b,
+                                 p.kv_stride_h, p.kv_stride_s, bk, len0, s_path, a, (int32_t)rank, S);
+        else
+            compact_row(kv, p.n_layers, p.kv_elem_bytes, p.n_kv_heads, p.head_dim, p.kv_stride_b, p.kv_stride_h,
+                        p.kv_stride_s, bk, len0, s_path, a);
+    }
     // next-round hidden state
     if (p.hidden_out != nullptr) {
         const int64_t bytes = (int64_t)p.hidden_dim * p.hidden_elem_bytes;
         const uint8_t* src = static_cast<const uint8_t*>(p.tree_hidden) + ((int64_t)b * p.nmax + s_path[a - 1]) * bytes;
         uint8_t* dst = static_cast<uint8_t*>(p.hidden_out) + (int64_t)b * bytes;
-        for (int64_t o = (int64_t)tid * 16; o < bytes; o += (int64_t)blockDim.x * 16)
+        for (int64_t o = ((int64_t)rank * blockDim.x + tid) * 16; o < bytes; o += (int64_t)S * blockDim.x * 16)
             *reinterpret_cast<uint4*>(dst + o) = *reinterpret_cast<const uint4*>(src + o);
     }
-    __syncthreads();
-    if (tid == 0) {
+    if constexpr (S > 1)
+        cl_sync();
+    else
+        __syncthreads();
+    if (rank == 0 && tid == 0) {
         if (p.update_len) p.row_len[b] = len0 + a;
         if (fin && p.active != nullptr) p.active[b] = 0;
     }
@@ -284,6 +357,36 @@ __global__ void extract_path_kernel(KvPtrs kv, int32_t n_layers, int32_t elem_by
     __syncthreads();
     if (a <= 0) return;
     compact_row(kv, n_layers, elem_bytes, n_heads, head_dim, sb, sh, ss, b, row_len[b], path, a);
+}
+
+using AcceptKernel = void (*)(AcceptParams, KvPtrs);
+
+static cudaError_t launch_accept(AcceptKernel kernel, int32_t B, cudaStream_t st, const AcceptParams& p,
+                                 const KvPtrs& kv) {
+    kernel<<<B, FG_SAMPLE_LANES, 0, st>>>(p, kv);
+    return cudaSuccess;
+}
+
+static cudaError_t launch_accept_cluster(AcceptKernel kernel, int32_t B, cudaStream_t st, const AcceptParams& p,
+                                         const KvPtrs& kv) {
+    const int64_t ebuf = cluster_ebuf_bytes(p.vocab);
+    if (ebuf > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ebuf);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)B * kAcceptCtas);
+    cfg.blockDim = dim3(kAcceptClusterThreads);
+    cfg.dynamicSmemBytes = (size_t)ebuf;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAcceptCtas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p, kv);
 }
 
 static bool kv_aligned(int32_t elem_bytes, int32_t head_dim, int64_t sb, int64_t sh, int64_t ss) {
@@ -384,18 +487,31 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
         if (s != FG_OK) return s;
         p.drawn = a->drawn;
     }
+    // fg-icdf-v1 draws in the walk run on a cluster of kAcceptCtas CTAs per row
+    const bool nucleus = a->do_sample && a->temperature != 0.0f && a->top_p > 0.0f && a->top_p < 1.0f;
+    // (the e_i buffer of one chunk group within 96 KB: V up to ~95k x 8 entries)
+    const bool clustered = !parallel && a->do_sample && a->temperature > 0.0f && !nucleus &&
+                           sample_chunk_len(a->vocab) <= kFindWarpMax && cluster_ebuf_bytes(a->vocab) <= 96 * 1024;
+    cudaError_t e = cudaSuccess;
     switch (a->logits_dtype) {
         case FG_DTYPE_F32:
-            accept_extract_kernel<float><<<a->B, FG_SAMPLE_LANES, 0, st>>>(p, kv);
+            e = clustered ? launch_accept_cluster(accept_extract_kernel<float, kAcceptCtas>, a->B, st, p, kv)
+                          : launch_accept(accept_extract_kernel<float, 1>, a->B, st, p, kv);
             break;
         case FG_DTYPE_BF16:
-            accept_extract_kernel<__nv_bfloat16><<<a->B, FG_SAMPLE_LANES, 0, st>>>(p, kv);
+            e = clustered ? launch_accept_cluster(accept_extract_kernel<__nv_bfloat16, kAcceptCtas>, a->B, st, p, kv)
+                          : launch_accept(accept_extract_kernel<__nv_bfloat16, 1>, a->B, st, p, kv);
             break;
         case FG_DTYPE_F16:
-            accept_extract_kernel<__half><<<a->B, FG_SAMPLE_LANES, 0, st>>>(p, kv);
+            e = clustered ? launch_accept_cluster(accept_extract_kernel<__half, kAcceptCtas>, a->B, st, p, kv)
+                          : launch_accept(accept_extract_kernel<__half, 1>, a->B, st, p, kv);
             break;
         default:
             return FG_EINVAL;
+    }
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return FG_ECUDA;
     }
     return launch_status();
 }

@@ -132,6 +132,28 @@ __device__ __forceinline__ float scaled_logit(const void* row, int32_t dtype, in
     return v;
 }
 
+// --------------------------------------------------------- cluster helpers
+// Rank of this CTA in its thread-block cluster.
+__device__ __forceinline__ uint32_t cl_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Every thread of every CTA of the cluster arrives and waits; shared-memory
+// writes before it are visible to the cluster's loads after it.
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of CTA `rank`'s copy of the shared variable at
+// `p` (distributed shared memory).
+__device__ __forceinline__ uint32_t cl_addr(const void* p, uint32_t rank) {
+    uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(p)), remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(rank));
+    return remote;
+}
+
 // ---------------------------------------------------------- block helpers
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

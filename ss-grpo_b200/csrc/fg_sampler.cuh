@@ -19,7 +19,7 @@ constexpr int kFindWarpMax = 1024;
 
 struct SampleSmem {
     float P[FG_SAMPLE_LANES + 1];
-    float e[kFindWarpMax];  // the searched chunk's e_i
+    alignas(16) float e[kFindWarpMax];  // the searched chunk's e_i
     float red[FG_SAMPLE_LANES / 32];
     int32_t redi[FG_SAMPLE_LANES / 32];
     int32_t result;
@@ -74,6 +74,60 @@ __device__ __forceinline__ int32_t block_best(float bv, int32_t bi, SampleSmem& 
 }
 
 // Row maximum (raw values) and its first index.
+// One warp writes e_i = fg_exp(x_i / T - m) of entries [lo, hi) (at most
+// kFindWarpMax) of a row to e[0, hi - lo): whole 16-byte vectors, every lane's
+// loads issued before they are used, when the row allows it.
+template <typename T>
+__device__ __forceinline__ void warp_chunk_exps(const T* row, int32_t lo, int32_t hi, float m, float temperature,
+                                                bool vec, float* e) {
+    const int lane = threadIdx.x & 31;
+    constexpr int NV = Vec<T>::N;
+    constexpr int PER = (kFindWarpMax / NV + 31) / 32;
+    if (vec && lo % NV == 0) {
+        const int32_t nv = (hi - lo) / NV;  // hi - lo is a multiple of NV here
+        uint4 q[PER];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int32_t v = lane + 32 * j;
+            q[j] = v < nv ? ldg16(row + lo + (int64_t)v * NV) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int32_t v = lane + 32 * j;
+            if (v < nv) {
+                float f[NV];
+                unpack<T>(q[j], f);
+#pragma unroll
+                for (int k = 0; k < NV; ++k) e[v * NV + k] = fg_exp(__fsub_rn(scale_t(f[k], temperature), m));
+            }
+        }
+    } else {
+        for (int32_t i = lo + lane; i < hi; i += 32) e[i - lo] = fg_exp(__fsub_rn(scale_t(to_f<T>(row[i]), temperature), m));
+    }
+    __syncwarp();
+}
+
+// The first i in [0, n) where base + (e[0] + ... + e[i]) > target, the sum
+// taken left to right in fp32 (one lane), or -1.  The values are read 16 at
+// a time ahead of their additions; the additions and comparisons are the
+// sequential ones, and none happens past the answer.
+__device__ __forceinline__ int32_t scan_chunk(const float* e, int32_t n, float base, float target) {
+    float c = 0.0f;
+    for (int32_t i0 = 0; i0 < n; i0 += 16) {
+        float4 q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[j] = reinterpret_cast<const float4*>(e + i0)[j];
+        const float* v = reinterpret_cast<const float*>(q);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (i0 + j >= n) return -1;
+            c = __fadd_rn(c, v[j]);
+            if (__fadd_rn(base, c) > target) return i0 + j;
+        }
+    }
+    return -1;
+}
+
 template <typename T>
 __device__ __forceinline__ void row_max(const T* row, int32_t V, float& bv, int32_t& bi) {
     bv = -INFINITY;
@@ -222,21 +276,10 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
         const int32_t t = sm.redi[0];
         if (tid < 32 && t >= 0) {
             const int32_t lo_t = min(t * C, V), hi_t = min(lo_t + C, V);
-            for (int32_t i = lo_t + tid; i < hi_t; i += 32)
-                sm.e[i - lo_t] = fg_exp(__fsub_rn(scale_t(to_f<T>(row[i]), temperature), m));
-            __syncwarp();
+            warp_chunk_exps<T>(row, lo_t, hi_t, m, temperature, vec, sm.e);
             if (tid == 0) {
-                const float base = sm.P[t];
-                float c = 0.0f;
-                int32_t found = -1;
-                for (int32_t i = 0; i < hi_t - lo_t; ++i) {
-                    c = __fadd_rn(c, sm.e[i]);
-                    if (__fadd_rn(base, c) > target) {
-                        found = lo_t + i;
-                        break;
-                    }
-                }
-                sm.result = found;
+                const int32_t i = scan_chunk(sm.e, hi_t - lo_t, sm.P[t], target);
+                sm.result = i < 0 ? -1 : lo_t + i;
             }
         }
     }
@@ -244,6 +287,213 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
     const int32_t r = sm.result;
     __syncthreads();
     return r;
+}
+
+// ------------------------------------------------- cluster-wide fg-icdf-v1
+// The draw of block_sample with a row spread over a cluster of S CTAs of NT
+// threads; CTA r owns chunks [r * 512 / S, (r + 1) * 512 / S).
+//   pass 1  every CTA takes the maximum of its part of the row and stores it
+//           into every CTA (distributed shared memory); the row maximum is
+//           the same value block_sample finds (only the value enters the
+//           draw, as x - m: a signed zero gives the same e_i either way).
+//   pass 2  in groups of kClusterChunkGroup chunks, all NT threads compute
+//           the group's e_i = fg_exp(x_i / T - m) into shared memory (each
+//           e_i alone, so they run in parallel), then thread c adds chunk
+//           c's e_i left to right -- the chunk total of block_sample, the
+//           same additions in the same order -- and stores it into CTA 0.
+//   find    CTA 0 forms the sequential prefix of the 512 totals, finds the
+//           target chunk and searches it exactly as block_sample does, and
+//           stores the token into every CTA.
+// All distributed-shared-memory traffic is stores before a cluster barrier
+// and local reads after it, so no CTA reads a peer's memory after the peer
+// may have exited.
+constexpr int kClusterChunkGroup = 32;
+
+template <int S, int NT>
+struct ClusterSampleSmem {
+    float P[FG_SAMPLE_LANES + 1];  // chunk totals, then their prefix (CTA 0)
+    alignas(16) float e[kFindWarpMax];  // the searched chunk's e_i (CTA 0)
+    float mv[S];                   // every CTA's maximum
+    float red[NT / 32];
+    int32_t target_chunk;
+    int32_t result;
+};
+
+// Floats of the e_i buffer (dynamic shared memory) for vocabulary V: one
+// group of chunks, each row padded to a multiple of 4 floats plus 4 so the
+// summing threads' 16-byte reads fall in distinct banks.
+__host__ __device__ __forceinline__ int32_t cluster_ebuf_stride(int32_t V) { return sample_chunk_len(V) + 4; }
+__host__ __device__ __forceinline__ int64_t cluster_ebuf_bytes(int32_t V) {
+    return (int64_t)kClusterChunkGroup * cluster_ebuf_stride(V) * 4;
+}
+
+// st.shared::cluster of one value into CTA `rank`'s copy of the variable.
+__device__ __forceinline__ void cl_st_f32(float* p, uint32_t rank, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cl_addr(p, rank)), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cl_st_s32(int32_t* p, uint32_t rank, int32_t v) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cl_addr(p, rank)), "r"(v) : "memory");
+}
+
+template <typename T, int S, int NT>
+__device__ int32_t cluster_sample(const T* row, int32_t V, float temperature, float u, ClusterSampleSmem<S, NT>& cs,
+                                  float* ebuf) {
+    constexpr int CPC = FG_SAMPLE_LANES / S;  // chunks per CTA
+    static_assert(CPC % kClusterChunkGroup == 0, "chunk groups tile a CTA's chunks");
+    const int tid = threadIdx.x;
+    const uint32_t rank = cl_rank();
+    const int32_t C = sample_chunk_len(V);
+    const bool vec = row_vectorizable<T>(row, V);
+    constexpr int NV = Vec<T>::N;
+    // pass 1: maximum of this CTA's part [rank * CPC * C, ...) of the row
+    {
+        const int32_t lo = min((int32_t)rank * CPC * C, V), hi = min(lo + CPC * C, V);
+        float bv = -INFINITY;
+        if (vec) {
+            const int32_t nvec = (hi - lo) / NV;  // lo, hi: multiples of C (a multiple of 8) or V
+            const T* base = row + lo;
+            for (int32_t v0 = tid; v0 < nvec; v0 += 8 * NT) {
+                uint4 q[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int32_t v = v0 + k * NT;
+                    q[k] = v < nvec ? ldg16(base + (int64_t)v * NV) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (v0 + k * NT >= nvec) break;
+                    float f[NV];
+                    unpack<T>(q[k], f);
+#pragma unroll
+                    for (int e = 0; e < NV; ++e) bv = fmaxf(bv, f[e]);
+                }
+            }
+        } else {
+            for (int32_t i = lo + tid; i < hi; i += NT) bv = fmaxf(bv, to_f<T>(row[i]));
+        }
+        bv = warp_max(bv);
+        if ((tid & 31) == 0) cs.red[tid >> 5] = bv;
+        __syncthreads();
+        if (tid < S) {
+            float m = cs.red[0];
+#pragma unroll
+            for (int w = 1; w < NT / 32; ++w) m = fmaxf(m, cs.red[w]);
+            cl_st_f32(&cs.mv[rank], tid, m);
+        }
+    }
+    cl_sync();  // (A) every CTA holds every CTA's maximum
+    float mraw = cs.mv[0];
+#pragma unroll
+    for (int r = 1; r < S; ++r) mraw = fmaxf(mraw, cs.mv[r]);
+    const float m = scale_t(mraw, temperature);
+    // pass 2: e_i of a group of chunks in parallel, then each chunk's total
+    const int32_t stride = cluster_ebuf_stride(V);
+    for (int grp = 0; grp < CPC; grp += kClusterChunkGroup) {
+        const int32_t c0 = (int32_t)rank * CPC + grp;  // first (global) chunk of the group
+        if (vec) {
+            // the group's vectors (chunk, vector) dealt round-robin; a batch
+            // of kBatch loads is issued before any is used
+            constexpr int kBatch = 6;
+            const int32_t vpc = C / NV;  // vectors per chunk
+            const int32_t items = kClusterChunkGroup * vpc;
+            for (int32_t it0 = tid; it0 < items; it0 += kBatch * NT) {
+                uint4 q[kBatch];
+                int32_t at[kBatch];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    const int32_t it = it0 + j * NT;
+                    const int32_t lc = it / vpc, v = it - lc * vpc;
+                    const int32_t i0 = (c0 + lc) * C + v * NV;
+                    at[j] = (it < items && i0 < V) ? lc * stride + v * NV : -1;
+                    q[j] = at[j] >= 0 ? ldg16(row + i0) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    if (at[j] < 0) continue;
+                    float f[NV];
+                    unpack<T>(q[j], f);
+                    float* dst = ebuf + at[j];
+#pragma unroll
+                    for (int e = 0; e < NV; e += 4)
+                        *reinterpret_cast<float4*>(dst + e) =
+                            make_float4(fg_exp(__fsub_rn(scale_t(f[e], temperature), m)),
+                                        fg_exp(__fsub_rn(scale_t(f[e + 1], temperature), m)),
+                                        fg_exp(__fsub_rn(scale_t(f[e + 2], temperature), m)),
+                                        fg_exp(__fsub_rn(scale_t(f[e + 3], temperature), m)));
+                }
+            }
+        } else {
+            for (int32_t it = tid; it < kClusterChunkGroup * C; it += NT) {
+                const int32_t lc = it / C, o = it - lc * C;
+                const int32_t i = (c0 + lc) * C + o;
+                if (i < V) ebuf[lc * stride + o] = fg_exp(__fsub_rn(scale_t(to_f<T>(row[i]), temperature), m));
+            }
+        }
+        __syncthreads();
+        if (tid < kClusterChunkGroup) {
+            const int32_t g = c0 + tid;
+            const int32_t n = max(0, min(g * C + C, V) - g * C);  // entries of chunk g
+            const float* src = ebuf + tid * stride;
+            float c = 0.0f;
+            int32_t i = 0;
+            // 16 values loaded ahead of their 16 additions
+            for (; i + 16 <= n; i += 16) {
+                float4 q[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) q[j] = *reinterpret_cast<const float4*>(src + i + 4 * j);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    c = __fadd_rn(c, q[j].x);
+                    c = __fadd_rn(c, q[j].y);
+                    c = __fadd_rn(c, q[j].z);
+                    c = __fadd_rn(c, q[j].w);
+                }
+            }
+            for (; i < n; ++i) c = __fadd_rn(c, src[i]);
+            cl_st_f32(&cs.P[g + 1], 0, c);
+        }
+        __syncthreads();  // the next group overwrites the buffer
+    }
+    cl_sync();  // (B) CTA 0 holds the 512 chunk totals
+    if (rank == 0) {
+        if (tid == 0) {
+            // the specified sequential sum, its loads batched ahead of the adds
+            float P = 0.0f;
+            cs.P[0] = 0.0f;
+            for (int t0 = 0; t0 < FG_SAMPLE_LANES; t0 += 16) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = cs.P[t0 + j + 1];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    P = __fadd_rn(P, v[j]);
+                    cs.P[t0 + j + 1] = P;
+                }
+            }
+            cs.target_chunk = -1;
+        }
+        __syncthreads();
+        const float target = __fmul_rn(u, cs.P[FG_SAMPLE_LANES]);
+        for (int t = tid; t < FG_SAMPLE_LANES; t += NT)
+            if (cs.P[t] <= target && target < cs.P[t + 1]) cs.target_chunk = t;
+        __syncthreads();
+        const int32_t t = cs.target_chunk;
+        if (tid < 32) {
+            int32_t found = -1;
+            if (t >= 0) {
+                const int32_t lo_t = min(t * C, V), hi_t = min(lo_t + C, V);
+                warp_chunk_exps<T>(row, lo_t, hi_t, m, temperature, vec, cs.e);
+                if (tid == 0) {
+                    const int32_t i = scan_chunk(cs.e, hi_t - lo_t, cs.P[t], target);
+                    found = i < 0 ? -1 : lo_t + i;
+                }
+            }
+            const int32_t tok = __shfl_sync(0xffffffffu, found, 0);
+            if (tid < S) cl_st_s32(&cs.result, tid, tok);
+        }
+    }
+    cl_sync();  // (C) every CTA holds the token
+    return cs.result;
 }
 
 }  // namespace fg

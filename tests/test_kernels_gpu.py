@@ -117,6 +117,34 @@ def test_row_topk_stable_and_lse(ops, dtype, V, k):
     assert torch.allclose(lse.cpu(), ref_lse, rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("dtype,V,k,rows", [(torch.bfloat16, 151936, 4, 128), (torch.bfloat16, 151936, 8, 9),
+                                            (torch.float32, 4096, 1, 20), (torch.bfloat16, 97, 16, 5),
+                                            (torch.float16, 128256, 2, 7), (torch.bfloat16, 13, 3, 3)])
+def test_row_topk_without_lse_spreads_rows_over_clusters(ops, dtype, V, k, rows):
+    """Without the logsumexp a row runs on an 8-CTA cluster (one vocabulary
+    slice per CTA, merged through distributed shared memory): indices,
+    values and maxima equal the CPU stable top-k and the one-CTA kernel's."""
+    g = torch.Generator().manual_seed(V + k)
+    x = (torch.randn(rows, V, generator=g) * 2).to(dtype)
+    x[rows // 2, :] = 0.5  # every entry tied
+    if V > 64:
+        x[0, V - 3:] = 40.0  # the best entries in the last slice
+    xd = x.to(DEV)
+    idx, val, mx, lse = ops.row_topk(xd, k, with_lse=False)
+    assert lse is None
+    idx1, val1, mx1, _ = ops.row_topk(xd, k)
+    assert torch.equal(idx, idx1) and torch.equal(val, val1) and torch.equal(mx, mx1)
+    for r in range(rows):
+        ri, rv = orc.topk_stable(x[r].float().numpy(), k)
+        assert np.array_equal(idx[r].cpu().numpy(), ri), r
+        assert np.array_equal(val[r].cpu().numpy(), rv), r
+    # a strided view (rows of a wider buffer)
+    wide = torch.zeros(rows, V + 64, dtype=dtype, device=DEV)
+    wide[:, :V] = xd
+    idx2, val2, mx2, _ = ops.row_topk(wide[:, :V], k, with_lse=False)
+    assert torch.equal(idx2, idx1) and torch.equal(val2, val1)
+
+
 # ---------------------------------------------------- fused lm_head + top-k
 @pytest.mark.parametrize("M,H,V,n_write,row0,k,lse", [
     (192, 1536, 151936, 64, 64, 4, False),   # config 2: 64 root rows + 2 heads x 64 rows
