@@ -64,8 +64,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=sorted(RUNS), default=2,
                     help="benchmark configuration (2: the headline; 3, 4: the 7B / 8B-shaped per-GPU shards)")
-    ap.add_argument("--sweep", choices=["attention"], default=None,
-                    help="config 5 instead: tree attention + extract_path over prefix length x nodes x batch")
+    ap.add_argument("--sweep", choices=["attention", "lm-head"], default=None,
+                    help="attention: config 5, tree attention + extract_path over prefix length x nodes x batch; "
+                         "lm-head: config 2's proposal lm_head, the reference's separate leaf recompute against "
+                         "the one fused projection")
     ap.add_argument("--sweep-max-gb", type=float, default=80.0,
                     help="skip sweep points whose K/V cache exceeds this many GB")
     ap.add_argument("--sweep-only", default=None,
@@ -646,6 +648,67 @@ def run_sweep(args, local_rank: int) -> dict:
             "points": points}
 
 
+def run_lmhead_sweep(args, local_rank: int) -> dict:
+    """Config 2's vocabulary projections around a round boundary (H 1536,
+    V 151,936, bf16, 64 rows, 2 active MEDUSA heads, top-4), timed alone
+    with CUDA graphs over 3 rotating weight copies (1.4 GB, so every call
+    streams its 467 MB of weights from HBM):
+      reference  the leaf-logit recompute after acceptance
+                 (flash_medusa_decoder.py:2836-2862: lm_head on the 64 last
+                 accepted hidden states) and, next round, the heads' lm_head
+                 on 128 rows + their top-k: two weight streams;
+      fused      this repository's round: the last accepted hidden state is
+                 gathered by K4 and projected in the next round's one GEMM
+                 together with the head rows (M = 192) + the top-k of the
+                 head rows: one weight stream;
+      tcgen05    the same fused projection as fg_lm_head_topk (the top-k in
+                 the GEMM epilogue)."""
+    import torch
+
+    from flashgrpo_b200 import ops
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    B, H, V, k, heads = 64, 1536, 151936, 4, 2
+    g = torch.Generator(device=device).manual_seed(3)
+    W = [torch.randn(V, H, device=device, generator=g).mul_(0.02).to(torch.bfloat16) for _ in range(3)]
+    X = torch.randn((1 + heads) * B, H, device=device, generator=g).to(torch.bfloat16)
+    logits = torch.empty((1 + heads) * B, V, device=device, dtype=torch.bfloat16)
+    n_top = heads * B
+    tk = (torch.empty((n_top, k), dtype=torch.int32, device=device), torch.empty((n_top, k), device=device),
+          torch.empty(n_top, device=device), None)
+    ws = torch.empty(max(ops.lm_head_topk_workspace_bytes(X.shape[0], V, B, k), 16) // 4 + 64, dtype=torch.int32,
+                     device=device)
+
+    def reference(i):
+        w = W[i % 3]
+        torch.mm(X[:B], w.t(), out=logits[:B])          # leaf recompute after acceptance
+        torch.mm(X[B:], w.t(), out=logits[B:])          # next round: the heads' projection
+        ops.row_topk(logits[B:], k, out=tk, with_lse=False)
+
+    def fused(i):
+        torch.mm(X, W[i % 3].t(), out=logits)
+        ops.row_topk(logits[B:], k, out=tk, with_lse=False)
+
+    def tcgen05(i):
+        ops.lm_head_topk(X, W[i % 3], n_logit_rows=B, logits=logits, topk_row0=B, k=k, topk_out=tk, workspace=ws)
+
+    peak, _ = measured_peaks()
+    out = {"sweep": "config 2 proposal lm_head: the reference's separate leaf-logit recompute against one fused "
+                    "projection (64 rows, 2 heads, H 1536, V 151,936, bf16, top-4)", "variants": {}}
+    for name, fn, streams in (("reference", reference, 2), ("fused", fused, 1), ("tcgen05", tcgen05, 1)):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        ms, n = graph_time([lambda i=i: fn(i) for i in range(3)])
+        wbytes = streams * V * H * 2
+        out["variants"][name] = {"us": ms * 1e3, "weight_streams": streams,
+                                 "weight_GB_s": wbytes / (ms * 1e-3) / 1e9, "hbm_frac": wbytes / (ms * 1e-3) / 1e9 / peak,
+                                 "calls_timed": n}
+        print(f"{name:10s} {ms * 1e3:8.1f} us  {streams} weight stream(s)", file=sys.stderr, flush=True)
+    return out
+
+
 # ------------------------------------------------------------- CPU oracle
 def cpu_oracle_round_rate(warm_rounds: int, timed_rounds: int, rows: int = 64, prefix: int = 1024, cfg_id: int = 2):
     """The oracle's restatement of the reference generate loop on the host
@@ -729,7 +792,8 @@ def main():
         return 0
     if args.sweep is not None:
         if rank == 0:
-            print(json.dumps(run_sweep(args, local_rank)), flush=True)
+            fn = run_sweep if args.sweep == "attention" else run_lmhead_sweep
+            print(json.dumps(fn(args, local_rank)), flush=True)
         return 0
     import torch
     import torch.distributed as dist

@@ -383,9 +383,16 @@ typedef struct fg_accept_args {
     const int32_t *plan_out;   /* [16] or NULL */
     int32_t internal_rows;     /* packed logits rows = grid of the draws */
     int32_t *drawn;            /* [internal_rows] int32 scratch, or NULL */
+    /* Round counters, each NULL to skip it: *acc_total += the rows' acc_len
+     * (the round's accepted tokens), *round_counter += 1 (the round index the
+     * next fg_philox_uniforms call reads). */
+    int64_t *acc_total;
+    int32_t *round_counter;
 } fg_accept_args;
 
-/* One CTA per row: the exact_target walk of exact_accept_paths_batch
+/* One CTA per row (fg-icdf-v1 draws: a cluster of 8 CTAs per row that
+ * shares each draw's exponentials, see fg_accept.cu): the exact_target walk
+ * of exact_accept_paths_batch
  * (flashgrpo_b200/decoding/acceptance.py:183-267), the post-accept clip /
  * EOS / pending-correction rules (flash_medusa_decoder.py:2289-2343), the
  * extract_path compaction of the accepted slots in every layer

@@ -68,6 +68,8 @@ struct AcceptParams {
     const int32_t* kv_rows;  // row -> cache row for the compaction (NULL = identity)
     int32_t kv_batch;
     const int32_t* drawn;    // parallel draws per packed logits row (NULL = draw during the walk)
+    int64_t* acc_total;      // += the rows' acc_len (NULL = skip)
+    int32_t* round_counter;  // += 1 per call (NULL = skip)
 };
 
 // CTAs per row and threads per CTA of the clustered walk
@@ -177,6 +179,7 @@ __global__ void __launch_bounds__(S > 1 ? kAcceptClusterThreads : FG_SAMPLE_LANE
             p.pending[b] = -1;
             p.last_node[b] = 0;
             p.finished[b] = 1;
+            if (p.round_counter != nullptr && b == 0) atomicAdd(p.round_counter, 1);
         }
         return;
     }
@@ -305,6 +308,8 @@ __global__ void __launch_bounds__(S > 1 ? kAcceptClusterThreads : FG_SAMPLE_LANE
     if (rank == 0 && tid == 0) {
         if (p.update_len) p.row_len[b] = len0 + a;
         if (fin && p.active != nullptr) p.active[b] = 0;
+        if (p.acc_total != nullptr) atomicAdd(reinterpret_cast<unsigned long long*>(p.acc_total), (unsigned long long)a);
+        if (p.round_counter != nullptr && b == 0) atomicAdd(p.round_counter, 1);
     }
 }
 
@@ -457,6 +462,8 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     p.kv_rows = a->kv_rows;
     p.kv_batch = a->kv_batch;
     p.drawn = nullptr;
+    p.acc_total = a->acc_total;
+    p.round_counter = a->round_counter;
     const bool parallel = a->drawn != nullptr;
     if (parallel && (!a->internal || !a->depths || a->internal_rows <= 0 || a->parent_stride != 0)) return FG_EINVAL;
     KvPtrs kv;

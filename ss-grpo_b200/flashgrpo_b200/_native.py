@@ -64,6 +64,7 @@ class AcceptArgs(ctypes.Structure):
         ("kv_stride_h", c_i64), ("kv_stride_s", c_i64), ("tree_hidden", c_vp), ("hidden_out", c_vp),
         ("hidden_dim", c_i32), ("hidden_elem_bytes", c_i32), ("kv_rows", c_vp), ("kv_batch", c_i32),
         ("internal", c_vp), ("depths", c_vp), ("plan_out", c_vp), ("internal_rows", c_i32), ("drawn", c_vp),
+        ("acc_total", c_vp), ("round_counter", c_vp),
     ]
 
 

@@ -299,7 +299,6 @@ class RoundBuffers:
         for k in ("acc_len", "correction", "last_node", "finished"):
             self.out[k] = torch.empty(B, **i32)
         self.acc_sum = torch.zeros(1, dtype=torch.int64, **f)
-        self.corr_used = torch.zeros(1, dtype=torch.int64, **f)
         ws = ops.attention_workspace_bytes(B, N_, spec.n_q_heads, spec.n_kv_heads, spec.head_dim, num_splits=0,
                                            max_kv_len=0)
         self.ws_bytes = ws
@@ -818,7 +817,6 @@ class VerifyEngine:
                 torch.mm(rb.hid_int, self.w.lm_head.t(), out=rb.tree_logits)
         if phase_event is not None:
             phase_event.record()
-        rb.corr_used += (st.pending >= 0).sum()
         outs = dict(rb.out)
         outs["pending"] = st.pending
         ops.accept_extract(logits=rb.tree_logits, slot=rb.tree["slot"], tokens=rb.tree["tokens"],
@@ -829,9 +827,8 @@ class VerifyEngine:
                            v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,
                            hidden_out=st.hidden, kv_rows=st.rows if isinstance(st, RoundView) else None,
                            parallel=(rb.tree["internal"], rb.tree["depths"], rb.tree["plan"], rb.drawn)
-                           if rb.n_int > 0 and cfg.parallel_draws else None)
-        rb.acc_sum += rb.out["acc_len"].sum()
-        st.round_dev += 1
+                           if rb.n_int > 0 and cfg.parallel_draws else None,
+                           acc_total=rb.acc_sum, round_counter=st.round_dev)
 
     def view(self, st: DecodeState, B: int, n_heads: int) -> RoundView:
         """A (cached) compact view of B of st's rows; fill view.rows before

@@ -352,13 +352,15 @@ def layer_pointer_arrays(k_layers, v_layers):
 def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
                    row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
                    tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0,
-                   top_p: float = 1.0, kv_rows=None, parallel=None):
+                   top_p: float = 1.0, kv_rows=None, parallel=None, acc_total=None, round_counter=None):
     """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
     acc_len/correction/pending/last_node/finished [B]; kv_rows (int32 [B],
     optional): row b compacts cache row kv_rows[b] of k_layers/v_layers.
     parallel (optional, shared topology): (internal [nmax], depths [nmax],
     plan_out [16] or None, drawn int32 [logits rows]) -- every internal
-    node's draw in parallel before the walk (the same tokens)."""
+    node's draw in parallel before the walk (the same tokens).  acc_total
+    (int64 [1]) and round_counter (int32 [1]), optional: the round's
+    accepted tokens are added to the first, 1 to the second."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     for name, t in (("slot", slot), ("tokens", tokens), ("parents", parents), ("row_len", row_len)):
@@ -394,6 +396,12 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
     if hidden_out is not None:
         a.tree_hidden, a.hidden_out = tree_hidden.data_ptr(), hidden_out.data_ptr()
         a.hidden_dim, a.hidden_elem_bytes = hidden_out.shape[-1], hidden_out.element_size()
+    if acc_total is not None:
+        _need(acc_total, "acc_total", torch.int64)
+        a.acc_total = acc_total.data_ptr()
+    if round_counter is not None:
+        _need(round_counter, "round_counter", torch.int32)
+        a.round_counter = round_counter.data_ptr()
     n_launch = 1
     if parallel is not None:
         internal, depths, plan_out, drawn = parallel

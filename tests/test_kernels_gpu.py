@@ -454,12 +454,18 @@ def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sa
     for k in ("acc_len", "correction", "pending", "last_node", "finished"):
         outs[k] = torch.full((B,), -9, dtype=torch.int32, device=DEV)
     rl = row_len.clone()
+    acc_total = torch.full((1,), 5, dtype=torch.int64, device=DEV)
+    round_counter = torch.full((1,), 11, dtype=torch.int32, device=DEV)
     ops.accept_extract(logits=logits, slot=slots, tokens=tokens, parents=parents, n_nodes=n_nodes,
                        uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
                        max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=parallel is not None,
                        k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out,
-                       top_p=top_p, kv_rows=kv_rows, parallel=parallel)
+                       top_p=top_p, kv_rows=kv_rows, parallel=parallel, acc_total=acc_total,
+                       round_counter=round_counter)
     torch.cuda.synchronize()
+    # the round counters: accepted tokens added up, one round counted
+    assert int(acc_total) == 5 + int(outs["acc_len"].sum())
+    assert int(round_counter) == 12
     return outs, rl
 
 
