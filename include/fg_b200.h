@@ -109,7 +109,9 @@ fg_status fg_sample_rows(const void *logits, int32_t dtype, int64_t row_stride, 
 /* Per row: the k best entries ordered by (value descending, index
  * ascending), the row maximum and logsumexp (rounded to the logits dtype,
  * as torch.logsumexp returns it; out_lse may be NULL to skip it, as only
- * adaptive trees use it).  k <= FG_MAX_TOPK.  Replaces torch.topk in
+ * adaptive trees use it).  k <= FG_MAX_TOPK.  Without out_lse every row
+ * runs on a cluster of 8 CTAs (a threshold selection over vocabulary
+ * slices); the result is the same.  Replaces torch.topk in
  * build_batch_trees (flashgrpo_b200/decoding/medusa_tree.py:767) and the
  * confidence reductions (flash_medusa_decoder.py:1034-1040). */
 fg_status fg_row_topk(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
