@@ -223,3 +223,44 @@ def test_result_dict_covers_the_reference_keys(golden_dir):
     assert abs(res["tree_verify_time_cost"] - 0.02 * 6 / 9) < 1e-12
     assert abs(res["medusa_head_time_cost"] + res["tree_verify_time_cost"] + res["cache_update_time_cost"]
                - 0.02) < 1e-12
+
+
+def test_bench_workloads_and_sweep_helpers():
+    """bench.py's host side: the three GPU configurations' tree plans (config
+    2: [4, 2] with 13 nodes; config 3: 4 heads, adaptive widths 2..8, 32
+    nodes; config 4: chain proposals within 64 nodes), the config-5 trees
+    (parents before children, depth <= 4 so accepted paths fit) and the
+    single-point sweep option."""
+    import sys
+    from pathlib import Path
+
+    import torch
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    import bench
+
+    c2 = bench.workload_config(2, 64, 1024, 28, 1)
+    assert (c2["tree"], c2["tree_nodes"], c2["active_heads"]) == ([4, 2], 13, 2)
+    c3 = bench.workload_config(3, 16, 2048, 28, 1)
+    assert c3["tree_nodes"] == 32 and c3["medusa_heads"] == 4 and c3["adaptive_topk"] == [2, 8]
+    c4 = bench.workload_config(4, 32, 4096, 32, 1)
+    assert c4["proposal_mode"] == "chain" and c4["tree_nodes"] <= 64 and c4["layers"] == 32
+    # the sharded global batch: every rank's config names its own rollouts
+    assert bench.workload_config(2, 64, 1024, 28, 8)["parallelism"].startswith("dp8")
+    g = torch.Generator().manual_seed(7)
+    for n in (1, 8, 16, 64, 128):
+        parents = bench.random_tree(n, g)
+        assert parents[0] == -1 and all(0 <= parents[j] < j for j in range(1, n))
+        depth = [0] * n
+        for j in range(1, n):
+            depth[j] = depth[parents[j]] + 1
+        assert max(depth) <= 4
+    old = sys.argv
+    try:
+        sys.argv = ["bench.py", "--sweep", "attention", "--sweep-only", "1024:8:32,16384:128:1"]
+        args = bench.parse_args()
+    finally:
+        sys.argv = old
+    assert args.sweep == "attention" and args.sweep_only == "1024:8:32,16384:128:1"
+    assert (args.rows, args.prefix, args.e2e_prompt, args.e2e_len) == (64, 1024, 256, 1024)
