@@ -40,6 +40,32 @@ __device__ __forceinline__ float scale_t(float v, float temperature) {
     return temperature > 0.0f && temperature != 1.0f ? __fdiv_rn(v, temperature) : v;
 }
 
+// The specified sequential prefix of the FG_SAMPLE_LANES chunk totals held
+// in P[1 .. FG_SAMPLE_LANES], in place (P[0] = 0, P[t + 1] = P[t] + total t,
+// left to right in fp32), by one thread: each batch of 8 totals is loaded
+// while the previous batch is added.
+__device__ __forceinline__ void sequential_prefix(float* P) {
+    constexpr int kB = 8;
+    float acc = 0.0f;
+    P[0] = 0.0f;
+    float v[kB], w[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) v[j] = P[j + 1];
+    for (int t0 = 0; t0 < FG_SAMPLE_LANES; t0 += kB) {
+        if (t0 + kB < FG_SAMPLE_LANES) {
+#pragma unroll
+            for (int j = 0; j < kB; ++j) w[j] = P[t0 + kB + j + 1];
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            acc = __fadd_rn(acc, v[j]);
+            P[t0 + j + 1] = acc;
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) v[j] = w[j];
+    }
+}
+
 // Block-wide (max value, lowest index) reduction; returns the index.
 __device__ __forceinline__ int32_t block_best(float bv, int32_t bi, SampleSmem& sm) {
     const int tid = threadIdx.x;
@@ -243,19 +269,7 @@ __device__ int32_t block_sample(const T* row, int32_t V, float temperature, bool
     if (tid == 0) sm.result = -1;
     __syncthreads();
     if (tid == 0) {
-        // the specified sequential sum, its loads batched ahead of the adds
-        float P = 0.0f;
-        sm.P[0] = 0.0f;
-        for (int t0 = 0; t0 < FG_SAMPLE_LANES; t0 += 16) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = sm.P[t0 + j + 1];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                P = __fadd_rn(P, v[j]);
-                sm.P[t0 + j + 1] = P;
-            }
-        }
+        sequential_prefix(sm.P);
     }
     __syncthreads();
     const float target = __fmul_rn(u, sm.P[FG_SAMPLE_LANES]);
@@ -457,19 +471,7 @@ __device__ int32_t cluster_sample(const T* row, int32_t V, float temperature, fl
     cl_sync();  // (B) CTA 0 holds the 512 chunk totals
     if (rank == 0) {
         if (tid == 0) {
-            // the specified sequential sum, its loads batched ahead of the adds
-            float P = 0.0f;
-            cs.P[0] = 0.0f;
-            for (int t0 = 0; t0 < FG_SAMPLE_LANES; t0 += 16) {
-                float v[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = cs.P[t0 + j + 1];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    P = __fadd_rn(P, v[j]);
-                    cs.P[t0 + j + 1] = P;
-                }
-            }
+            sequential_prefix(cs.P);
             cs.target_chunk = -1;
         }
         __syncthreads();
