@@ -487,7 +487,11 @@ def test_accept_matches_reference_fixture(ops, golden_dir):
 @pytest.mark.parametrize("parallel", [False, True])
 @pytest.mark.parametrize("dtype,V,B,peak,top_p", [(torch.bfloat16, 151936, 64, 6.0, 1.0), (torch.float32, 4096, 12, 8.0, 1.0),
                                                   (torch.float16, 1000, 33, 5.0, 1.0), (torch.bfloat16, 151936, 64, 6.0, 0.9),
-                                                  (torch.float32, 4096, 12, 2.0, 0.5)])
+                                                  (torch.float32, 4096, 12, 2.0, 0.5),
+                                                  # rows of an odd length: the scalar paths of the clustered draw
+                                                  (torch.bfloat16, 1001, 9, 5.0, 1.0),
+                                                  # 8 rows x 5 parents x 8 = 320 chunk-group loads in flight
+                                                  (torch.bfloat16, 40000, 8, 3.0, 1.0)])
 def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p, parallel):
     """K4 against the oracle walk, bit for bit: drawing during the walk, and
     (parallel) every internal node's draw made before the walk on the shared
@@ -916,6 +920,14 @@ def test_norms_and_activations(ops, dtype):
                           rtol=tol)
     idx = torch.tensor([3, 0, 36, 3], dtype=torch.int32, device=DEV)
     assert torch.equal(ops.gather_rows(x, idx), x[idx.long()])
+    # RMSNorm over the model widths: one warp per row up to 4 KB rows, one
+    # 128-thread block per row above (ragged row counts for the 8-row blocks)
+    for dim, rows in ((256, 9), (3584, 17), (4096, 3)):
+        xx = torch.randn(rows, dim, generator=g).to(dtype).to(DEV)
+        ww = (torch.rand(dim, generator=g) + 0.5).to(dtype).to(DEV)
+        vv = xx.float().pow(2).mean(-1, keepdim=True)
+        rr = ww * (xx.float() * torch.rsqrt(vv + 1e-6)).to(dtype)
+        assert torch.allclose(ops.rmsnorm(xx, ww, 1e-6).float(), rr.float(), atol=tol, rtol=tol), dim
 
 
 def test_bounded_wait_times_out_and_context_survives(ops):
