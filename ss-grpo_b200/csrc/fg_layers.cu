@@ -229,57 +229,6 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const T* __restrict__ 
     }
 }
 
-// Rows of up to 32 x kWarpRowVecs 16-byte vectors: one warp per row, the
-// row kept in registers, the sum of squares reduced with shuffles (no shared
-// memory or block barrier), 8 rows per 256-thread block.
-constexpr int kWarpRowVecs = 8;
-
-template <typename T>
-__global__ void __launch_bounds__(256) rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w,
-                                                           int32_t n_rows, int32_t dim, float eps,
-                                                           T* __restrict__ y) {
-    pdl_wait_then_release();
-    constexpr int NV = 16 / sizeof(T);
-    const int32_t row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= n_rows) return;
-    const int32_t nvec = dim / NV;
-    const T* xr = x + (int64_t)row * dim;
-    uint4 u[kWarpRowVecs];
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kWarpRowVecs; ++k) {
-        const int32_t vi = lane + k * 32;
-        u[k] = vi < nvec ? *reinterpret_cast<const uint4*>(xr + vi * NV) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int k = 0; k < kWarpRowVecs; ++k) {
-        const T* e = reinterpret_cast<const T*>(&u[k]);
-#pragma unroll
-        for (int j = 0; j < NV; ++j) {
-            const float v = tf<T>(e[j]);
-            ss += v * v;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float r = rsqrtf(ss / (float)dim + eps);
-    T* yr = y + (int64_t)row * dim;
-#pragma unroll
-    for (int k = 0; k < kWarpRowVecs; ++k) {
-        const int32_t vi = lane + k * 32;
-        if (vi >= nvec) break;
-        const uint4 uw = *reinterpret_cast<const uint4*>(w + vi * NV);
-        const T* e = reinterpret_cast<const T*>(&u[k]);
-        const T* we = reinterpret_cast<const T*>(&uw);
-        uint4 res;
-        T* o = reinterpret_cast<T*>(&res);
-#pragma unroll
-        for (int j = 0; j < NV; ++j) o[j] = from_f<T>(tf<T>(we[j]) * rnd<T>(tf<T>(e[j]) * r));
-        *reinterpret_cast<uint4*>(yr + vi * NV) = res;
-    }
-}
-
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int32_t dim, float eps,
                                T* __restrict__ y) {
@@ -440,15 +389,7 @@ extern "C" fg_status fg_rmsnorm(const void* x, const void* weight, int32_t dtype
     const int esz = dtype == FG_DTYPE_F32 ? 4 : 2;
     const bool vec = (dim * esz) % 16 == 0 && dim * esz <= 128 * 4 * 16 && ((uintptr_t)x % 16) == 0 &&
                      ((uintptr_t)y % 16) == 0 && ((uintptr_t)weight % 16) == 0;
-    if (vec && dim * esz <= 32 * kWarpRowVecs * 16) {
-        cudaError_t e = cudaSuccess;
-        FG_DISPATCH(dtype, (e = launch_pdl(rmsnorm_warp_kernel<T>, dim3((n_rows + 7) / 8), dim3(256), 0, st,
-                                           (const T*)x, (const T*)weight, n_rows, dim, eps, (T*)y)));
-        if (e != cudaSuccess) {
-            set_cuda_error(e);
-            return FG_ECUDA;
-        }
-    } else if (vec) {
+    if (vec) {
         cudaError_t e = cudaSuccess;
         FG_DISPATCH(dtype, (e = launch_pdl(rmsnorm_vec_kernel<T>, dim3(n_rows), dim3(128), 0, st, (const T*)x,
                                            (const T*)weight, dim, eps, (T*)y)));

@@ -920,8 +920,7 @@ def test_norms_and_activations(ops, dtype):
                           rtol=tol)
     idx = torch.tensor([3, 0, 36, 3], dtype=torch.int32, device=DEV)
     assert torch.equal(ops.gather_rows(x, idx), x[idx.long()])
-    # RMSNorm over the model widths: one warp per row up to 4 KB rows, one
-    # 128-thread block per row above (ragged row counts for the 8-row blocks)
+    # RMSNorm over the model widths (the vectorized kernel up to 8 KB rows)
     for dim, rows in ((256, 9), (3584, 17), (4096, 3)):
         xx = torch.randn(rows, dim, generator=g).to(dtype).to(DEV)
         ww = (torch.rand(dim, generator=g) + 0.5).to(dtype).to(DEV)
