@@ -7,7 +7,8 @@
 // visible to every node, tree slot j to node i iff bit j of anc_bits[i].
 //
 // bf16 path (head_dim 128): tc::attn_tc_kernel (fg_attention_tc.cu), grid
-// (split, kv_head x row_group, row).  A CTA owns the query rows of one KV head
+// (split, kv_head x row_group, row); KV heads with more than 128 query rows
+// take tc::attn_tc_wide_kernel (fg_attention_tc2.cu, 256 rows per CTA).  A CTA owns the query rows of one KV head
 // -- row r = node * G + g, up to 128 rows -- and streams its share of the
 // row's KV slots [0, kv_len + n_nodes) through 4-D tensor maps over
 // [B, Hkv, capacity, D] (128-slot x 64-dim boxes, 128-byte swizzle).  With
@@ -128,12 +129,42 @@ static int auto_splits(int32_t items, int32_t max_kv_len, int32_t n_nodes) {
 
 using namespace fg;
 
-static int resolve_splits(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads, int32_t num_splits,
-                          int32_t max_kv_len) {
-    const int G = n_q_heads / n_kv_heads;
-    const int groups = (n_nodes * G + kMaxRows - 1) / kMaxRows;
-    const int items = B * n_kv_heads * groups;
-    return num_splits > 0 ? num_splits : auto_splits(items, max_kv_len, n_nodes);
+// How a bf16 call runs: 129-256 query rows per KV head take the wide
+// kernel (one 256-row group, a pair of 128-row sub-items in the workspace)
+// when its grid fills the GPU without splits (at least kWideMinItems
+// items), the rest the 128-row kernel; splits per item as requested or
+// auto.  Measured: at 256 rows and >= 256 items the wide kernel is 3-22 %
+// faster; with 64 items it needs 2 splits and is 55 % slower (the 7B shape
+// with 16 rows per GPU), and with 512 rows its halved grid quantises worse
+// onto the SMs (10-13 % slower).  Workspace: per sub-item and split the fp32 (O, m, l) partials,
+// then one counter per item.
+constexpr int kWideMinItems = 148;  // one CTA per SM
+
+struct AttnPlan {
+    bool wide;
+    int groups;  // row groups per KV head (of 256 rows when wide, else 128)
+    int items;   // B x Hkv x groups
+    int subs;    // 128-row sub-items in the workspace
+    int splits;
+};
+
+static AttnPlan plan_attention(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads, int32_t num_splits,
+                               int32_t max_kv_len) {
+    AttnPlan a;
+    const int rows = n_nodes * (n_q_heads / n_kv_heads);
+    a.wide = rows > kMaxRows && rows <= tc::kWideRows && B * n_kv_heads >= kWideMinItems;
+    const int per = a.wide ? tc::kWideRows : kMaxRows;
+    a.groups = (rows + per - 1) / per;
+    a.items = B * n_kv_heads * a.groups;
+    a.subs = a.wide ? 2 * a.items : a.items;
+    a.splits = num_splits > 0 ? num_splits : auto_splits(a.items, max_kv_len, n_nodes);
+    return a;
+}
+
+static size_t plan_workspace_bytes(const AttnPlan& a) {
+    if (a.splits <= 1) return 0;
+    return (size_t)a.subs * a.splits * (size_t)(kMaxRows * kD + 2 * kMaxRows) * sizeof(float) +
+           (size_t)a.items * sizeof(int32_t);
 }
 
 extern "C" size_t fg_tree_attention_workspace_size(int32_t B, int32_t n_nodes, int32_t n_q_heads, int32_t n_kv_heads,
@@ -142,12 +173,7 @@ extern "C" size_t fg_tree_attention_workspace_size(int32_t B, int32_t n_nodes, i
         num_splits > tc::kMaxSplits)
         return 0;
     (void)head_dim;
-    const int G = n_q_heads / n_kv_heads;
-    const int groups = (n_nodes * G + kMaxRows - 1) / kMaxRows;
-    const size_t items = (size_t)B * n_kv_heads * groups;
-    const int splits = resolve_splits(B, n_nodes, n_q_heads, n_kv_heads, num_splits, max_kv_len);
-    if (splits <= 1) return 0;
-    return items * splits * (size_t)(kMaxRows * kD + 2 * kMaxRows) * sizeof(float) + items * sizeof(int32_t);
+    return plan_workspace_bytes(plan_attention(B, n_nodes, n_q_heads, n_kv_heads, num_splits, max_kv_len));
 }
 
 extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv_layer* kv, const int32_t* kv_len,
@@ -189,10 +215,10 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
     p.Hkv = n_kv_heads;
     p.G = G;
     p.rows_total = n_nodes * G;
-    p.groups = (p.rows_total + kMaxRows - 1) / kMaxRows;
-    const int items = B * n_kv_heads * p.groups;
-    p.splits = resolve_splits(B, n_nodes, n_q_heads, n_kv_heads, num_splits,
-                              max_kv_len > 0 ? max_kv_len : kv->capacity);
+    const AttnPlan plan = plan_attention(B, n_nodes, n_q_heads, n_kv_heads, num_splits,
+                                         max_kv_len > 0 ? max_kv_len : kv->capacity);
+    p.groups = plan.groups;
+    p.splits = plan.splits;
     // the kernel takes the row maximum of the raw scores and applies the scale
     // inside the exponent, which needs a positive scale
     if (!(scale > 0.0f)) return FG_EINVAL;
@@ -203,28 +229,29 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
     p.kv_rows = kv->rows;
     p.kv_batch = kv->batch;
     if (p.splits > 1) {
-        const size_t need = (size_t)items * p.splits * (kMaxRows * kD + 2 * kMaxRows) * sizeof(float) +
-                            (size_t)items * sizeof(int32_t);
+        const size_t need = plan_workspace_bytes(plan);
         if (!workspace || workspace_bytes < need || ((uintptr_t)workspace % 16)) return FG_ECAPACITY;
         p.ws_o = (float*)workspace;
-        p.ws_ml = p.ws_o + (size_t)items * p.splits * kMaxRows * kD;
-        p.ws_cnt = (int32_t*)(p.ws_ml + (size_t)items * p.splits * 2 * kMaxRows);
+        p.ws_ml = p.ws_o + (size_t)plan.subs * p.splits * kMaxRows * kD;
+        p.ws_cnt = (int32_t*)(p.ws_ml + (size_t)plan.subs * p.splits * 2 * kMaxRows);
     }
     CUtensorMap mk, mv;
     if (!make_kv_map(&mk, kv->k, cache_b, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s) ||
         !make_kv_map(&mv, kv->v, cache_b, n_kv_heads, kv->capacity, kv->stride_b, kv->stride_h, kv->stride_s))
         return FG_EINVAL;
-    static bool attr_set[64] = {};
+    static bool attr_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             tc::kSmemBytes);
+    if (dev < 0 || dev >= 64 || !attr_set[plan.wide][dev]) {
+        cudaError_t e = plan.wide ? cudaFuncSetAttribute(tc::attn_tc_wide_kernel,
+                                                         cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kWSmemBytes)
+                                  : cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         tc::kSmemBytes);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             return FG_ECUDA;
         }
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[plan.wide][dev] = true;
     }
     // Programmatic launch: the CTAs may start (TMEM, barriers, prefix tile
     // loads) while the preceding kernel of the stream finishes; the kernel
@@ -232,14 +259,15 @@ extern "C" fg_status fg_tree_attention(const void* q, int32_t dtype, const fg_kv
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.splits, n_kv_heads * p.groups, B);
     cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cfg.dynamicSmemBytes = plan.wide ? tc::kWSmemBytes : tc::kSmemBytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mk, mv, p);
+    const cudaError_t e = plan.wide ? cudaLaunchKernelEx(&cfg, tc::attn_tc_wide_kernel, mk, mv, p)
+                                    : cudaLaunchKernelEx(&cfg, tc::attn_tc_kernel, mk, mv, p);
     if (e != cudaSuccess) {
         set_cuda_error(e);
         return FG_ECUDA;

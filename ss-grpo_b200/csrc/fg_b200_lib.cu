@@ -8,6 +8,7 @@
 #include "fg_accept.cu"
 #include "fg_layers.cu"
 #include "fg_attention_tc.cu"
+#include "fg_attention_tc2.cu"
 #include "fg_attention.cu"
 #include "fg_attention_noalloc.cu"
 #include "fg_lmhead_tc.cu"

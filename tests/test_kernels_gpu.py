@@ -614,6 +614,9 @@ def _attn_reference(q, k, v, kv_len, tree, scale):
     # config-5 sweep corners: the longest prefix with the fewest nodes, a long
     # prefix with 4 query-row groups per KV head
     (1, 8, 32, 8, 32768, 0), (2, 128, 32, 8, 16384, 0),
+    # 129-256 query rows per KV head on >= 148 (row, head) items: the wide
+    # kernel (two 128-row halves per CTA, P in TMEM), whole and with 3 splits
+    (19, 64, 32, 8, 300, 0), (19, 53, 32, 8, 1500, 3), (37, 32, 28, 4, 517, 0),
 ])
 def test_tree_attention_bf16(ops, B, n, hq, hkv, L, splits):
     g = torch.Generator().manual_seed(B * 1000 + n)
