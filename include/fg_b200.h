@@ -44,6 +44,12 @@
  *   S there); kept = entries before or at K*;
  *   t = trunc(double(u) * double(S)); token = first index (ascending) among
  *   kept entries whose running kept mass exceeds t.
+ * Top-k variant "fg-icdf-v1k" (0 < top_k < V; the top_k branch of
+ * sample_from_logits, acceptance.py:68-79): the K-set is the first top_k
+ *   entries of that order, Zk its mass; with 0 < top_p < 1,
+ *   P = trunc(double(top_p) * double(Zk)) and K*, S as above, otherwise K* is
+ *   the K-set's last entry and S = Zk; kept, t and token as above.  Equal
+ *   logits are ordered by index (torch.topk leaves their order unspecified).
  */
 #ifndef FG_B200_H_
 #define FG_B200_H_
@@ -95,16 +101,17 @@ fg_status fg_philox_uniforms(uint64_t seed, const int32_t *seq_ids, int32_t n_ro
                              const int32_t *round_dev, int32_t n_draws, float *out, void *stream);
 
 /* One token per row of logits [n_rows, row_stride] (dtype FG_DTYPE_*),
- * uniform uniforms[r * u_stride]: fg-icdf-v1 for top_p >= 1 (or <= 0), the
- * nucleus variant fg-icdf-v1n for 0 < top_p < 1 (the kept set of
- * logits_to_probs, acceptance.py:7-31, on exact integer masses).  forced
- * (nullable): rows with forced[r] >= 0 take that token instead (pending
- * correction tokens).  Replaces sample_from_logits with top_k = None
- * (flashgrpo_b200/decoding/acceptance.py:34-130) for the root token of a
- * round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1717-1743). */
+ * uniform uniforms[r * u_stride]: fg-icdf-v1 for top_p >= 1 (or <= 0) and
+ * top_k outside (0, vocab), the nucleus variant fg-icdf-v1n for
+ * 0 < top_p < 1 (the kept set of logits_to_probs, acceptance.py:7-31, on
+ * exact integer masses), the top-k variant fg-icdf-v1k for 0 < top_k < vocab
+ * (with or without a top_p cut).  forced (nullable): rows with forced[r] >= 0
+ * take that token instead (pending correction tokens).  Replaces
+ * sample_from_logits (flashgrpo_b200/decoding/acceptance.py:34-130) for the
+ * root token of a round (flashgrpo_b200/decoding/flash_medusa_decoder.py:1717-1743). */
 fg_status fg_sample_rows(const void *logits, int32_t dtype, int64_t row_stride, int32_t vocab, int32_t n_rows,
                          const float *uniforms, int64_t u_stride, int32_t do_sample, float temperature,
-                         float top_p, const int32_t *forced, int32_t *out_tokens, void *stream);
+                         float top_p, int32_t top_k, const int32_t *forced, int32_t *out_tokens, void *stream);
 
 /* Per row: the k best entries ordered by (value descending, index
  * ascending), the row maximum and logsumexp (rounded to the logits dtype,
@@ -340,6 +347,7 @@ typedef struct fg_accept_args {
     int32_t do_sample;
     float temperature;
     float top_p;               /* 0 < top_p < 1: nucleus draws (fg-icdf-v1n) */
+    int32_t top_k;             /* 0 < top_k < vocab: top-k draws (fg-icdf-v1k); 0: no cut */
     int32_t eos_id;
     int32_t max_length;
     int32_t *row_len;          /* [B] logical length before the round; advanced if update_len */

@@ -51,6 +51,18 @@
  *   token    = first index (ascending) among kept entries whose running kept
  *              mass exceeds t.
  *
+ * Top-k variant "fg-icdf-v1k" (0 < top_k < V), the top_k branch of
+ * sample_from_logits (acceptance.py:68-79: the top_k sorted candidates, a
+ * softmax over them, then the nucleus mask when 0 < top_p < 1), with the
+ * same integer masses and order:
+ *   K-set    = the first top_k sorted positions; Zk = their summed mass
+ *   top_p in (0, 1): P = trunc(double(top_p) * double(Zk)) and K*, S as in
+ *              v1n (P < Zk puts K* inside the K-set); otherwise K* = the
+ *              last K-set position and S = Zk
+ *   kept, t and the token as in v1n.
+ * torch.topk's order among equal logits is unspecified; here ties go to the
+ * lower index, like every other sorted order of this path.
+ *
  * Build: oracle/build_oracle.sh (gcc -O2 -ffp-contract=off, no fast-math).
  */
 #include <math.h>
@@ -221,49 +233,57 @@ static int fgo_keyed_cmp(const void *pa, const void *pb) {
     return a->idx < b->idx ? -1 : (a->idx > b->idx ? 1 : 0);
 }
 
-/* The fg-icdf-v1n boundary of one row by an explicit sort (see the header):
- * fills q[V] and returns the boundary index (-1 if every entry is NaN/-inf),
- * with its key in *tau and the running mass there in *S. */
-static int32_t fgo_nucleus_boundary(const float *logits, int32_t V, float temperature, float top_p, uint64_t *q,
-                                    uint32_t *tau_out, uint64_t *S_out) {
+/* The fg-icdf-v1n / v1k boundary of one row by an explicit sort (see the
+ * header; top_k outside (0, V) means no top-k cut): fills q[V] and returns
+ * the boundary index (-1 if every entry is NaN/-inf), with its key in *tau
+ * and the running mass there in *S. */
+static int32_t fgo_kept_boundary(const float *logits, int32_t V, float temperature, float top_p, int32_t top_k,
+                                 uint64_t *q, uint32_t *tau_out, uint64_t *S_out) {
     float m = -INFINITY;
     for (int32_t i = 0; i < V; ++i) m = fmaxf(m, fgo_scaled(logits, i, temperature));
     if (!(m > -INFINITY)) return -1;
     fgo_keyed *ord = (fgo_keyed *)malloc((size_t)V * sizeof(fgo_keyed));
     if (!ord) return -1;
-    uint64_t Z = 0;
     for (int32_t i = 0; i < V; ++i) {
         const float x = fgo_scaled(logits, i, temperature);
         const float e = fgo_exp(x - m);
         q[i] = (uint64_t)(e * 1099511627776.0f); /* 2^40, exact scaling; truncation */
         ord[i].key = fgo_nucleus_key(x);
         ord[i].idx = i;
-        Z += q[i];
     }
-    const uint64_t P = (uint64_t)((double)top_p * (double)Z);
     qsort(ord, (size_t)V, sizeof(fgo_keyed), fgo_keyed_cmp);
-    uint64_t cum = 0;
+    const int32_t klim = (top_k > 0 && top_k < V) ? top_k : V;
+    uint64_t Zk = 0;
+    for (int32_t k = 0; k < klim; ++k) Zk += q[ord[k].idx];
     int32_t istar = -1;
-    for (int32_t k = 0; k < V; ++k) {
-        cum += q[ord[k].idx];
-        if (cum > P) {
-            *tau_out = ord[k].key;
-            istar = ord[k].idx;
-            *S_out = cum;
-            break;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        const uint64_t P = (uint64_t)((double)top_p * (double)Zk);
+        uint64_t cum = 0;
+        for (int32_t k = 0; k < klim; ++k) {
+            cum += q[ord[k].idx];
+            if (cum > P) {
+                *tau_out = ord[k].key;
+                istar = ord[k].idx;
+                *S_out = cum;
+                break;
+            }
         }
+    } else {
+        *tau_out = ord[klim - 1].key;
+        istar = ord[klim - 1].idx;
+        *S_out = Zk;
     }
     free(ord);
     return istar;
 }
 
-/* Kept set of the fg-icdf-v1n nucleus (mask[i] = 1 for kept entries). */
-int32_t fgo_nucleus_kept(const float *logits, int32_t V, float temperature, float top_p, uint8_t *mask) {
+/* Kept set of an fg-icdf-v1n / v1k draw (mask[i] = 1 for kept entries). */
+int32_t fgo_kept_set(const float *logits, int32_t V, float temperature, float top_p, int32_t top_k, uint8_t *mask) {
     uint64_t *q = (uint64_t *)malloc((size_t)V * sizeof(uint64_t));
     if (!q) return -1;
     uint32_t tau = 0;
     uint64_t S = 0;
-    const int32_t istar = fgo_nucleus_boundary(logits, V, temperature, top_p, q, &tau, &S);
+    const int32_t istar = fgo_kept_boundary(logits, V, temperature, top_p, top_k, q, &tau, &S);
     for (int32_t i = 0; i < V; ++i) {
         const uint32_t key = fgo_nucleus_key(fgo_scaled(logits, i, temperature));
         mask[i] = (istar >= 0 && (key > tau || (key == tau && i <= istar))) ? 1 : 0;
@@ -272,13 +292,17 @@ int32_t fgo_nucleus_kept(const float *logits, int32_t V, float temperature, floa
     return istar;
 }
 
-/* fg-icdf-v1n sample of one row (see the header). */
-int32_t fgo_sample_row_nucleus(const float *logits, int32_t V, float temperature, float top_p, float u) {
+int32_t fgo_nucleus_kept(const float *logits, int32_t V, float temperature, float top_p, uint8_t *mask) {
+    return fgo_kept_set(logits, V, temperature, top_p, 0, mask);
+}
+
+/* fg-icdf-v1n / v1k sample of one row (see the header). */
+int32_t fgo_sample_row_kept(const float *logits, int32_t V, float temperature, float top_p, int32_t top_k, float u) {
     uint64_t *q = (uint64_t *)malloc((size_t)V * sizeof(uint64_t));
     if (!q) return -1;
     uint32_t tau = 0;
     uint64_t S = 0;
-    const int32_t istar = fgo_nucleus_boundary(logits, V, temperature, top_p, q, &tau, &S);
+    const int32_t istar = fgo_kept_boundary(logits, V, temperature, top_p, top_k, q, &tau, &S);
     int32_t token = -1;
     if (istar >= 0) {
         const uint64_t t = (uint64_t)((double)u * (double)S);
@@ -298,17 +322,21 @@ int32_t fgo_sample_row_nucleus(const float *logits, int32_t V, float temperature
     return token;
 }
 
-/* Dispatch: greedy, fg-icdf-v1 (top_p outside (0, 1)) or fg-icdf-v1n. */
-int32_t fgo_sample_row_p(const float *logits, int32_t V, float temperature, int32_t do_sample, float top_p, float u) {
+/* Dispatch: greedy, fg-icdf-v1 (no top-k cut, top_p outside (0, 1)),
+ * fg-icdf-v1n (top_p in (0, 1)) or fg-icdf-v1k (0 < top_k < V). */
+int32_t fgo_sample_row_pk(const float *logits, int32_t V, float temperature, int32_t do_sample, float top_p,
+                          int32_t top_k, float u) {
     if (!do_sample || temperature == 0.0f) return fgo_argmax(logits, V);
-    if (top_p > 0.0f && top_p < 1.0f) return fgo_sample_row_nucleus(logits, V, temperature, top_p, u);
+    if ((top_p > 0.0f && top_p < 1.0f) || (top_k > 0 && top_k < V))
+        return fgo_sample_row_kept(logits, V, temperature, top_p, top_k, u);
     return fgo_sample_row(logits, V, temperature, do_sample, u);
 }
 
 void fgo_sample_rows(const float *logits, int64_t row_stride, int32_t V, int32_t n_rows, const float *uniforms,
-                     int32_t do_sample, float temperature, float top_p, int32_t *out) {
+                     int32_t do_sample, float temperature, float top_p, int32_t top_k, int32_t *out) {
     for (int32_t r = 0; r < n_rows; ++r)
-        out[r] = fgo_sample_row_p(logits + (int64_t)r * row_stride, V, temperature, do_sample, top_p, uniforms[r]);
+        out[r] = fgo_sample_row_pk(logits + (int64_t)r * row_stride, V, temperature, do_sample, top_p, top_k,
+                                   uniforms[r]);
 }
 
 /* ------------------------------------------------------- acceptance walk */
@@ -325,7 +353,8 @@ void fgo_sample_rows(const float *logits, int64_t row_stride, int32_t V, int32_t
 int32_t fgo_accept_walk(const float *logits, int64_t row_stride, int32_t V, const int32_t *slot,
                         const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes, int32_t nmax,
                         const float *uniforms, int32_t u_stride, int32_t B, int32_t do_sample, float temperature,
-                        float top_p, int32_t eos_id, int32_t max_length, const int32_t *row_len, int32_t dcap,
+                        float top_p, int32_t top_k, int32_t eos_id, int32_t max_length, const int32_t *row_len,
+                        int32_t dcap,
                         int32_t *acc_tokens, int32_t *acc_nodes, int32_t *acc_len, int32_t *raw_len,
                         int32_t *correction, int32_t *pending, int32_t *last_node, int32_t *finished) {
     for (int32_t b = 0; b < B; ++b) {
@@ -348,8 +377,8 @@ int32_t fgo_accept_walk(const float *logits, int64_t row_stride, int32_t V, cons
             if (first_child < 0) break;
             const int32_t s = sl[parent];
             if (s < 0) return -(b + 1);
-            const int32_t sampled = fgo_sample_row_p(logits + (int64_t)s * row_stride, V, temperature, do_sample,
-                                                     top_p, uniforms[(int64_t)b * u_stride + step]);
+            const int32_t sampled = fgo_sample_row_pk(logits + (int64_t)s * row_stride, V, temperature, do_sample,
+                                                      top_p, top_k, uniforms[(int64_t)b * u_stride + step]);
             ++step;
             int32_t match = -1;
             for (int32_t j = first_child; j < n; ++j)

@@ -43,7 +43,10 @@ def lib():
         _lib.fgo_sample_row.restype = ctypes.c_int32
         _lib.fgo_sample_row.argtypes = [_f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_float]
         _lib.fgo_sample_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _f32p,
-                                         ctypes.c_int32, ctypes.c_float, ctypes.c_float, _i32p]
+                                         ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_int32, _i32p]
+        _lib.fgo_kept_set.restype = ctypes.c_int32
+        _lib.fgo_kept_set.argtypes = [_f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_int32,
+                                      ctypes.POINTER(ctypes.c_uint8)]
         _lib.fgo_nucleus_kept.restype = ctypes.c_int32
         _lib.fgo_nucleus_kept.argtypes = [_f32p, ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                           ctypes.POINTER(ctypes.c_uint8)]
@@ -51,7 +54,7 @@ def lib():
         _lib.fgo_accept_walk.argtypes = [
             _f32p, ctypes.c_int64, ctypes.c_int32, _i32p, _i32p, _i32p, _i32p, ctypes.c_int32,
             _f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_int32,
-            ctypes.c_int32, _i32p, ctypes.c_int32, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p,
+            ctypes.c_int32, ctypes.c_int32, _i32p, ctypes.c_int32, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p,
         ]
         _lib.fgo_extract_path.argtypes = [
             ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_int32,
@@ -111,14 +114,14 @@ def chunk_len(V: int) -> int:
 
 
 def sample_rows(logits: np.ndarray, uniforms, *, do_sample: bool = True, temperature: float = 1.0,
-                top_p: float = 1.0) -> np.ndarray:
+                top_p: float = 1.0, top_k: int | None = None) -> np.ndarray:
     x = _cf(logits)
     if x.ndim == 1:
         x = x[None]
     u = _cf(np.broadcast_to(np.asarray(uniforms, dtype=np.float32), (x.shape[0],)))
     out = np.zeros(x.shape[0], dtype=np.int32)
     lib().fgo_sample_rows(_p(x, _f32p), x.shape[1], x.shape[1], x.shape[0], _p(u, _f32p), int(bool(do_sample)),
-                          float(temperature), float(top_p), _p(out, _i32p))
+                          float(temperature), float(top_p), int(top_k or 0), _p(out, _i32p))
     return out
 
 
@@ -128,6 +131,15 @@ def nucleus_kept(row: np.ndarray, temperature: float, top_p: float) -> np.ndarra
     mask = np.zeros(r.shape[0], dtype=np.uint8)
     lib().fgo_nucleus_kept(_p(r, _f32p), r.shape[0], float(temperature), float(top_p),
                            mask.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
+    return mask.astype(bool)
+
+
+def kept_set(row: np.ndarray, temperature: float, top_p: float, top_k: int | None) -> np.ndarray:
+    """fg-icdf-v1n / v1k kept set of one logits row (bool mask)."""
+    r = _cf(row)
+    mask = np.zeros(r.shape[0], dtype=np.uint8)
+    lib().fgo_kept_set(_p(r, _f32p), r.shape[0], float(temperature), float(top_p), int(top_k or 0),
+                       mask.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
     return mask.astype(bool)
 
 
@@ -159,7 +171,8 @@ def build_dense_trees(root, cand_idx: np.ndarray, topk_by_depth, budget: int, nm
 
 
 def accept_walk(logits: np.ndarray, slot, tokens, parents, n_nodes, uniforms, *, do_sample: bool, temperature: float,
-                eos_id: int, max_length: int, row_len, dcap: int, top_p: float = 1.0) -> dict:
+                eos_id: int, max_length: int, row_len, dcap: int, top_p: float = 1.0,
+                top_k: int | None = None) -> dict:
     x = _cf(logits)
     slot = _c32(slot)
     tokens = _c32(tokens)
@@ -174,7 +187,7 @@ def accept_walk(logits: np.ndarray, slot, tokens, parents, n_nodes, uniforms, *,
     rc = lib().fgo_accept_walk(
         _p(x, _f32p), x.shape[1], x.shape[1], _p(slot, _i32p), _p(tokens, _i32p), _p(parents, _i32p),
         _p(n_nodes, _i32p), nmax, _p(u, _f32p), u.shape[1], B, int(bool(do_sample)), float(temperature),
-        float(top_p), eos_id,
+        float(top_p), int(top_k or 0), eos_id,
         max_length, _p(row_len, _i32p), dcap, _p(out["acc_tokens"], _i32p), _p(out["acc_nodes"], _i32p),
         _p(out["acc_len"], _i32p), _p(out["raw_len"], _i32p), _p(out["correction"], _i32p),
         _p(out["pending"], _i32p), _p(out["last_node"], _i32p), _p(out["finished"], _i32p),

@@ -343,12 +343,13 @@ class CallOrderSampler:
         self.seed = int(seed)
         self.calls = 0
 
-    def __call__(self, logits_rows: torch.Tensor, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0):
+    def __call__(self, logits_rows: torch.Tensor, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0,
+                 top_k=None):
         u = np.array([native.uniform(self.seed, k, self.calls, 0) for k in range(logits_rows.shape[0])],
                      dtype=np.float32)
         self.calls += 1
         return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature,
-                                  top_p=top_p)
+                                  top_p=top_p, top_k=top_k)
 
 
 class SeqRoundSampler:
@@ -360,13 +361,24 @@ class SeqRoundSampler:
     def __init__(self, seed=0):
         self.seed = int(seed)
 
-    def __call__(self, logits_rows, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0):
+    def __call__(self, logits_rows, seq_ids, round_idx, draw, *, do_sample, temperature, top_p=1.0, top_k=None):
         u = np.array([native.uniform(self.seed, int(s), int(round_idx), int(draw)) for s in seq_ids], dtype=np.float32)
         return native.sample_rows(logits_rows.float().numpy(), u, do_sample=do_sample, temperature=temperature,
-                                  top_p=top_p)
+                                  top_p=top_p, top_k=top_k)
 
 
-def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *, do_sample, temperature, top_p=1.0):
+def _cut_kwargs(top_p, top_k) -> dict:
+    """top_p / top_k keyword arguments, passed only when they cut anything."""
+    kw = {}
+    if top_p is not None and top_p != 1.0:
+        kw["top_p"] = top_p
+    if top_k is not None:
+        kw["top_k"] = int(top_k)
+    return kw
+
+
+def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *, do_sample, temperature, top_p=1.0,
+                      top_k=None):
     """Depth-synchronous exact_target walk (acceptance.py:183-267)."""
     B = len(trees)
     acc_tokens = [[int(t.tokens[0])] for t in trees]
@@ -378,7 +390,7 @@ def accept_walk_batch(trees, tree_logits, slots, sampler, seq_ids, round_idx, *,
     while active:
         rows = torch.stack([tree_logits[slots[b][parent[b]]] for b in active])
         sampled = sampler(rows, [seq_ids[b] for b in active], round_idx, 1 + step,
-                          do_sample=do_sample, temperature=temperature, **({"top_p": top_p} if top_p != 1.0 else {}))
+                          do_sample=do_sample, temperature=temperature, **_cut_kwargs(top_p, top_k))
         step += 1
         still = []
         for b, tok in zip(active, sampled.tolist()):
@@ -457,6 +469,7 @@ class OracleConfig:
     do_sample: bool = True
     temperature: float = 1.0
     top_p: float = 1.0
+    top_k: int | None = None
     adaptive_tree_enabled: bool = False
     adaptive_confidence_metric: str = "top1_prob"
     adaptive_confidence_quantile: float = 0.25
@@ -556,7 +569,7 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
         if fresh:
             toks = sampler(cur_logits[fresh], [active_ids[r] for r in fresh], round_idx, 0,
                            do_sample=cfg.do_sample, temperature=cfg.temperature,
-                           **({"top_p": cfg.top_p} if cfg.top_p != 1.0 else {}))
+                           **_cut_kwargs(cfg.top_p, cfg.top_k))
             for r, t in zip(fresh, toks.tolist()):
                 root[r] = int(t)
         for r in range(B):
@@ -622,7 +635,8 @@ def generate(model, heads, input_ids, attention_mask, cfg: OracleConfig, sampler
         else:
             raw_tok, raw_nodes, _, raw_corr = accept_walk_batch(trees, tree_logits, slots, sampler, active_ids,
                                                                 round_idx, do_sample=cfg.do_sample,
-                                                                temperature=cfg.temperature, top_p=cfg.top_p)
+                                                                temperature=cfg.temperature, top_p=cfg.top_p,
+                                                                top_k=cfg.top_k)
         acc, acc_nodes, fin = [], [], []
         for r in range(B):
             tk = raw_tok[r][: max(1, int(remaining[r]))]

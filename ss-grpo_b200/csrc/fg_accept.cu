@@ -41,6 +41,7 @@ struct AcceptParams {
     int32_t do_sample;
     float temperature;
     float top_p;
+    int32_t top_k;
     int32_t eos_id;
     int32_t max_length;
     int32_t* row_len;
@@ -221,9 +222,9 @@ __global__ void __launch_bounds__(S > 1 ? kAcceptClusterThreads : FG_SAMPLE_LANE
             if constexpr (S == 1) {
                 __shared__ SampleSmem sm;
                 __shared__ NucleusSmem ns;
-                const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
-                drawn = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
-                                : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+                drawn = sample_cuts(p.do_sample, p.temperature, p.top_p, p.top_k, p.vocab)
+                            ? block_sample_kept<T>(row, p.vocab, p.temperature, p.top_p, p.top_k, u, sm, ns)
+                            : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
             } else {
                 __shared__ ClusterSampleSmem<S, kAcceptClusterThreads> cs;
                 extern __shared__ __align__(16) float ebuf[];
@@ -345,9 +346,9 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) draw_internal_kernel(AcceptPa
     }
     const T* row = static_cast<const T*>(p.logits) + (int64_t)j * p.logits_row_stride;
     const float u = p.uniforms[(int64_t)b * p.u_stride + step];
-    const bool nucleus = p.do_sample != 0 && p.temperature != 0.0f && p.top_p > 0.0f && p.top_p < 1.0f;
-    const int32_t t = nucleus ? block_sample_nucleus<T>(row, p.vocab, p.temperature, p.top_p, u, sm, ns)
-                              : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
+    const int32_t t = sample_cuts(p.do_sample, p.temperature, p.top_p, p.top_k, p.vocab)
+                          ? block_sample_kept<T>(row, p.vocab, p.temperature, p.top_p, p.top_k, u, sm, ns)
+                          : block_sample<T>(row, p.vocab, p.temperature, p.do_sample != 0, u, sm);
     if (threadIdx.x == 0) drawn[j] = t;
 }
 
@@ -435,6 +436,7 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
     p.do_sample = a->do_sample;
     p.temperature = a->temperature;
     p.top_p = a->top_p;
+    p.top_k = a->top_k;
     p.eos_id = a->eos_id;
     p.max_length = a->max_length;
     p.row_len = a->row_len;
@@ -495,9 +497,9 @@ extern "C" fg_status fg_accept_extract(const fg_accept_args* a, void* stream) {
         p.drawn = a->drawn;
     }
     // fg-icdf-v1 draws in the walk run on a cluster of kAcceptCtas CTAs per row
-    const bool nucleus = a->do_sample && a->temperature != 0.0f && a->top_p > 0.0f && a->top_p < 1.0f;
+    const bool cuts = sample_cuts(a->do_sample, a->temperature, a->top_p, a->top_k, a->vocab);
     // (the e_i buffer of one chunk group within 96 KB: V up to ~95k x 8 entries)
-    const bool clustered = !parallel && a->do_sample && a->temperature > 0.0f && !nucleus &&
+    const bool clustered = !parallel && a->do_sample && a->temperature > 0.0f && !cuts &&
                            sample_chunk_len(a->vocab) <= kFindWarpMax && cluster_ebuf_bytes(a->vocab) <= 96 * 1024;
     cudaError_t e = cudaSuccess;
     switch (a->logits_dtype) {

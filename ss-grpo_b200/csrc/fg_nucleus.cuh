@@ -25,6 +25,13 @@
 // probability q_i / S without a second search.  K* is found without sorting:
 // a 4-level radix select over the keys (8-bit digits, exact integer bucket
 // masses), then an index-ordered scan of the boundary key's entries.
+//
+// Top-k variant "fg-icdf-v1k" (0 < top_k < V; the top_k branch of
+// sample_from_logits, acceptance.py:68-79): the K-set is the first top_k
+// sorted positions, found by the same radix select on counts instead of
+// masses; Zk = its mass; with 0 < top_p < 1, P = trunc(double(top_p) *
+// double(Zk)) and K* as above (P < Zk puts K* inside the K-set), otherwise
+// K* = the K-set's last position and S = Zk; the draw as above.
 #pragma once
 
 #include "fg_sampler.cuh"
@@ -81,7 +88,8 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
 
 // One radix level: histogram of digit (key >> shift) & 255 over the entries
 // whose key bits above the digit equal `prefix` (all entries when shift = 24).
-template <typename T>
+// kCount: each entry weighs 1 instead of its mass q.
+template <typename T, bool kCount = false>
 __device__ __forceinline__ unsigned long long nucleus_level(const T* row, int32_t V, float temperature, float m,
                                                             int shift, uint32_t prefix, bool with_total,
                                                             NucleusSmem& ns) {
@@ -99,7 +107,7 @@ __device__ __forceinline__ unsigned long long nucleus_level(const T* row, int32_
         const uint32_t key = nucleus_key(x);
         const uint32_t above_bits = shift == 24 ? 0u : (key >> (shift + 8));  // shift + 8 <= 24 here
         act = act && above_bits == prefix;
-        const unsigned long long q = act ? nucleus_q(x, m) : 0ull;
+        const unsigned long long q = act ? (kCount ? 1ull : nucleus_q(x, m)) : 0ull;
         if (with_total) tot += q;
         nucleus_hist_add(ns.hist, (key >> shift) & 255u, q, act);
     }
@@ -147,49 +155,44 @@ __device__ __forceinline__ void nucleus_chunk_sums(const T* row, int32_t V, int3
     __syncthreads();
 }
 
-// fg-icdf-v1n draw (0 < top_p < 1, T > 0, do_sample); returns -1 only when
-// every entry is NaN or -inf.
-template <typename T>
-__device__ int32_t block_sample_nucleus(const T* row, int32_t V, float temperature, float top_p, float u,
-                                        SampleSmem& sm, NucleusSmem& ns) {
+struct SortedPick {
+    int32_t idx;               // -1: the weights never exceed the threshold
+    uint32_t key;
+    unsigned long long weight; // running weight at idx
+};
+
+// Finishes a sorted-order selection whose first radix level the caller has
+// run: the first sorted position (key descending, index ascending) at which
+// the running weight (mass q, or 1 with kCount) exceeds thr.
+template <typename T, bool kCount>
+__device__ __forceinline__ SortedPick sorted_select_finish(const T* row, int32_t V, float temperature, float m,
+                                                           unsigned long long thr, NucleusSmem& ns) {
     const int tid = threadIdx.x;
-    float bv;
-    int32_t bi;
-    row_max<T>(row, V, bv, bi);
-    block_best(bv, bi, sm);
-    const float m = scale_t(sm.red[0], temperature);
-    __syncthreads();
-    if (!(m > -INFINITY)) return -1;
-    // level 1 with the total mass
-    if (tid == 0) ns.base = 0ull;
-    const unsigned long long z_part = nucleus_level<T>(row, V, temperature, m, 24, 0u, true, ns);
-    const unsigned long long Z = block_sum_u64(z_part, ns);
-    const unsigned long long P = __double2ull_rz(__dmul_rn((double)top_p, __ull2double_rn(Z)));
-    nucleus_pick(P, 24, ns);
+    nucleus_pick(thr, 24, ns);
     for (int shift = 16; shift >= 0; shift -= 8) {
         const uint32_t prefix = ns.prefix;
-        nucleus_level<T>(row, V, temperature, m, shift, prefix, false, ns);
-        nucleus_pick(P, shift, ns);
+        nucleus_level<T, kCount>(row, V, temperature, m, shift, prefix, false, ns);
+        nucleus_pick(thr, shift, ns);
     }
-    const uint32_t tau = ns.prefix;
-    const unsigned long long above = ns.base;  // mass of keys > tau
-    // boundary entry: index order inside the key == tau group
+    const uint32_t key_sel = ns.prefix;
+    const unsigned long long above = ns.base;  // weight of keys > key_sel
+    // boundary entry: index order inside the key == key_sel group
     const int32_t C = sample_chunk_len(V);
-    auto tie_q = [&](int32_t i) -> unsigned long long {
+    auto tie_w = [&](int32_t i) -> unsigned long long {
         const float x = scale_t(to_f<T>(row[i]), temperature);
-        return nucleus_key(x) == tau ? nucleus_q(x, m) : 0ull;
+        return nucleus_key(x) == key_sel ? (kCount ? 1ull : nucleus_q(x, m)) : 0ull;
     };
-    nucleus_chunk_sums<T>(row, V, C, tie_q, ns);
+    nucleus_chunk_sums<T>(row, V, C, tie_w, ns);
     if (tid == 0) ns.istar = -1;
     __syncthreads();
     {
         const unsigned long long p0 = above + ns.part[tid], p1 = above + ns.part[tid + 1];
-        if (p0 <= P && P < p1) {
+        if (p0 <= thr && thr < p1) {
             const int32_t lo = min(tid * C, V), hi = min(lo + C, V);
             unsigned long long acc = p0;
             for (int32_t i = lo; i < hi; ++i) {
-                acc += tie_q(i);
-                if (acc > P) {
+                acc += tie_w(i);
+                if (acc > thr) {
                     ns.istar = i;
                     ns.S = acc;
                     break;
@@ -198,11 +201,73 @@ __device__ int32_t block_sample_nucleus(const T* row, int32_t V, float temperatu
         }
     }
     __syncthreads();
-    const int32_t istar = ns.istar;
-    const unsigned long long S = ns.S;
+    const SortedPick r{ns.istar, key_sel, ns.S};
     __syncthreads();
+    return r;
+}
+
+// fg-icdf-v1n / v1k draw (0 < top_p < 1 or 0 < top_k < V; T > 0, do_sample);
+// returns -1 only when every entry is NaN or -inf.
+template <typename T>
+__device__ int32_t block_sample_kept(const T* row, int32_t V, float temperature, float top_p, int32_t top_k,
+                                     float u, SampleSmem& sm, NucleusSmem& ns) {
+    const int tid = threadIdx.x;
+    float bv;
+    int32_t bi;
+    row_max<T>(row, V, bv, bi);
+    block_best(bv, bi, sm);
+    const float m = scale_t(sm.red[0], temperature);
+    __syncthreads();
+    if (!(m > -INFINITY)) return -1;
+    const bool cut_k = top_k > 0 && top_k < V;
+    const bool cut_p = top_p > 0.0f && top_p < 1.0f;
+    uint32_t tau = 0;
+    int32_t istar = -1;
+    unsigned long long S = 0;
+    if (cut_k) {
+        // the K-set: sorted positions 0 .. top_k - 1, by a count selection
+        if (tid == 0) ns.base = 0ull;
+        nucleus_level<T, true>(row, V, temperature, m, 24, 0u, false, ns);
+        const SortedPick kp =
+            sorted_select_finish<T, true>(row, V, temperature, m, (unsigned long long)(top_k - 1), ns);
+        if (kp.idx < 0) return -1;
+        const uint32_t tau_k = kp.key;
+        const int32_t i_k = kp.idx;
+        // Zk: the K-set's mass
+        unsigned long long zpart = 0;
+        for (int32_t i = tid; i < V; i += FG_SAMPLE_LANES) {
+            const float x = scale_t(to_f<T>(row[i]), temperature);
+            const uint32_t k = nucleus_key(x);
+            if (k > tau_k || (k == tau_k && i <= i_k)) zpart += nucleus_q(x, m);
+        }
+        const unsigned long long Zk = block_sum_u64(zpart, ns);
+        if (cut_p) {
+            const unsigned long long P = __double2ull_rz(__dmul_rn((double)top_p, __ull2double_rn(Zk)));
+            if (tid == 0) ns.base = 0ull;
+            nucleus_level<T>(row, V, temperature, m, 24, 0u, false, ns);
+            const SortedPick pp = sorted_select_finish<T, false>(row, V, temperature, m, P, ns);
+            istar = pp.idx;
+            tau = pp.key;
+            S = pp.weight;
+        } else {
+            tau = tau_k;
+            istar = i_k;
+            S = Zk;
+        }
+    } else {
+        // level 1 with the total mass
+        if (tid == 0) ns.base = 0ull;
+        const unsigned long long z_part = nucleus_level<T>(row, V, temperature, m, 24, 0u, true, ns);
+        const unsigned long long Z = block_sum_u64(z_part, ns);
+        const unsigned long long P = __double2ull_rz(__dmul_rn((double)top_p, __ull2double_rn(Z)));
+        const SortedPick pp = sorted_select_finish<T, false>(row, V, temperature, m, P, ns);
+        istar = pp.idx;
+        tau = pp.key;
+        S = pp.weight;
+    }
     if (istar < 0) return -1;
     // the draw: index order over the kept entries
+    const int32_t C = sample_chunk_len(V);
     const unsigned long long t = __double2ull_rz(__dmul_rn((double)u, __ull2double_rn(S)));
     auto kept_q = [&](int32_t i) -> unsigned long long {
         const float x = scale_t(to_f<T>(row[i]), temperature);
@@ -227,6 +292,12 @@ __device__ int32_t block_sample_nucleus(const T* row, int32_t V, float temperatu
     const int32_t r = ns.result;
     __syncthreads();
     return r;
+}
+
+// True when a draw with these knobs takes the kept-set form (v1n / v1k).
+__host__ __device__ __forceinline__ bool sample_cuts(int32_t do_sample, float temperature, float top_p,
+                                                     int32_t top_k, int32_t V) {
+    return do_sample != 0 && temperature != 0.0f && ((top_p > 0.0f && top_p < 1.0f) || (top_k > 0 && top_k < V));
 }
 
 }  // namespace fg

@@ -18,7 +18,8 @@ __global__ void philox_uniforms_kernel(uint64_t seed, const int32_t* __restrict_
 template <typename T>
 __global__ void __launch_bounds__(FG_SAMPLE_LANES) sample_rows_kernel(
     const T* __restrict__ logits, int64_t row_stride, int32_t V, const float* __restrict__ uniforms,
-    int64_t u_stride, int32_t do_sample, float temperature, float top_p, const int32_t* __restrict__ forced,
+    int64_t u_stride, int32_t do_sample, float temperature, float top_p, int32_t top_k,
+    const int32_t* __restrict__ forced,
     int32_t* __restrict__ out) {
     __shared__ SampleSmem sm;
     __shared__ NucleusSmem ns;
@@ -29,9 +30,9 @@ __global__ void __launch_bounds__(FG_SAMPLE_LANES) sample_rows_kernel(
     }
     const T* row = logits + (int64_t)r * row_stride;
     const float u = uniforms[(int64_t)r * u_stride];
-    const bool nucleus = do_sample != 0 && temperature != 0.0f && top_p > 0.0f && top_p < 1.0f;
-    const int32_t tok = nucleus ? block_sample_nucleus<T>(row, V, temperature, top_p, u, sm, ns)
-                                : block_sample<T>(row, V, temperature, do_sample != 0, u, sm);
+    const int32_t tok = sample_cuts(do_sample, temperature, top_p, top_k, V)
+                            ? block_sample_kept<T>(row, V, temperature, top_p, top_k, u, sm, ns)
+                            : block_sample<T>(row, V, temperature, do_sample != 0, u, sm);
     if (threadIdx.x == 0) out[r] = tok;
 }
 
@@ -588,26 +589,26 @@ extern "C" fg_status fg_philox_uniforms(uint64_t seed, const int32_t* seq_ids, i
 
 extern "C" fg_status fg_sample_rows(const void* logits, int32_t dtype, int64_t row_stride, int32_t vocab,
                                     int32_t n_rows, const float* uniforms, int64_t u_stride, int32_t do_sample,
-                                    float temperature, float top_p, const int32_t* forced, int32_t* out_tokens,
-                                    void* stream) {
+                                    float temperature, float top_p, int32_t top_k, const int32_t* forced,
+                                    int32_t* out_tokens, void* stream) {
     if (n_rows == 0) return FG_OK;
     if (!logits || !uniforms || !out_tokens || vocab <= 0 || n_rows < 0 || row_stride < vocab) return FG_EINVAL;
     cudaStream_t st = (cudaStream_t)stream;
     switch (dtype) {
         case FG_DTYPE_F32:
             sample_rows_kernel<float><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
-                (const float*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, forced,
-                out_tokens);
+                (const float*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, top_k,
+                forced, out_tokens);
             break;
         case FG_DTYPE_BF16:
             sample_rows_kernel<__nv_bfloat16><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
-                (const __nv_bfloat16*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, forced,
-                out_tokens);
+                (const __nv_bfloat16*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, top_k,
+                forced, out_tokens);
             break;
         case FG_DTYPE_F16:
             sample_rows_kernel<__half><<<n_rows, FG_SAMPLE_LANES, 0, st>>>(
-                (const __half*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, forced,
-                out_tokens);
+                (const __half*)logits, row_stride, vocab, uniforms, u_stride, do_sample, temperature, top_p, top_k,
+                forced, out_tokens);
             break;
         default:
             return FG_EINVAL;

@@ -56,7 +56,7 @@ class AcceptArgs(ctypes.Structure):
         ("logits", c_vp), ("logits_dtype", c_i32), ("logits_row_stride", c_i64), ("vocab", c_i32),
         ("slot", c_vp), ("tokens", c_vp), ("parents", c_vp), ("parent_stride", c_i32), ("n_nodes", c_vp),
         ("n_nodes_shared", c_i32), ("nmax", c_i32), ("uniforms", c_vp), ("u_stride", c_i32), ("B", c_i32),
-        ("do_sample", c_i32), ("temperature", c_f32), ("top_p", c_f32), ("eos_id", c_i32), ("max_length", c_i32), ("row_len", c_vp),
+        ("do_sample", c_i32), ("temperature", c_f32), ("top_p", c_f32), ("top_k", c_i32), ("eos_id", c_i32), ("max_length", c_i32), ("row_len", c_vp),
         ("update_len", c_i32), ("active", c_vp), ("dcap", c_i32), ("acc_tokens", c_vp), ("acc_nodes", c_vp),
         ("acc_len", c_vp), ("correction", c_vp), ("pending", c_vp), ("last_node", c_vp), ("finished", c_vp),
         ("n_layers", c_i32), ("k_layers", ctypes.POINTER(c_u64)), ("v_layers", ctypes.POINTER(c_u64)),
@@ -76,8 +76,8 @@ SIGNATURES = {
     "fg_read_device_error": (c_i32, [ctypes.POINTER(c_i32), c_i32]),
     "fg_wait_flag": (c_i32, [c_vp, c_i64, c_vp, c_vp]),
     "fg_philox_uniforms": (c_i32, [c_u64, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp]),
-    "fg_sample_rows": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_f32, c_f32, c_vp, c_vp,
-                               c_vp]),
+    "fg_sample_rows": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_f32, c_f32, c_i32, c_vp,
+                               c_vp, c_vp]),
     "fg_row_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "fg_lm_head_topk_workspace_size": (ctypes.c_size_t, [c_i32, c_i32, c_i32, c_i32]),
     "fg_lm_head_topk": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32,

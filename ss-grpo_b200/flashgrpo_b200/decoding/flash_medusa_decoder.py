@@ -9,8 +9,9 @@ CUDA graph and reads back the accepted tokens.
 
 Sampling: draws come from Philox uniforms indexed by (sequence id, round,
 draw) and the fg-icdf-v1 inverse CDF, so a seeded run is reproducible bit for
-bit.  Nucleus sampling (``top_p < 1``), adaptive trees and chain proposals
-are supported; ``top_k`` sampling, ``cache_update_mode="recompute_accepted"``,
+bit.  Nucleus (``top_p < 1``) and top-k sampling (fg-icdf-v1n / v1k: the
+reference's kept sets on exact integer masses), adaptive trees and chain
+proposals are supported; ``cache_update_mode="recompute_accepted"``,
 the sparse tree layouts, adaptive widths with chain proposals and the
 Reflex/HRDCR machinery are not on this path and are rejected explicitly.
 
@@ -107,8 +108,6 @@ class FlashMedusaDecoder:
             raise NotImplementedError("sparse tree layouts belong to the Reflex/HRDCR subsystem (tree_layout='dense')")
         if config.reflex_enabled:
             raise NotImplementedError("Reflex/HRDCR proposal adaptation is not on the B200 path")
-        if config.top_k is not None:
-            raise NotImplementedError("top_k sampling is not on the B200 path yet")
         if config.lm_head_kernel not in {"fused", "separate"}:
             raise ValueError(f"Unsupported lm_head_kernel={config.lm_head_kernel}")
         if config.dense_kernel not in {"auto", "native", "cublas"}:
@@ -161,8 +160,10 @@ class FlashMedusaDecoder:
         pad = getattr(self.tokenizer, "pad_token_id", None)
         eos = eos if eos is not None else (pad if pad is not None else 0)
         top_p = 1.0 if cfg.top_p is None else float(cfg.top_p)
+        # the reference cuts only for 0 < top_k < vocab (acceptance.py:68); so do the kernels
+        top_k = 0 if cfg.top_k is None else int(cfg.top_k)
         return RoundConfig(do_sample=bool(cfg.do_sample), temperature=float(cfg.temperature), top_p=top_p,
-                           eos_id=int(eos),
+                           top_k=top_k, eos_id=int(eos),
                            max_length=int(max_length), seed=int(cfg.sampling_seed),
                            attn_splits=int(cfg.attention_splits), lm_head=str(cfg.lm_head_kernel),
                            dense=str(cfg.dense_kernel), chain=chain,

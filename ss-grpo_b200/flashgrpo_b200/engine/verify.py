@@ -139,6 +139,7 @@ class RoundConfig:
     do_sample: bool = True
     temperature: float = 1.0
     top_p: float = 1.0  # 0 < top_p < 1: nucleus draws (fg-icdf-v1n)
+    top_k: int = 0  # 0 < top_k < vocab: top-k draws (fg-icdf-v1k); otherwise no cut
     eos_id: int = 1
     max_length: int = 1 << 30
     seed: int = 0
@@ -602,7 +603,7 @@ class VerifyEngine:
                 ops.row_topk(rb.logits[B:M], rb.kmax, out=rb.topk)
         ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
-                        top_p=cfg.top_p, forced=st.pending, out=rb.root)
+                        top_p=cfg.top_p, top_k=cfg.top_k, forced=st.pending, out=rb.root)
 
     # ------------------------------------------------------ chain proposals
     def _chain_cell(self, state: torch.Tensor, emb: torch.Tensor) -> torch.Tensor:
@@ -688,7 +689,7 @@ class VerifyEngine:
             torch.mm(st.X[:B], self.w.lm_head.t(), out=rb.logits[:B])
         ops.philox_uniforms(cfg.seed, st.seq_ids, 0, rb.n_draws, out=rb.U, round_dev=st.round_dev)
         ops.sample_rows(rb.logits[:B], rb.U, do_sample=cfg.do_sample, temperature=cfg.temperature,
-                        top_p=cfg.top_p, forced=st.pending, out=rb.root)
+                        top_p=cfg.top_p, top_k=cfg.top_k, forced=st.pending, out=rb.root)
         if idx is None:  # the state was not bootstrapped together with the root logits
             if cfg.chain_bootstrap and len(self.heads) > 0:
                 hw = self.heads.heads[0]
@@ -821,7 +822,8 @@ class VerifyEngine:
         outs["pending"] = st.pending
         ops.accept_extract(logits=rb.tree_logits, slot=rb.tree["slot"], tokens=rb.tree["tokens"],
                            parents=rb.tree["parents"], n_nodes=None, n_nodes_shared=rb.N, uniforms=rb.U[:, 1:],
-                           do_sample=cfg.do_sample, temperature=cfg.temperature, top_p=cfg.top_p, eos_id=cfg.eos_id,
+                           do_sample=cfg.do_sample, temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k,
+                           eos_id=cfg.eos_id,
                            max_length=cfg.max_length, row_len=st.row_len, outputs=outs, dcap=rb.dcap,
                            update_len=True, active=st.active, k_layers=[st.k[l] for l in range(self.spec.n_layers)],
                            v_layers=[st.v[l] for l in range(self.spec.n_layers)], tree_hidden=rb.tree_hidden,

@@ -75,10 +75,10 @@ def philox_uniforms(seed: int, seq_ids: torch.Tensor, round_idx: int, n_draws: i
 
 
 def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool = True, temperature: float = 1.0,
-                top_p: float = 1.0, forced: torch.Tensor | None = None,
+                top_p: float = 1.0, top_k: int | None = None, forced: torch.Tensor | None = None,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """fg-icdf-v1 draw per row (fg-icdf-v1n when 0 < top_p < 1); uniforms
-    [n] or [n, k] (column 0 is used)."""
+    """fg-icdf-v1 draw per row (fg-icdf-v1n when 0 < top_p < 1, fg-icdf-v1k
+    when 0 < top_k < vocab); uniforms [n] or [n, k] (column 0 is used)."""
     _need(logits, "logits", contiguous=False)
     stride, vocab = _rows(logits, "logits")
     _need(uniforms, "uniforms", torch.float32, contiguous=False)
@@ -89,7 +89,8 @@ def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor, *, do_sample: bool
     if out is None:
         out = torch.empty(n, dtype=torch.int32, device=logits.device)
     N.call("fg_sample_rows", _ptr(logits), dtype_code(logits), stride, vocab, n, _ptr(uniforms), u_stride,
-           int(bool(do_sample)), float(temperature), float(top_p), _ptr(forced), _ptr(out), _stream(logits))
+           int(bool(do_sample)), float(temperature), float(top_p), int(top_k or 0), _ptr(forced), _ptr(out),
+           _stream(logits))
     return out
 
 
@@ -352,7 +353,8 @@ def layer_pointer_arrays(k_layers, v_layers):
 def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sample, temperature, eos_id, max_length,
                    row_len, outputs: dict, dcap: int, update_len: bool = True, active=None, k_layers=(), v_layers=(),
                    tree_hidden=None, hidden_out=None, parents_shared: bool = True, n_nodes_shared: int = 0,
-                   top_p: float = 1.0, kv_rows=None, parallel=None, acc_total=None, round_counter=None):
+                   top_p: float = 1.0, top_k: int | None = None, kv_rows=None, parallel=None, acc_total=None,
+                   round_counter=None):
     """K4.  outputs holds int32 tensors acc_tokens/acc_nodes [B, dcap] and
     acc_len/correction/pending/last_node/finished [B]; kv_rows (int32 [B],
     optional): row b compacts cache row kv_rows[b] of k_layers/v_layers.
@@ -378,6 +380,7 @@ def accept_extract(*, logits, slot, tokens, parents, n_nodes, uniforms, do_sampl
     a.nmax = nmax
     a.uniforms, a.u_stride = uniforms.data_ptr(), uniforms.stride(0)
     a.B, a.do_sample, a.temperature, a.top_p = B, int(bool(do_sample)), float(temperature), float(top_p)
+    a.top_k = int(top_k or 0)
     a.eos_id, a.max_length = int(eos_id), int(max_length)
     a.row_len, a.update_len, a.active, a.dcap = row_len.data_ptr(), int(bool(update_len)), _ptr(active), int(dcap)
     for key in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):

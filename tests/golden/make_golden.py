@@ -270,14 +270,13 @@ class _CallOrderRefSampler:
         self.calls = 0
 
     def __call__(self, logits, *, do_sample=True, temperature=1.0, top_p=1.0, top_k=None, nucleus_topk_hint=2048):
-        assert top_k is None
         x = logits.detach().float().numpy()
         u = np.array([native.uniform(self.seed, k, self.calls, 0) for k in range(x.shape[0])], dtype=np.float32)
         self.calls += 1
-        # top_p < 1: the fg-icdf-v1n draw from the nucleus kept set
+        # top_p < 1 / top_k: the fg-icdf-v1n / v1k draw from the kept set
         p = 1.0 if top_p is None else float(top_p)
         return torch.from_numpy(native.sample_rows(x, u, do_sample=do_sample, temperature=temperature,
-                                                   top_p=p).astype(np.int64))
+                                                   top_p=p, top_k=top_k).astype(np.int64))
 
 
 def gen_generate():
@@ -304,6 +303,12 @@ def gen_generate():
         "chain_conc_p09": dict(tree_mode="concurrency_aware", cpeak_nodes=64, fixed_tree_topk_by_depth=(4, 3, 2),
                                max_tree_nodes_per_seq=16, max_tree_depth=4, repeats=2, max_new=16, seed=19,
                                proposal_mode="chain", chain_bootstrap_from_medusa=True, top_p=0.9),
+        # top-k draws (sample_from_logits' top_k branch), alone and with top_p
+        "topk_8": dict(tree_mode="fixed", fixed_tree_topk_by_depth=(4, 2, 2), max_tree_nodes_per_seq=16,
+                       max_tree_depth=4, repeats=1, max_new=20, seed=23, top_k=8),
+        "topk_40_p09": dict(tree_mode="concurrency_aware", cpeak_nodes=64, fixed_tree_topk_by_depth=(4, 3, 2),
+                            max_tree_nodes_per_seq=16, max_tree_depth=4, repeats=2, max_new=16, seed=29, top_k=40,
+                            top_p=0.9),
     }
     model = synth.build_model(1)
     ids, mask = synth.random_prompts(4, 128, 4096, seed=0)
@@ -317,6 +322,7 @@ def gen_generate():
             num_medusa_heads=3, tree_mode=r["tree_mode"], cpeak_nodes=r.get("cpeak_nodes", 512),
             max_tree_nodes_per_seq=r["max_tree_nodes_per_seq"], max_tree_depth=r["max_tree_depth"],
             fixed_tree_topk_by_depth=r["fixed_tree_topk_by_depth"], temperature=1.0, top_p=r.get("top_p", 1.0),
+            top_k=r.get("top_k"),
             adaptive_tree_enabled=r.get("adaptive_tree_enabled", False),
             adaptive_min_topk_by_depth=r.get("adaptive_min_topk_by_depth", (1, 1, 1)),
             proposal_mode=r.get("proposal_mode", "medusa"),
@@ -377,8 +383,63 @@ def gen_nucleus():
                         top_p=np.array(tops, dtype=np.float32), kept=np.stack(kept), margin=np.array(margin))
 
 
+# -------------------------------------------------------------------- top-k
+def gen_topk():
+    """Kept sets of the reference's top-k rule on seeded rows with distinct
+    logits: the tokens sample_from_logits' top_k branch (acceptance.py:68-79)
+    hands to torch.multinomial with non-zero weight, captured at that call,
+    and the non-zero entries of logits_to_probs (acceptance.py:7-31) with the
+    same arguments, which must agree.  With 0 < top_p < 1 the row's margin is
+    as in gen_nucleus, on the cumulative sums over the k candidates."""
+    g = torch.Generator().manual_seed(2025)
+    rows, temps, tops, ks, kept, margin = [], [], [], [], [], []
+    seen = []
+    real_multinomial = torch.multinomial
+
+    def capture(weights, num_samples, *a, **kw):
+        seen.append(weights.detach().clone())
+        return real_multinomial(weights, num_samples, *a, **kw)
+
+    for r in range(48):
+        V = [97, 512, 1000, 4096][r % 4]
+        scale = [0.5, 1.0, 3.0, 8.0][(r // 4) % 4]
+        logits = torch.randn(V, generator=g) * scale
+        T = [1.0, 0.7, 1.3][r % 3]
+        top_k = [1, 2, 7, 40, 96][r % 5]
+        top_p = [1.0, 0.9, 0.5, 0.95][(r // 2) % 4]
+        seen.clear()
+        torch.multinomial = capture
+        try:
+            ref_acc.sample_from_logits(logits[None], do_sample=True, temperature=T, top_p=top_p, top_k=top_k)
+        finally:
+            torch.multinomial = real_multinomial
+        cand = torch.topk(logits[None], k=top_k, dim=-1, largest=True, sorted=True).indices[0]
+        mask = np.zeros(V, dtype=bool)
+        mask[cand[seen[0][0] > 0].numpy()] = True
+        probs = ref_acc.logits_to_probs(logits[None], temperature=T, top_p=top_p, top_k=top_k)[0]
+        assert np.array_equal(mask, (probs > 0).numpy()), r
+        sp = torch.softmax(logits.float().topk(top_k).values / T, dim=-1)
+        cum = torch.cumsum(sp, dim=-1)
+        if 0.0 < top_p < 1.0:
+            k = int((cum > top_p).nonzero()[0]) if bool((cum > top_p).any()) else top_k - 1
+            lo = float(cum[k - 1]) if k > 0 else 0.0
+            margin.append(min(abs(float(cum[k]) - top_p), abs(lo - top_p)))
+        else:
+            margin.append(1.0)
+        rows.append(np.pad(logits.numpy().astype(np.float32), (0, 4096 - V), constant_values=np.nan))
+        temps.append(T)
+        tops.append(top_p)
+        ks.append(top_k)
+        kept.append(np.pad(mask, (0, 4096 - V)))
+    np.savez_compressed(HERE / "topk.npz", logits=np.stack(rows), vocab=np.array([[97, 512, 1000, 4096][r % 4]
+                        for r in range(48)], dtype=np.int32), temperature=np.array(temps, dtype=np.float32),
+                        top_p=np.array(tops, dtype=np.float32), top_k=np.array(ks, dtype=np.int32),
+                        kept=np.stack(kept), margin=np.array(margin))
+
+
 GENERATORS = {"planner": lambda: gen_planner(), "trees": lambda: gen_trees(), "accept": lambda: gen_accept(),
-              "extract": lambda: gen_extract(), "generate": lambda: gen_generate(), "nucleus": lambda: gen_nucleus()}
+              "extract": lambda: gen_extract(), "generate": lambda: gen_generate(), "nucleus": lambda: gen_nucleus(),
+              "topk": lambda: gen_topk()}
 
 if __name__ == "__main__":
     # python tests/golden/make_golden.py [name ...]  (default: every fixture)

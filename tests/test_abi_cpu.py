@@ -41,7 +41,7 @@ def test_host_only_entry_points():
     assert lib.fg_version().decode().startswith("fg_b200")
     assert lib.fg_status_string(_native.FG_ETIMEOUT).decode() == "device wait timed out"
     # argument validation happens before any CUDA call
-    assert lib.fg_sample_rows(None, 1, 10, 10, 3, None, 1, 1, 1.0, 1.0, None, None, None) == _native.FG_EINVAL
+    assert lib.fg_sample_rows(None, 1, 10, 10, 3, None, 1, 1, 1.0, 1.0, 0, None, None, None) == _native.FG_EINVAL
     assert lib.fg_row_topk(ctypes.c_void_p(16), 1, 100, 100, 2, 99, ctypes.c_void_p(16), ctypes.c_void_p(16),
                            ctypes.c_void_p(16), ctypes.c_void_p(16), None) == _native.FG_ECAPACITY
     assert lib.fg_tree_attention_workspace_size(64, 13, 12, 2, 128, 1, 1024) == 0

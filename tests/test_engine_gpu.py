@@ -45,6 +45,10 @@ def _heads_list(st, n):
     dict(tree_mode="fixed", fixed=(3, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=13, chain=True),
     dict(tree_mode="fixed", fixed=(2, 2), mx=7, depth=3, repeats=2, max_new=16, seed=17, chain=True,
          bootstrap=False),
+    # top-k draws, alone and with top_p
+    dict(tree_mode="fixed", fixed=(4, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=23, top_k=8),
+    dict(tree_mode="concurrency_aware", cpeak=64, fixed=(4, 3, 2), mx=16, depth=4, repeats=2, max_new=16, seed=29,
+         top_k=40, top_p=0.9),
 ])
 def test_generate_config1_matches_oracle(run):
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder
@@ -62,7 +66,8 @@ def test_generate_config1_matches_oracle(run):
     ocfg = rp.OracleConfig(tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                            max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
                            fixed_tree_topk_by_depth=run["fixed"], do_sample=not greedy,
-                           top_p=run.get("top_p", 1.0), adaptive_tree_enabled=run.get("adaptive", False),
+                           top_p=run.get("top_p", 1.0), top_k=run.get("top_k"),
+                           adaptive_tree_enabled=run.get("adaptive", False),
                            adaptive_confidence_low=0.3, adaptive_confidence_high=0.9,
                            proposal_mode="chain" if chain else "medusa", chain_cell=cell,
                            chain_bootstrap_from_medusa=run.get("bootstrap", True))
@@ -70,7 +75,8 @@ def test_generate_config1_matches_oracle(run):
                       repeats=run["repeats"], max_length=128 + run["max_new"])
     cfg = FlashMedusaConfig(num_medusa_heads=3, tree_mode=run["tree_mode"], cpeak_nodes=run.get("cpeak", 512),
                             max_tree_nodes_per_seq=run["mx"], max_tree_depth=run["depth"],
-                            fixed_tree_topk_by_depth=run["fixed"], top_p=run.get("top_p", 1.0), do_sample=not greedy,
+                            fixed_tree_topk_by_depth=run["fixed"], top_p=run.get("top_p", 1.0),
+                            top_k=run.get("top_k"), do_sample=not greedy,
                             adaptive_tree_enabled=run.get("adaptive", False), adaptive_confidence_low=0.3,
                             adaptive_confidence_high=0.9, proposal_mode="chain" if chain else "medusa",
                             chain_bootstrap_from_medusa=run.get("bootstrap", True),

@@ -77,6 +77,29 @@ def test_sample_rows_nucleus_bit_exact(ops, dtype, V, temp, scale, top_p):
         assert orc.nucleus_kept(logits[r].float().numpy(), temp, top_p)[got[r]]
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("V,temp,scale,top_k,top_p", [(4096, 1.0, 8.0, 20, 1.0), (151936, 1.0, 2.0, 50, 1.0),
+                                                      (151936, 0.8, 2.0, 40, 0.9), (97, 0.7, 3.0, 96, 0.5),
+                                                      (1000, 1.0, 0.05, 1, 1.0), (128256, 1.3, 1.0, 300, 0.95)])
+def test_sample_rows_topk_bit_exact(ops, dtype, V, temp, scale, top_k, top_p):
+    # fg-icdf-v1k: the K-set by a count radix select on the GPU vs an explicit
+    # sort on the CPU; the tied row puts the K-set boundary inside a tie group
+    g = torch.Generator().manual_seed(V + top_k + int(top_p * 100))
+    n = 16
+    logits = (torch.randn(n, V, generator=g) * scale).to(dtype)
+    logits[2] = logits[2].round()  # heavy ties
+    u = torch.rand(n, generator=g)
+    u[0], u[1] = 0.0, 1.0 - 2 ** -24
+    got = ops.sample_rows(logits.to(DEV), u.to(DEV), temperature=temp, top_p=top_p, top_k=top_k).cpu().numpy()
+    ref = orc.sample_rows(logits.float().numpy(), u.numpy(), temperature=temp, top_p=top_p, top_k=top_k)
+    assert np.array_equal(got, ref)
+    for r in range(4):
+        assert orc.kept_set(logits[r].float().numpy(), temp, top_p, top_k)[got[r]]
+    # top_k >= V is no cut: the fg-icdf-v1 / v1n draw
+    same = ops.sample_rows(logits.to(DEV), u.to(DEV), temperature=temp, top_p=top_p, top_k=V).cpu().numpy()
+    assert np.array_equal(same, orc.sample_rows(logits.float().numpy(), u.numpy(), temperature=temp, top_p=top_p))
+
+
 def test_sample_rows_forced_and_strided(ops):
     logits = torch.randn(6, 3, 512).to(DEV)
     view = logits[:, 1, :]  # row stride 1536
@@ -448,7 +471,7 @@ def test_build_tree_matches_oracle(ops, case):
 # ------------------------------------------------ acceptance + compaction
 def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sample, temperature, row_len,
                 max_length=1 << 30, eos=-7, dcap=8, k_layers=(), v_layers=(), tree_hidden=None, hidden_out=None,
-                top_p=1.0, kv_rows=None, parallel=None):
+                top_p=1.0, top_k=None, kv_rows=None, parallel=None):
     B = tokens.shape[0]
     outs = {k: torch.full((B, dcap), -9, dtype=torch.int32, device=DEV) for k in ("acc_tokens", "acc_nodes")}
     for k in ("acc_len", "correction", "pending", "last_node", "finished"):
@@ -460,7 +483,7 @@ def _run_accept(ops, logits, slots, tokens, parents, n_nodes, uniforms, *, do_sa
                        uniforms=uniforms, do_sample=do_sample, temperature=temperature, eos_id=eos,
                        max_length=max_length, row_len=rl, outputs=outs, dcap=dcap, parents_shared=parallel is not None,
                        k_layers=k_layers, v_layers=v_layers, tree_hidden=tree_hidden, hidden_out=hidden_out,
-                       top_p=top_p, kv_rows=kv_rows, parallel=parallel, acc_total=acc_total,
+                       top_p=top_p, top_k=top_k, kv_rows=kv_rows, parallel=parallel, acc_total=acc_total,
                        round_counter=round_counter)
     torch.cuda.synchronize()
     # the round counters: accepted tokens added up, one round counted
@@ -485,14 +508,17 @@ def test_accept_matches_reference_fixture(ops, golden_dir):
 
 
 @pytest.mark.parametrize("parallel", [False, True])
-@pytest.mark.parametrize("dtype,V,B,peak,top_p", [(torch.bfloat16, 151936, 64, 6.0, 1.0), (torch.float32, 4096, 12, 8.0, 1.0),
-                                                  (torch.float16, 1000, 33, 5.0, 1.0), (torch.bfloat16, 151936, 64, 6.0, 0.9),
-                                                  (torch.float32, 4096, 12, 2.0, 0.5),
-                                                  # rows of an odd length: the scalar paths of the clustered draw
-                                                  (torch.bfloat16, 1001, 9, 5.0, 1.0),
-                                                  # 8 rows x 5 parents x 8 = 320 chunk-group loads in flight
-                                                  (torch.bfloat16, 40000, 8, 3.0, 1.0)])
-def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p, parallel):
+@pytest.mark.parametrize("dtype,V,B,peak,top_p,top_k", [
+    (torch.bfloat16, 151936, 64, 6.0, 1.0, None), (torch.float32, 4096, 12, 8.0, 1.0, None),
+    (torch.float16, 1000, 33, 5.0, 1.0, None), (torch.bfloat16, 151936, 64, 6.0, 0.9, None),
+    (torch.float32, 4096, 12, 2.0, 0.5, None),
+    # rows of an odd length: the scalar paths of the clustered draw
+    (torch.bfloat16, 1001, 9, 5.0, 1.0, None),
+    # 8 rows x 5 parents x 8 = 320 chunk-group loads in flight
+    (torch.bfloat16, 40000, 8, 3.0, 1.0, None),
+    # top-k draws (fg-icdf-v1k), alone and with a top_p cut
+    (torch.bfloat16, 151936, 64, 6.0, 1.0, 50), (torch.float32, 4096, 12, 2.0, 0.8, 20)])
+def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p, top_k, parallel):
     """K4 against the oracle walk, bit for bit: drawing during the walk, and
     (parallel) every internal node's draw made before the walk on the shared
     topology."""
@@ -532,10 +558,10 @@ def test_accept_extract_random_bit_exact(ops, dtype, V, B, peak, top_p, parallel
                            par_arg, torch.full((B,), n, dtype=torch.int32, device=DEV), U.to(DEV),
                            do_sample=True, temperature=1.0, row_len=row_len.to(DEV), max_length=max_length, eos=eos,
                            dcap=8, k_layers=kl, v_layers=vl, tree_hidden=hidden, hidden_out=hout, top_p=top_p,
-                           parallel=par_in)
+                           top_k=top_k, parallel=par_in)
     ref = orc.accept_walk(packed.float().numpy(), np.array(slots), tok.numpy(), par.numpy(), np.full(B, n), U.numpy(),
                           do_sample=True, temperature=1.0, eos_id=eos, max_length=max_length,
-                          row_len=row_len.numpy(), dcap=8, top_p=top_p)
+                          row_len=row_len.numpy(), dcap=8, top_p=top_p, top_k=top_k)
     for k in ("acc_tokens", "acc_nodes", "acc_len", "correction", "pending", "last_node", "finished"):
         assert np.array_equal(outs[k].cpu().numpy(), ref[k]), k
     assert np.array_equal(rl.cpu().numpy(), row_len.numpy() + ref["acc_len"])

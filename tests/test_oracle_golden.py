@@ -368,9 +368,65 @@ def test_planner_matches_reference_fixture(golden_dir):
                                        low=c["low"], high=c["high"]) == c["out"]
 
 
+# ------------------------------------------------------------------ top-k
+def test_topk_kept_set_matches_reference(golden_dir):
+    # sample_from_logits' top_k branch (acceptance.py:68-79) on 48 seeded rows,
+    # top_k in {1, 2, 7, 40, 96}, top_p in {1, 0.9, 0.5, 0.95}
+    d = np.load(golden_dir / "topk.npz")
+    compared = 0
+    for r in range(d["logits"].shape[0]):
+        V = int(d["vocab"][r])
+        if d["margin"][r] < 1e-5:
+            continue
+        mine = native.kept_set(d["logits"][r, :V], float(d["temperature"][r]), float(d["top_p"][r]),
+                               int(d["top_k"][r]))
+        assert np.array_equal(mine, d["kept"][r, :V]), r
+        compared += 1
+    assert compared >= 40
+
+
+def test_topk_sampler_matches_renormalised_kept_distribution():
+    rng = np.random.default_rng(13)
+    logits = (rng.standard_normal(300) * 2).astype(np.float32)
+    order = np.argsort(-logits, kind="stable")
+    for temp, top_k, top_p in ((1.0, 12, 1.0), (0.7, 30, 0.8)):
+        p = np.exp((logits[order[:top_k]].astype(np.float64) - logits.max()) / temp)
+        p /= p.sum()
+        k = top_k - 1 if top_p >= 1.0 else int(np.argmax(np.cumsum(p) > top_p))
+        want = np.zeros(300, dtype=bool)
+        want[order[: k + 1]] = True
+        assert np.array_equal(native.kept_set(logits, temp, top_p, top_k), want)
+        q = np.zeros(300)
+        q[order[: k + 1]] = p[: k + 1] / p[: k + 1].sum()
+        u = native.philox_uniforms(22, np.arange(60_000), 3, 1)[:, 0]
+        s = native.sample_rows(np.broadcast_to(logits, (60_000, 300)).copy(), u, temperature=temp, top_p=top_p,
+                               top_k=top_k)
+        assert want[s].all()
+        freq = np.bincount(s, minlength=300) / s.size
+        assert np.max(np.abs(freq - q)) < 0.015
+
+
+def test_topk_edges():
+    x = np.array([1.0, 2.0, 2.0, 2.0, 0.0, 2.0], dtype=np.float32)
+    u = np.linspace(0, 1 - 2 ** -24, 64, dtype=np.float32)
+    rows = np.broadcast_to(x, (64, 6)).copy()
+    # ties go to the lower index: top_k = 2 keeps entries 1 and 2 of the four 2.0s
+    assert native.kept_set(x, 1.0, 1.0, 2).tolist() == [False, True, True, False, False, False]
+    assert set(native.sample_rows(rows, u, top_k=2).tolist()) == {1, 2}
+    # top_k = 1 is the argmax for every u; top_k >= V (or <= 0) is no cut
+    assert set(native.sample_rows(rows, u, top_k=1).tolist()) == {1}
+    assert np.array_equal(native.sample_rows(rows, u, top_k=6), native.sample_rows(rows, u))
+    assert np.array_equal(native.sample_rows(rows, u, top_k=0), native.sample_rows(rows, u))
+    # with top_p the nucleus is taken over the k candidates' renormalised mass
+    assert native.kept_set(x, 1.0, 0.3, 3).tolist() == [False, True, False, False, False, False]
+    assert native.kept_set(x, 1.0, 0.5, 3).tolist() == [False, True, True, False, False, False]
+    # greedy ignores top_k
+    assert native.sample_rows(x, [0.9], do_sample=False, top_k=3)[0] == 1
+
+
 # --------------------------------------------------------------- generate
 GENERATE_RUNS = ["fixed_422", "conc_rep2", "adaptive", "nucleus_095", "chain_boot", "chain_noboot",
-                 "chain_conc_p09"]
+                 "chain_conc_p09", "topk_8", "topk_40_p09"]
 
 
 def oracle_generate_run(r: dict):
@@ -389,7 +445,7 @@ def oracle_generate_run(r: dict):
     cfg = rp.OracleConfig(tree_mode=r["tree_mode"], cpeak_nodes=r.get("cpeak_nodes", 512),
                           max_tree_nodes_per_seq=r["max_tree_nodes_per_seq"], max_tree_depth=r["max_tree_depth"],
                           fixed_tree_topk_by_depth=tuple(r["fixed_tree_topk_by_depth"]),
-                          top_p=r.get("top_p", 1.0),
+                          top_p=r.get("top_p", 1.0), top_k=r.get("top_k"),
                           adaptive_tree_enabled=r.get("adaptive_tree_enabled", False),
                           adaptive_min_topk_by_depth=tuple(r.get("adaptive_min_topk_by_depth", (1, 1, 1))),
                           proposal_mode=r.get("proposal_mode", "medusa"), chain_cell=cell,
