@@ -198,7 +198,6 @@ class FlashMedusaDecoder:
         acc = RolloutStats(min(cfg.num_medusa_heads, len(eng.heads)))
         pending_host = [-1] * B
         graphs, seen = self._graphs, self._seen
-        pinned = None
         rcfg_key = dataclasses.astuple(rcfg)
         setups: dict = {}
         flat_bufs: dict = {}
@@ -206,20 +205,14 @@ class FlashMedusaDecoder:
         timer = self._phase_events(dev)
         use_tree = int(generation_step) >= int(cfg.enable_medusa_spec_after)
 
-        def account(d):
-            """Host bookkeeping of a finished round (tokens, statistics); runs
-            while the next round executes on the device."""
-            rows_d, acc_d, toks_d, dcap_d, pend_before = d
-            for i, r in enumerate(rows_d):
-                generated[r].extend(toks_d[i * dcap_d: i * dcap_d + acc_d[i]])
-            acc.rows(acc_d, pend_before)
+        rows_sent: set = set()
+        pinned = [None, None]  # round outputs, alternating between consecutive rounds
+        n_launched = 0
 
-        deferred = None
-        while any(active_host):
-            # finished rows retire: the round runs on the active rows only
-            # (select_cache_batch semantics), through a row map into the
-            # cache when some rows have finished
-            act_rows = [r for r in range(B) if active_host[r]]
+        def launch(act_rows):
+            """Enqueue one round over act_rows and the copy of its outputs to
+            pinned host memory; returns what processing the round needs."""
+            nonlocal n_launched
             n_active = len(act_rows)
             setup = setups.get(n_active)
             if setup is None:
@@ -238,14 +231,18 @@ class FlashMedusaDecoder:
             plan, nh, dcap, adaptive, params = setup
             if n_active < B:
                 rs = eng.view(st, n_active, n_heads)
-                rows_host = torch.tensor(act_rows, dtype=torch.int32).pin_memory()
-                rs.rows.copy_(rows_host, non_blocking=True)
+                # finished rows only ever leave, so a row count names one row
+                # set within a call: its map is sent once
+                if n_active not in rows_sent:
+                    rows_host = torch.tensor(act_rows, dtype=torch.int32).pin_memory()
+                    rs.rows.copy_(rows_host, non_blocking=True)
+                    rows_sent.add(n_active)
             else:
                 rs = st
             rb = eng.buffers(n_active, plan, nh, dcap, adaptive=adaptive)
             # CUDA events at the phase boundaries on sampled rounds (every
             # round with statistical_time)
-            timed = bool(statistical_time) or acc.rounds % interval == 0
+            timed = bool(statistical_time) or n_launched % interval == 0
             ev = timer if timed else None
             key = (id(rs), n_active, rb.N, tuple(plan.topk_by_depth), plan.node_budget_per_seq, adaptive, rcfg_key,
                    timed)
@@ -265,23 +262,23 @@ class FlashMedusaDecoder:
                 fb = flat_bufs[(id(rb), id(rs))] = torch.empty(sum(t.numel() for t in parts), dtype=torch.int32,
                                                               device=dev)
             torch.cat(parts, out=fb)
-            if pinned is None or pinned.numel() < fb.numel():
-                pinned = torch.empty(fb.numel(), dtype=torch.int32, pin_memory=True)
-            host = pinned[: fb.numel()]
+            slot = n_launched & 1
+            if pinned[slot] is None or pinned[slot].numel() < fb.numel():
+                pinned[slot] = torch.empty(fb.numel(), dtype=torch.int32, pin_memory=True)
+            host = pinned[slot][: fb.numel()]
             host.copy_(fb, non_blocking=True)
-            if deferred is not None:
-                account(deferred)
-                deferred = None
-            torch.cuda.current_stream(dev).synchronize()
-            wall = time.time() - tv
-            phases = [timer[i].elapsed_time(timer[i + 1]) / 1000.0 for i in range(3)] if timed else None
-            vals = host.tolist()
-            Br = n_active  # outputs are per round row: round row i is state row act_rows[i]
-            acc_len = vals[:Br]
-            fin = vals[Br:2 * Br]
-            pend = vals[2 * Br:3 * Br]
-            last = vals[3 * Br:4 * Br]
-            plan_dev = vals[4 * Br:4 * Br + 16]
+            n_launched += 1
+            return act_rows, plan, nh, dcap, adaptive, timed, tv, host.numpy()
+
+        def process(rnd, wall, phases):
+            """Host bookkeeping of a finished round (tokens, statistics); runs
+            while the next round executes on the device."""
+            act_rows, plan, nh, dcap, adaptive, _, _, vals = rnd
+            Br = len(act_rows)  # outputs are per round row: round row i is state row act_rows[i]
+            acc_len = vals[:Br].tolist()
+            pend = vals[2 * Br:3 * Br].tolist()
+            last = vals[3 * Br:4 * Br].tolist()
+            plan_dev = vals[4 * Br:4 * Br + 16].tolist()
             toks = vals[4 * Br + 16:]
             # the round's tree as built on the device (adaptive rounds may be smaller)
             topk_round = plan_dev[2:2 + plan_dev[1]] if nh > 0 else []
@@ -289,22 +286,38 @@ class FlashMedusaDecoder:
             if nh > 0 and n_tree <= 1 and not cfg.allow_recompute_fallback:
                 # the reference's verify needs a tree cache to extract from (:2881-2882)
                 raise RuntimeError("KV extraction was requested but no tree cache was available")
-            acc.round(n_active, plan.node_budget_per_seq, topk_round, n_tree, last, use_tree, nh, wall, phases)
-            acc.last_plan = {"B_cur": n_active, "node_budget_per_seq": plan.node_budget_per_seq,
+            acc.round(Br, plan.node_budget_per_seq, topk_round, n_tree, last, use_tree, nh, wall, phases)
+            acc.last_plan = {"B_cur": Br, "node_budget_per_seq": plan.node_budget_per_seq,
                              "active_heads": plan.active_heads, "topk_by_depth": list(topk_round),
                              "actual_nodes": n_tree, "proposal_mode": "chain" if rcfg.chain else "medusa",
                              "adaptive_tree": {"topk": list(topk_round)} if adaptive else {},
                              "nodes_by_head": tree_level_counts(topk_round, n_tree)}
-            # what the next round's shape depends on now; the rest after its launch
             pend_before = [pending_host[r] for r in act_rows]
-            for i, r in enumerate(act_rows):
-                row_len_host[r] += acc_len[i]
-                if fin[i]:
-                    active_host[r] = False
-                pending_host[r] = pend[i]
-            deferred = (act_rows, acc_len, toks, dcap, pend_before)
-        if deferred is not None:
-            account(deferred)
+            for i, row in enumerate(act_rows):
+                row_len_host[row] += acc_len[i]
+                pending_host[row] = pend[i]
+                generated[row].extend(toks[i * dcap: i * dcap + acc_len[i]].tolist())
+            acc.rows(acc_len, pend_before)
+
+        # One round in flight ahead of the host: as soon as a round's outputs
+        # are on the host, the next round (whose row set depends only on the
+        # finished flags) is launched, and the finished round's tokens and
+        # statistics are processed while it runs.
+        cur = launch([r for r in range(B) if active_host[r]])
+        while cur is not None:
+            torch.cuda.current_stream(dev).synchronize()
+            wall = time.time() - cur[6]
+            phases = [timer[i].elapsed_time(timer[i + 1]) / 1000.0 for i in range(3)] if cur[5] else None
+            vals = cur[7]
+            Br = len(cur[0])
+            fin = vals[Br:2 * Br]
+            if fin.any():
+                for i in fin.nonzero()[0].tolist():
+                    active_host[cur[0][i]] = False
+            act_rows = [r for r in cur[0] if active_host[r]]
+            nxt = launch(act_rows) if act_rows else None
+            process(cur, wall, phases)
+            cur = nxt
         return acc.result(generated, prefill_time=prefill_time, total_time=time.time() - total_start,
                           statistical_time=bool(statistical_time), cache_update_mode=cfg.cache_update_mode)
 
