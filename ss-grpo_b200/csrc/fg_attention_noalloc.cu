@@ -75,9 +75,10 @@ extern "C" fg_status fg_tree_attention_noalloc(const void* q, int32_t dtype, con
     if (need > 0) {
         scratch = fg::noalloc_scratch_ptr();
         if (!scratch) return FG_ECUDA;
-        // the split counters (the last `items` int32 of the layout) must start at zero
-        const int G = n_q_heads / n_kv_heads;
-        const size_t items = (size_t)B * n_kv_heads * ((n_nodes * G + fg::kMaxRows - 1) / fg::kMaxRows);
+        // the split counters (the last plan.items int32 of the layout, one per
+        // row group of a KV head) must start at zero
+        const size_t items =
+            (size_t)plan_attention(B, n_nodes, n_q_heads, n_kv_heads, num_splits, kv_max).items;
         const cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + need - items * sizeof(int32_t), 0,
                                               items * sizeof(int32_t), (cudaStream_t)stream);
         if (e != cudaSuccess) {
