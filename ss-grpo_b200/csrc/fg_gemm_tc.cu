@@ -101,9 +101,8 @@ __device__ __forceinline__ float bf(float v) { return __bfloat162float(__float2b
 // fg_silu_mul evaluates it (the result is rounded to bf16)
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// 8 consecutive bf16 as floats (16-byte load)
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
+// 8 bf16 held in a 16-byte vector, as floats
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -113,10 +112,36 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
     }
 }
 
-// The epilogue of 8 consecutive outputs [col, col + 8) of one row, from the
-// fp32 accumulators g (and u for SwiGLU), stored as one 16-byte vector.
+// The bias and residual inputs of one 32-column chunk of a row, loaded ahead
+// of the accumulator they are added to.  The loads of a chunk are issued
+// together (and before the tile's MMAs finish): added one 8-wide group at a
+// time, each load would wait behind the previous group's store, which may
+// alias it (the residual add runs in place).
+struct EpiIn {
+    uint4 b[4];
+    uint4 r[4];
+};
+
 template <int EPI>
-__device__ __forceinline__ void finish8(const Params& p, int row, int col, const float* g, const float* u) {
+__device__ __forceinline__ void epi_load(const Params& p, int row, int col0, int n, EpiIn& in) {
+    if constexpr (EPI == FG_EPI_SWIGLU) return;
+    if (p.splits != 1 || row >= p.M) return;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (8 * q < n && col0 + 8 * q < p.N) {
+            if (p.bias) in.b[q] = *reinterpret_cast<const uint4*>(p.bias + col0 + 8 * q);
+            if constexpr (EPI == FG_EPI_RESID)
+                in.r[q] = *reinterpret_cast<const uint4*>(p.resid + (int64_t)row * p.ld_resid + col0 + 8 * q);
+        }
+    }
+}
+
+// The epilogue of 8 consecutive outputs [col, col + 8) of one row, from the
+// fp32 accumulators g (and u for SwiGLU) and the preloaded bias / residual
+// vectors, stored as one 16-byte vector.
+template <int EPI>
+__device__ __forceinline__ void finish8_in(const Params& p, int row, int col, const float* g, const float* u,
+                                           const uint4& bq, const uint4& rq) {
     float o[8];
     if constexpr (EPI == FG_EPI_SWIGLU) {
 #pragma unroll
@@ -126,13 +151,13 @@ __device__ __forceinline__ void finish8(const Params& p, int row, int col, const
         for (int e = 0; e < 8; ++e) o[e] = g[e];
         if (p.bias) {
             float b[8];
-            load8(p.bias + col, b);
+            unpack8(bq, b);
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] += b[e];
         }
         if constexpr (EPI == FG_EPI_RESID) {
             float r[8];
-            load8(p.resid + (int64_t)row * p.ld_resid + col, r);
+            unpack8(rq, r);
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] += r[e];
         }
@@ -145,17 +170,28 @@ __device__ __forceinline__ void finish8(const Params& p, int row, int col, const
     *reinterpret_cast<uint4*>(p.out + (int64_t)row * p.ld_out + col) = v;
 }
 
+// finish8_in with its inputs loaded here (the split-K reduce, one group per thread)
+template <int EPI>
+__device__ __forceinline__ void finish8(const Params& p, int row, int col, const float* g, const float* u) {
+    uint4 bq = make_uint4(0, 0, 0, 0), rq = make_uint4(0, 0, 0, 0);
+    if constexpr (EPI != FG_EPI_SWIGLU) {
+        if (p.bias) bq = *reinterpret_cast<const uint4*>(p.bias + col);
+        if constexpr (EPI == FG_EPI_RESID) rq = *reinterpret_cast<const uint4*>(p.resid + (int64_t)row * p.ld_resid + col);
+    }
+    finish8_in<EPI>(p, row, col, g, u, bq, rq);
+}
+
 // One 32-column chunk of a warp's outputs after the TMEM reads: the epilogue
 // of its 8-wide groups (one k range), or its fp32 partials (split-K).
 template <int EPI>
 __device__ __forceinline__ void emit32(const Params& p, int row, int col0, int n, int ks, const float* g,
-                                       const float* u) {
+                                       const float* u, const EpiIn& in) {
     if (row >= p.M) return;
     if (p.splits == 1) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             if (8 * q >= n || col0 + 8 * q >= p.N) break;
-            finish8<EPI>(p, row, col0 + 8 * q, g + 8 * q, u + 8 * q);
+            finish8_in<EPI>(p, row, col0 + 8 * q, g + 8 * q, u + 8 * q, in.b[q], in.r[q]);
         }
     } else {
         const int64_t nw = EPI == FG_EPI_SWIGLU ? 2 * (int64_t)p.N : p.N;
@@ -293,20 +329,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int span = p.bn / 2, o0 = grp * span;
         for (int i = 0; i < my_units; ++i) {
             const int a = i & 1;
-            if (!__all_sync(0xffffffffu, bar_wait(&bars->acc_full[a], (i >> 1) & 1, abort_flag))) break;
-            fence_after();
             int nt, ks, mt;
             decode(p, (int)blockIdx.x + i * (int)gridDim.x, nt, ks, mt);
             const int row = mt * kBM + q4 * 32 + lane;
+            const int col0 = nt * p.bn + o0;
+            // the first chunk's bias / residual load while the MMAs run
+            EpiIn cur;
+            epi_load<EPI>(p, row, col0, min(32, span), cur);
+            if (!__all_sync(0xffffffffu, bar_wait(&bars->acc_full[a], (i >> 1) & 1, abort_flag))) break;
+            fence_after();
             const uint32_t acc = lane_addr + (uint32_t)(a * 256);
             // 32-column TMEM reads (warp-uniform); columns past this warp's
             // range stay inside the accumulator and are dropped
 #pragma unroll 1
             for (int c = 0; c < span; c += 32) {
+                EpiIn nxt;
+                if (c + 32 < span) epi_load<EPI>(p, row, col0 + c + 32, min(32, span - c - 32), nxt);
                 float g[32], u[32];
                 tld32(acc + (uint32_t)(o0 + c), g);
                 if constexpr (EPI == FG_EPI_SWIGLU) tld32(acc + (uint32_t)(p.bn + o0 + c), u);
-                emit32<EPI>(p, row, nt * p.bn + o0 + c, min(32, span - c), ks, g, u);
+                emit32<EPI>(p, row, col0 + c, min(32, span - c), ks, g, u, cur);
+                cur = nxt;
             }
             fence_before();
             __syncwarp();
@@ -514,18 +557,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
         const uint32_t empty0 = at_rank0(&bars->acc_empty[0]), empty1 = at_rank0(&bars->acc_empty[1]);
         for (int i = 0; i < my_units; ++i) {
             const int a = i & 1;
-            if (!__all_sync(0xffffffffu, bar_wait(&bars->acc_full[a], (i >> 1) & 1, abort_flag))) break;
-            fence_after();
             int nt, ks, mt;
             decode(p, cid + i * ncl, nt, ks, mt);
             const int row = mt * kTile + (int)rank * kBM + q4 * 32 + lane;
+            const int col0 = nt * p.bn + o0;
+            EpiIn cur;
+            epi_load<EPI>(p, row, col0, min(32, span), cur);
+            if (!__all_sync(0xffffffffu, bar_wait(&bars->acc_full[a], (i >> 1) & 1, abort_flag))) break;
+            fence_after();
             const uint32_t acc = lane_addr + (uint32_t)(a * 256);
 #pragma unroll 1
             for (int c = 0; c < span; c += 32) {
+                EpiIn nxt;
+                if (c + 32 < span) epi_load<EPI>(p, row, col0 + c + 32, min(32, span - c - 32), nxt);
                 float g[32], u[32];
                 tld32(acc + (uint32_t)(o0 + c), g);
                 if constexpr (EPI == FG_EPI_SWIGLU) tld32(acc + (uint32_t)(p.bn + o0 + c), u);
-                emit32<EPI>(p, row, nt * p.bn + o0 + c, min(32, span - c), ks, g, u);
+                emit32<EPI>(p, row, col0 + c, min(32, span - c), ks, g, u, cur);
+                cur = nxt;
             }
             fence_before();
             __syncwarp();
