@@ -40,8 +40,9 @@ def _call(lib, name, *args):
 
 
 @pytest.mark.parametrize("B,n,hq,hkv,L,splits", [(8, 13, 12, 2, 1024, 3), (4, 32, 28, 4, 600, 0), (2, 64, 32, 8, 300, 2),
-                                                  # the 256-row form (224 rows per KV head, 160 items), split
-                                                  (40, 32, 28, 4, 300, 2)])
+                                                  # the 256-row form (224 rows per KV head, 160 items); its
+                                                  # split-K partials would outgrow the shared buffer
+                                                  (40, 32, 28, 4, 300, 0)])
 def test_noalloc_attention_matches_workspace_entry_point(B, n, hq, hkv, L, splits):
     from flashgrpo_b200 import _native, ops
 
