@@ -70,6 +70,7 @@ struct Params {
     int32_t bn;        // outputs per tile
     int32_t nb;        // W rows per tile = MMA N (bn, or 2 bn for SwiGLU)
     int32_t n_mt, n_nt, splits, nk, units, stage_bytes;
+    int32_t cps;       // 64-wide k chunks per ring stage (1, or 2 when nk is even)
     const __nv_bfloat16* bias;   // [N] or null
     const __nv_bfloat16* resid;  // FG_EPI_RESID: [M, ld_resid]
     int64_t ld_resid;
@@ -94,6 +95,31 @@ __device__ __forceinline__ void decode(const Params& p, int u, int& nt, int& ks,
     const int r = u - nt * per_nt;
     ks = r / p.n_mt;
     mt = r - ks * p.n_mt;
+}
+
+// The k range [kc0, kc1) of split ks, in whole stages of cps chunks.
+__device__ __forceinline__ void k_range(const Params& p, int ks, int& kc0, int& kc1) {
+    const int np = p.nk / p.cps;
+    kc0 = p.cps * (ks * np / p.splits);
+    kc1 = p.cps * ((ks + 1) * np / p.splits);
+}
+
+// One stage's boxes through the k-chunked maps: coordinates (0, row, chunk)
+// or, for the stacked gate/up weights, (0, row, half, chunk).  A box spans
+// cps chunks, so a stage is one instruction per operand.
+__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int row, int kc, uint64_t* b, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4}], [%5], %6;" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(kc), "r"(sa(b)), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma_4d(void* dst, const CUtensorMap* map, int row, int kc, uint64_t* b, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4, %5}], [%6], %7;" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(0), "r"(kc), "r"(sa(b)), "l"(pol)
+        : "memory");
 }
 
 __device__ __forceinline__ float bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -217,12 +243,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     volatile int* abort_flag = &bars->abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int my_units = p.units > (int)blockIdx.x ? (p.units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const uint32_t stage_tx = (uint32_t)(kABytes + p.nb * 128);
+    const int cps = p.cps;
+    const uint32_t stage_tx = (uint32_t)p.stage_bytes;
 
+    // W boxes of a stage: the tile's rows for cps chunks (SwiGLU: its gate
+    // rows then its up rows per chunk, through the 4-D map)
     auto load_w = [&](uint8_t* st, int nt, int kc, uint64_t* bar, uint64_t pol) {
-        lmh::tma_2d(st + kABytes, &tmW, kc * kKc, nt * p.bn, bar, pol);
         if constexpr (EPI == FG_EPI_SWIGLU)
-            lmh::tma_2d(st + kABytes + p.bn * 128, &tmW, kc * kKc, p.N + nt * p.bn, bar, pol);
+            tma_4d(st + cps * kABytes, &tmW, nt * p.bn, kc, bar, pol);
+        else
+            tma_3d(st + cps * kABytes, &tmW, nt * p.bn, kc, bar, pol);
     };
     // the first stages of this CTA's first unit: weights before the grid dependency wait
     int pre = 0;
@@ -241,12 +271,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (my_units > 0) {
             int nt, ks, mt;
             decode(p, blockIdx.x, nt, ks, mt);
-            const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
-            pre = min(STAGES, kc1 - kc0);
+            int kc0, kc1;
+            k_range(p, ks, kc0, kc1);
+            pre = min(STAGES, (kc1 - kc0) / cps);
             const uint64_t pol_w = lmh::policy_evict_first();
             for (int j = 0; j < pre; ++j) {
                 bar_expect(&bars->full[j], stage_tx);
-                load_w(smem + kOffStage + j * p.stage_bytes, nt, kc0 + j, &bars->full[j], pol_w);
+                load_w(smem + kOffStage + j * p.stage_bytes, nt, kc0 + j * cps, &bars->full[j], pol_w);
             }
         }
     }
@@ -273,8 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             for (int i = 0; i < my_units && ok; ++i) {
                 int nt, ks, mt;
                 decode(p, (int)blockIdx.x + i * (int)gridDim.x, nt, ks, mt);
-                const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
-                for (int kc = kc0; kc < kc1; ++kc, ++it) {
+                int kc0, kc1;
+                k_range(p, ks, kc0, kc1);
+                for (int kc = kc0; kc < kc1; kc += cps, ++it) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !(ok = bar_wait(&bars->empty[s], ((it / STAGES) - 1) & 1, abort_flag)))
                         break;
@@ -283,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         bar_expect(&bars->full[s], stage_tx);
                         load_w(st, nt, kc, &bars->full[s], pol_w);
                     }
-                    lmh::tma_2d(st, &tmX, kc * kKc, mt * kBM, &bars->full[s], pol_x);
+                    tma_3d(st, &tmX, mt * kBM, kc, &bars->full[s], pol_x);
                     issued = it + 1;
                 }
             }
@@ -299,20 +331,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             for (int i = 0; i < my_units && ok; ++i) {
                 int nt, ks, mt;
                 decode(p, (int)blockIdx.x + i * (int)gridDim.x, nt, ks, mt);
-                const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
+                int kc0, kc1;
+                k_range(p, ks, kc0, kc1);
                 const int a = i & 1;
                 if (i >= 2 && !(ok = bar_wait(&bars->acc_empty[a], ((i >> 1) - 1) & 1, abort_flag))) break;
                 fence_after();
-                for (int kc = kc0; kc < kc1; ++kc, ++it) {
+                for (int kc = kc0; kc < kc1; kc += cps, ++it) {
                     const int s = it % STAGES;
                     if (!(ok = bar_wait(&bars->full[s], (it / STAGES) & 1, abort_flag))) break;
                     fence_after();
-                    const uint32_t a_addr = sa(smem + kOffStage + s * p.stage_bytes);
-                    const uint32_t b_addr = a_addr + (uint32_t)kABytes;
+                    const uint32_t a_base = sa(smem + kOffStage + s * p.stage_bytes);
+                    const uint32_t b_base = a_base + (uint32_t)(cps * kABytes);
+                    for (int c = 0; c < cps; ++c) {
+                        const uint32_t a_addr = a_base + (uint32_t)(c * kABytes);
+                        const uint32_t b_addr = b_base + (uint32_t)(c * p.nb * 128);
 #pragma unroll
-                    for (int kk = 0; kk < kKc / 16; ++kk)
-                        umma(tmem + (uint32_t)(a * 256), sdesc(a_addr + kk * 32, 16, 1024),
-                             sdesc(b_addr + kk * 32, 16, 1024), idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < kKc / 16; ++kk)
+                            umma(tmem + (uint32_t)(a * 256), sdesc(a_addr + kk * 32, 16, 1024),
+                                 sdesc(b_addr + kk * 32, 16, 1024), idesc, (kc > kc0 || c > 0 || kk > 0) ? 1u : 0u);
+                    }
                     umma_commit(&bars->empty[s]);
                 }
                 if (ok) umma_commit(&bars->acc_full[a]);
@@ -398,12 +435,13 @@ __device__ __forceinline__ uint32_t at_rank0(const void* p) {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tma_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1, uint32_t mbar,
+// A stage's box through a k-chunked map, completing on the even CTA's barrier
+__device__ __forceinline__ void tma_3d_pair(void* dst, const CUtensorMap* map, int row, int kc, uint32_t mbar,
                                             uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(sa(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(mbar), "l"(policy)
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(sa(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(kc), "r"(mbar), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -440,8 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
     const uint32_t rank = cluster_rank();
     const int cid = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
     const int my_units = p.units > cid ? (p.units - 1 - cid) / ncl + 1 : 0;
-    const int bh = p.nb / 2;  // weight rows this CTA loads per stage
-    const uint32_t pair_tx = 2u * (uint32_t)(kABytes + bh * 128);
+    const int bh = p.nb / 2;  // weight rows this CTA loads per chunk
+    const int cps = p.cps;
+    const uint32_t pair_tx = 2u * (uint32_t)p.stage_bytes;
     constexpr int kTile = 2 * kBM;  // tokens per tile
     auto w_row = [&](int nt) {
         return EPI == FG_EPI_SWIGLU ? (int)rank * p.N + nt * p.bn : nt * p.bn + (int)rank * bh;
@@ -476,13 +515,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
     if (threadIdx.x == 0 && my_units > 0) {
         int nt, ks, mt;
         decode(p, cid, nt, ks, mt);
-        const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
-        pre = min(STAGES, kc1 - kc0);
+        int kc0, kc1;
+        k_range(p, ks, kc0, kc1);
+        pre = min(STAGES, (kc1 - kc0) / cps);
         const uint64_t pol_w = lmh::policy_evict_first();
         for (int j = 0; j < pre; ++j) {
             uint8_t* st = smem + kOffStage + j * p.stage_bytes;
             if (rank == 0) bar_expect(&bars->full[j], pair_tx);
-            tma_2d_pair(st + kABytes, &tmW, (kc0 + j) * kKc, w_row(nt), at_rank0(&bars->full[j]), pol_w);
+            tma_3d_pair(st + cps * kABytes, &tmW, w_row(nt), kc0 + j * cps, at_rank0(&bars->full[j]), pol_w);
         }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -497,8 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
             for (int i = 0; i < my_units && ok; ++i) {
                 int nt, ks, mt;
                 decode(p, cid + i * ncl, nt, ks, mt);
-                const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
-                for (int kc = kc0; kc < kc1; ++kc, ++it) {
+                int kc0, kc1;
+                k_range(p, ks, kc0, kc1);
+                for (int kc = kc0; kc < kc1; kc += cps, ++it) {
                     const int s = it % STAGES;
                     if (it >= STAGES && !(ok = bar_wait(&bars->empty[s], ((it / STAGES) - 1) & 1, abort_flag)))
                         break;
@@ -506,9 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
                     const uint32_t full0 = at_rank0(&bars->full[s]);
                     if (it >= pre) {
                         if (rank == 0) bar_expect(&bars->full[s], pair_tx);
-                        tma_2d_pair(st + kABytes, &tmW, kc * kKc, w_row(nt), full0, pol_w);
+                        tma_3d_pair(st + cps * kABytes, &tmW, w_row(nt), kc, full0, pol_w);
                     }
-                    tma_2d_pair(st, &tmX, kc * kKc, mt * kTile + (int)rank * kBM, full0, pol_x);
+                    tma_3d_pair(st, &tmX, mt * kTile + (int)rank * kBM, kc, full0, pol_x);
                     issued = it + 1;
                 }
             }
@@ -528,20 +569,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(const __grid_con
             for (int i = 0; i < my_units && ok; ++i) {
                 int nt, ks, mt;
                 decode(p, cid + i * ncl, nt, ks, mt);
-                const int kc0 = ks * p.nk / p.splits, kc1 = (ks + 1) * p.nk / p.splits;
+                int kc0, kc1;
+                k_range(p, ks, kc0, kc1);
                 const int a = i & 1;
                 if (i >= 2 && !(ok = bar_wait(&bars->acc_empty[a], ((i >> 1) - 1) & 1, abort_flag))) break;
                 fence_after();
-                for (int kc = kc0; kc < kc1; ++kc, ++it) {
+                for (int kc = kc0; kc < kc1; kc += cps, ++it) {
                     const int s = it % STAGES;
                     if (!(ok = bar_wait(&bars->full[s], (it / STAGES) & 1, abort_flag))) break;
                     fence_after();
-                    const uint32_t a_addr = sa(smem + kOffStage + s * p.stage_bytes);
-                    const uint32_t b_addr = a_addr + (uint32_t)kABytes;
+                    const uint32_t a_base = sa(smem + kOffStage + s * p.stage_bytes);
+                    const uint32_t b_base = a_base + (uint32_t)(cps * kABytes);
+                    for (int c = 0; c < cps; ++c) {
+                        const uint32_t a_addr = a_base + (uint32_t)(c * kABytes);
+                        const uint32_t b_addr = b_base + (uint32_t)(c * bh * 128);
 #pragma unroll
-                    for (int kk = 0; kk < kKc / 16; ++kk)
-                        umma_pair(tmem + (uint32_t)(a * 256), sdesc(a_addr + kk * 32, 16, 1024),
-                                  sdesc(b_addr + kk * 32, 16, 1024), idesc, (kc > kc0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < kKc / 16; ++kk)
+                            umma_pair(tmem + (uint32_t)(a * 256), sdesc(a_addr + kk * 32, 16, 1024),
+                                      sdesc(b_addr + kk * 32, 16, 1024), idesc,
+                                      (kc > kc0 || c > 0 || kk > 0) ? 1u : 0u);
+                    }
                     umma_commit_pair(&bars->empty[s]);
                 }
                 if (ok) umma_commit_pair(&bars->acc_full[a]);
@@ -713,12 +760,50 @@ static cudaError_t launch_tile(cudaLaunchConfig_t& cfg, const CUtensorMap& mx, c
     return cudaLaunchKernelEx(&cfg, KERNEL, mx, mw, p);
 }
 
+// ring slots compiled: 2, 3, 4, 6, 8 on one SM (k-chunk pairs or single
+// chunks), 3 or 6 on a pair
 template <int EPI>
-static cudaError_t launch_1sm(int stages, cudaLaunchConfig_t& cfg, const CUtensorMap& mx, const CUtensorMap& mw,
+static cudaError_t launch_1sm(int slots, cudaLaunchConfig_t& cfg, const CUtensorMap& mx, const CUtensorMap& mw,
                               const Params& p) {
-    return stages == 8   ? launch_tile<gemm_kernel<EPI, 8>>(cfg, mx, mw, p)
-           : stages == 6 ? launch_tile<gemm_kernel<EPI, 6>>(cfg, mx, mw, p)
-                         : launch_tile<gemm_kernel<EPI, 4>>(cfg, mx, mw, p);
+    return slots == 8   ? launch_tile<gemm_kernel<EPI, 8>>(cfg, mx, mw, p)
+           : slots == 6 ? launch_tile<gemm_kernel<EPI, 6>>(cfg, mx, mw, p)
+           : slots == 4 ? launch_tile<gemm_kernel<EPI, 4>>(cfg, mx, mw, p)
+           : slots == 3 ? launch_tile<gemm_kernel<EPI, 3>>(cfg, mx, mw, p)
+                        : launch_tile<gemm_kernel<EPI, 2>>(cfg, mx, mw, p);
+}
+template <int EPI>
+static cudaError_t launch_pair(int slots, cudaLaunchConfig_t& cfg, const CUtensorMap& mx, const CUtensorMap& mw,
+                               const Params& p) {
+    return slots == 6 ? launch_tile<gemm_pair_kernel<EPI, 6>>(cfg, mx, mw, p)
+                      : launch_tile<gemm_pair_kernel<EPI, 3>>(cfg, mx, mw, p);
+}
+
+// [rows, K] bf16 seen as (64 k, row, k chunk): a box of box_rows rows and
+// cps chunks lands as cps consecutive 128B-swizzled [box_rows x 64] tiles.
+static bool make_map_kc(CUtensorMap* map, const void* base, int64_t rows, int64_t K, uint32_t box_rows, int cps) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kKc, (cuuint64_t)rows, (cuuint64_t)(K / kKc)};
+    const cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)kKc * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kKc, box_rows, (cuuint32_t)cps};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// The stacked gate/up weights [2 I, K] as (64 k, row, half, k chunk): a box
+// of bn rows, both halves and cps chunks lands per chunk as the bn gate rows
+// followed by the bn up rows, the B operand of one N = 2 bn MMA.
+static bool make_map_glu(CUtensorMap* map, const void* base, int64_t I, int64_t K, uint32_t bn, int cps) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)kKc, (cuuint64_t)I, 2, (cuuint64_t)(K / kKc)};
+    const cuuint64_t strides[3] = {(cuuint64_t)K * 2, (cuuint64_t)I * K * 2, (cuuint64_t)kKc * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)kKc, bn, 2, (cuuint32_t)cps};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static fg_status run(const void* x, int32_t M, int32_t K, const void* w, int32_t N, const void* bias,
@@ -747,7 +832,25 @@ static fg_status run(const void* x, int32_t M, int32_t K, const void* w, int32_t
     if (splits > p.nk) return FG_EINVAL;
     p.splits = splits;
     p.units = p.n_mt * p.n_nt * splits;
-    p.stage_bytes = stage_bytes(pair, nb);
+    // `stages` k chunks in flight, as ring slots of two chunks each when K
+    // has an even number of chunks (one TMA instruction per operand and
+    // stage moves twice the bytes: the per-SM ingest grows with the bytes per
+    // instruction); as many two-chunk slots as fit, at least two
+    p.cps = 1;
+    int slots = stages;
+    if (p.nk % 2 == 0 && splits <= p.nk / 2) {
+        const int fit2 = (kSmemMax - 1024 - kOffStage) / (2 * stage_bytes(pair, nb));
+        const int want = pair ? 3 : min(stages / 2, 4);
+        if (fit2 >= 2) {
+            p.cps = 2;
+            slots = pair ? (fit2 >= 3 ? 3 : 0) : min(want, fit2);
+            if (slots == 0) {
+                p.cps = 1;
+                slots = stages;
+            }
+        }
+    }
+    p.stage_bytes = p.cps * stage_bytes(pair, nb);
     p.bias = (const __nv_bfloat16*)bias;
     p.resid = (const __nv_bfloat16*)resid;
     p.ld_resid = ld_resid;
@@ -763,12 +866,14 @@ static fg_status run(const void* x, int32_t M, int32_t K, const void* w, int32_t
     // (SwiGLU: the gate rows on the even CTA, the up rows on the odd one)
     const int wbox = pair ? nb / 2 : bn;
     CUtensorMap mx, mw;
-    if (!lmh::make_map_2d(&mx, x, K, M, K, kBM) ||
-        !lmh::make_map_2d(&mw, w, K, epi == FG_EPI_SWIGLU ? 2 * (int64_t)N : N, K, (uint32_t)wbox))
+    const bool glu4 = epi == FG_EPI_SWIGLU && !pair;
+    if (!make_map_kc(&mx, x, M, K, kBM, p.cps) ||
+        !(glu4 ? make_map_glu(&mw, w, N, K, (uint32_t)bn, p.cps)
+               : make_map_kc(&mw, w, epi == FG_EPI_SWIGLU ? 2 * (int64_t)N : N, K, (uint32_t)wbox, p.cps)))
         return FG_EINVAL;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = 1024 + kOffStage + stages * p.stage_bytes;
+    cfg.dynamicSmemBytes = 1024 + kOffStage + slots * p.stage_bytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -783,15 +888,15 @@ static fg_status run(const void* x, int32_t M, int32_t K, const void* w, int32_t
         const int pairs = p.units < sms / 2 ? p.units : sms / 2;
         cfg.gridDim = dim3(2 * pairs);
         cfg.numAttrs = 2;
-        e = epi == FG_EPI_STORE   ? launch_tile<gemm_pair_kernel<FG_EPI_STORE, kStagesPair>>(cfg, mx, mw, p)
-            : epi == FG_EPI_RESID ? launch_tile<gemm_pair_kernel<FG_EPI_RESID, kStagesPair>>(cfg, mx, mw, p)
-                                  : launch_tile<gemm_pair_kernel<FG_EPI_SWIGLU, kStagesPair>>(cfg, mx, mw, p);
+        e = epi == FG_EPI_STORE   ? launch_pair<FG_EPI_STORE>(slots, cfg, mx, mw, p)
+            : epi == FG_EPI_RESID ? launch_pair<FG_EPI_RESID>(slots, cfg, mx, mw, p)
+                                  : launch_pair<FG_EPI_SWIGLU>(slots, cfg, mx, mw, p);
     } else {
         cfg.gridDim = dim3(p.units < sms ? p.units : sms);
         cfg.numAttrs = 1;
-        e = epi == FG_EPI_STORE   ? launch_1sm<FG_EPI_STORE>(stages, cfg, mx, mw, p)
-            : epi == FG_EPI_RESID ? launch_1sm<FG_EPI_RESID>(stages, cfg, mx, mw, p)
-                                  : launch_1sm<FG_EPI_SWIGLU>(stages, cfg, mx, mw, p);
+        e = epi == FG_EPI_STORE   ? launch_1sm<FG_EPI_STORE>(slots, cfg, mx, mw, p)
+            : epi == FG_EPI_RESID ? launch_1sm<FG_EPI_RESID>(slots, cfg, mx, mw, p)
+                                  : launch_1sm<FG_EPI_SWIGLU>(slots, cfg, mx, mw, p);
     }
     if (e == cudaSuccess && splits > 1) {
         const int64_t items = (int64_t)M * (N / 8);
