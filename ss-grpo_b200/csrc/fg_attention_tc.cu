@@ -435,7 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             constexpr uint32_t id_pv = idesc_bf16(kD, true);
             const uint32_t q_addr = sa(smem + kOffQ);
             int nq = 0, npv = 0;
-            bool ok = true;
             uint64_t t_idle = 0;
             for (uint32_t spin = 0; npv < nmine; ++spin) {
                 bool progress = false;
@@ -475,22 +474,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                     t_idle = 0;
                 } else if ((spin & 255u) == 0u) {
                     // bounded like every other wait: ~1 s without progress aborts the CTA
-                    if (*abort_flag) {
-                        ok = false;
-                        break;
-                    }
+                    if (*abort_flag) break;
                     const uint64_t now = gtime();
                     if (t_idle == 0) {
                         t_idle = now;
                     } else if ((int64_t)(now - t_idle) > kWaitNs) {
                         *abort_flag = 1;
                         atomicCAS(&g_fg_error_word, 0, FG_ETIMEOUT);
-                        ok = false;
                         break;
                     }
                 }
             }
-            (void)ok;
             // everything issued has completed before TMEM is read or freed
             umma_commit(&bars->drain);
             bar_drain(&bars->drain, 0);
