@@ -309,6 +309,10 @@ def gen_generate():
         "topk_40_p09": dict(tree_mode="concurrency_aware", cpeak_nodes=64, fixed_tree_topk_by_depth=(4, 3, 2),
                             max_tree_nodes_per_seq=16, max_tree_depth=4, repeats=2, max_new=16, seed=29, top_k=40,
                             top_p=0.9),
+        # top-k draws with chain proposals
+        "chain_topk16": dict(tree_mode="fixed", fixed_tree_topk_by_depth=(3, 2, 2), max_tree_nodes_per_seq=16,
+                             max_tree_depth=4, repeats=1, max_new=16, seed=31, proposal_mode="chain",
+                             chain_bootstrap_from_medusa=True, top_k=16),
     }
     model = synth.build_model(1)
     ids, mask = synth.random_prompts(4, 128, 4096, seed=0)

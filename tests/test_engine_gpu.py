@@ -49,6 +49,7 @@ def _heads_list(st, n):
     dict(tree_mode="fixed", fixed=(4, 2, 2), mx=16, depth=4, repeats=1, max_new=20, seed=23, top_k=8),
     dict(tree_mode="concurrency_aware", cpeak=64, fixed=(4, 3, 2), mx=16, depth=4, repeats=2, max_new=16, seed=29,
          top_k=40, top_p=0.9),
+    dict(tree_mode="fixed", fixed=(3, 2, 2), mx=16, depth=4, repeats=1, max_new=16, seed=31, chain=True, top_k=16),
 ])
 def test_generate_config1_matches_oracle(run):
     from flashgrpo_b200.decoding.flash_medusa_decoder import FlashMedusaConfig, FlashMedusaDecoder

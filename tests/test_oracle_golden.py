@@ -426,7 +426,7 @@ def test_topk_edges():
 
 # --------------------------------------------------------------- generate
 GENERATE_RUNS = ["fixed_422", "conc_rep2", "adaptive", "nucleus_095", "chain_boot", "chain_noboot",
-                 "chain_conc_p09", "topk_8", "topk_40_p09"]
+                 "chain_conc_p09", "topk_8", "topk_40_p09", "chain_topk16"]
 
 
 def oracle_generate_run(r: dict):
