@@ -296,65 +296,65 @@ __global__ void __launch_bounds__(kThreads, 1) lmhead_topk_kernel(const __grid_c
                                     if (vb + j < v_end) dst[j] = x[j];
                             }
                         }
-                        continue;
-                    }
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(__float2bfloat16_rn(x[j]));
-                    if (write) {
-                        __nv_bfloat16* dst = p.logits + (int64_t)row * p.logits_ld + vb;
-                        if (p.logits_vec && vb + 32 <= v_end) {
+                        for (int j = 0; j < 32; ++j) x[j] = __bfloat162float(__float2bfloat16_rn(x[j]));
+                        if (write) {
+                            __nv_bfloat16* dst = p.logits + (int64_t)row * p.logits_ld + vb;
+                            if (p.logits_vec && vb + 32 <= v_end) {
 #pragma unroll
-                            for (int qq = 0; qq < 4; ++qq) {
-                                uint4 u;
-                                u.x = tc::pack2(x[8 * qq + 0], x[8 * qq + 1]);
-                                u.y = tc::pack2(x[8 * qq + 2], x[8 * qq + 3]);
-                                u.z = tc::pack2(x[8 * qq + 4], x[8 * qq + 5]);
-                                u.w = tc::pack2(x[8 * qq + 6], x[8 * qq + 7]);
-                                *reinterpret_cast<uint4*>(dst + 8 * qq) = u;
-                            }
-                        } else {
+                                for (int qq = 0; qq < 4; ++qq) {
+                                    uint4 u;
+                                    u.x = tc::pack2(x[8 * qq + 0], x[8 * qq + 1]);
+                                    u.y = tc::pack2(x[8 * qq + 2], x[8 * qq + 3]);
+                                    u.z = tc::pack2(x[8 * qq + 4], x[8 * qq + 5]);
+                                    u.w = tc::pack2(x[8 * qq + 6], x[8 * qq + 7]);
+                                    *reinterpret_cast<uint4*>(dst + 8 * qq) = u;
+                                }
+                            } else {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (vb + j < v_end) dst[j] = __float2bfloat16_rn(x[j]);
-                        }
-                    }
-                    if (topk) {
-                        const int n_ok = min(32, v_end - vb);
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) x[j] = j < n_ok ? x[j] : -INFINITY;
-                        if (p.want_lse) {
-                            float cm[8];
-#pragma unroll
-                            for (int qq = 0; qq < 8; ++qq)
-                                cm[qq] = fmaxf(fmaxf(x[qq], x[qq + 8]), fmaxf(x[qq + 16], x[qq + 24]));
-                            const float cmax = fmaxf(fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])),
-                                                     fmaxf(fmaxf(cm[4], cm[5]), fmaxf(cm[6], cm[7])));
-                            if (cmax != -INFINITY) {
-                                // online (max, sum exp) one chunk at a time
-                                const float mn = fmaxf(m[b], cmax);
-                                float e = 0.0f;
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) e += expf(x[j] - mn);  // masked: exp(-inf) = 0
-                                sx[b] = (m[b] == -INFINITY ? 0.0f : sx[b] * expf(m[b] - mn)) + e;
-                                m[b] = mn;
+                                for (int j = 0; j < 32; ++j)
+                                    if (vb + j < v_end) dst[j] = __float2bfloat16_rn(x[j]);
                             }
                         }
-                        // branch-free insertion: an element passes only strictly
-                        // smaller values (equal values keep the smaller index)
+                        if (topk) {
+                            const int n_ok = min(32, v_end - vb);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int l = j & (kL - 1);
-                            float cv = x[j];
-                            int32_t ci = vb + j;
+                            for (int j = 0; j < 32; ++j) x[j] = j < n_ok ? x[j] : -INFINITY;
+                            if (p.want_lse) {
+                                float cm[8];
 #pragma unroll
-                            for (int qq = 0; qq < K; ++qq) {
-                                const bool gt = cv > lv[b][l][qq];
-                                const float nv = gt ? cv : lv[b][l][qq];
-                                const int32_t ni = gt ? ci : li[b][l][qq];
-                                cv = gt ? lv[b][l][qq] : cv;
-                                ci = gt ? li[b][l][qq] : ci;
-                                lv[b][l][qq] = nv;
-                                li[b][l][qq] = ni;
+                                for (int qq = 0; qq < 8; ++qq)
+                                    cm[qq] = fmaxf(fmaxf(x[qq], x[qq + 8]), fmaxf(x[qq + 16], x[qq + 24]));
+                                const float cmax = fmaxf(fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])),
+                                                         fmaxf(fmaxf(cm[4], cm[5]), fmaxf(cm[6], cm[7])));
+                                if (cmax != -INFINITY) {
+                                    // online (max, sum exp) one chunk at a time
+                                    const float mn = fmaxf(m[b], cmax);
+                                    float e = 0.0f;
+#pragma unroll
+                                    for (int j = 0; j < 32; ++j) e += expf(x[j] - mn);  // masked: exp(-inf) = 0
+                                    sx[b] = (m[b] == -INFINITY ? 0.0f : sx[b] * expf(m[b] - mn)) + e;
+                                    m[b] = mn;
+                                }
+                            }
+                            // branch-free insertion: an element passes only strictly
+                            // smaller values (equal values keep the smaller index)
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const int l = j & (kL - 1);
+                                float cv = x[j];
+                                int32_t ci = vb + j;
+#pragma unroll
+                                for (int qq = 0; qq < K; ++qq) {
+                                    const bool gt = cv > lv[b][l][qq];
+                                    const float nv = gt ? cv : lv[b][l][qq];
+                                    const int32_t ni = gt ? ci : li[b][l][qq];
+                                    cv = gt ? lv[b][l][qq] : cv;
+                                    ci = gt ? li[b][l][qq] : ci;
+                                    lv[b][l][qq] = nv;
+                                    li[b][l][qq] = ni;
+                                }
                             }
                         }
                     }
