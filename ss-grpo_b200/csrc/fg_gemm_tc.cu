@@ -17,14 +17,19 @@
 // Tiles: 128 tokens x bn outputs on one SM (bn a multiple of 16, <= 256;
 // SwiGLU stacks the bn gate rows on the bn up rows, MMA N = 2 bn <= 256), or
 // 256 tokens on a pair of SMs (below), 64-wide k chunks through a ring of
-// shared-memory stages.  The epilogue and the ring depth are template
-// parameters, so the kernels carry no per-element mode branches.  Work units are
-// (output tile, k range): with split-K the units write fp32 partial tiles
-// to a workspace and a second kernel adds them in k order and applies the
-// epilogue, so results do not depend on which CTA finishes first.  Persistent grid, units ordered weight-tile-major so the
-// token tiles sharing a weight tile run together and the weights stream from
-// HBM about once:
-//   warp 0     TMA producer (X box 128 x 64, W box bn x 64, 128-byte swizzle);
+// shared-memory slots -- two chunks per slot when K has an even number of
+// chunks, each operand of a slot one TMA box through a (64 k, row, chunk)
+// tensor map, since an SM takes in more bytes per second with fewer, larger
+// TMA instructions.  The epilogue and the ring depth are template
+// parameters, so the kernels carry no per-element mode branches.  Work units
+// are (output tile, k range): with split-K the units write fp32 partial
+// tiles to a workspace and a second kernel adds them in k order and applies
+// the epilogue, so results do not depend on which CTA finishes first.
+// Persistent grid, units ordered weight-tile-major so the token tiles
+// sharing a weight tile run together and the weights stream from HBM about
+// once:
+//   warp 0     TMA producer (X box 128 rows x 64 k x cps chunks, W box bn rows
+//              x 64 k x cps chunks, 128-byte swizzle);
 //   warp 1     allocates 512 TMEM columns (two accumulators, 256 apart); one
 //              thread issues tcgen05.mma, commits stages and tiles;
 //   warps 4-11 epilogue: warp w reads TMEM lanes 32 (w % 4) .. (one token row
