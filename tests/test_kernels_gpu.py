@@ -859,6 +859,10 @@ def _linear_ref(x, w, epi, bias=None, resid=None):
     (832, 1536, 2048, 0, True, 256, 128, 1),     # QKV with bias
     (320, 1536, 151936, 0, False, 256, 256, 1),  # internal-node lm_head
     (300, 512, 1024, 2, False, 256, 64, 2),      # SwiGLU split-K on a pair
+    # one k chunk per ring slot: an odd number of chunks, or more splits than chunk pairs
+    (200, 192, 256, 0, True, 128, 64, 1),
+    (300, 320, 512, 1, False, 256, 128, 1),
+    (256, 512, 256, 2, False, 128, 64, 8),
 ])
 def test_linear_epilogues_match_fp32(ops, M, K, N, epi, bias, bm, bn, splits):
     """fg_linear against an fp32 torch reference of the same projection and
@@ -894,14 +898,15 @@ def test_linear_epilogues_match_fp32(ops, M, K, N, epi, bias, bm, bn, splits):
 
 def test_linear_ring_depths_give_the_same_bits(ops):
     """The ring depth only changes how many k chunks are in flight: 4, 6 and
-    8 stages give identical outputs (the k order of the accumulation is the
-    same), for a fused epilogue and a split-K tile."""
+    8 chunks (2, 3 and 4 two-chunk slots) give identical outputs (the k
+    order of the accumulation is the same), for a fused epilogue and a
+    split-K tile."""
     g = torch.Generator().manual_seed(3)
     M, K, N = 300, 1024, 512
     x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
     w = (torch.randn(N, K, generator=g) * K ** -0.5).to(torch.bfloat16).to(DEV)
     r = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV)
-    for bn, splits in ((64, 1), (64, 2)):  # 24 KB stages: 8 of them fit
+    for bn, splits in ((64, 1), (64, 2)):  # 48 KB two-chunk slots: 4 of them fit
         need = ops.linear_workspace_bytes(M, N, K, 1, bn, splits, 128)
         ws = torch.zeros(need // 4 + 16, dtype=torch.int32, device=DEV) if need else None
         outs = [ops.linear(x, w, resid=r, out=r.clone(), bm=128, bn=bn, splits=splits, stages=st, workspace=ws)
