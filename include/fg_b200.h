@@ -474,8 +474,10 @@ fg_status fg_gate_up_silu(const void *x, int32_t dtype, int32_t T, int32_t H, co
  * sharing each weight box) x bn outputs (a multiple of 16, at most 256; the
  * epilogue's TMEM reads must fit the tile's accumulator, FG_EINVAL
  * otherwise) with the k range cut into `splits` parts (split-K), through a
- * ring of `stages` 64-wide k chunks; any of bm / bn / splits / stages <= 0 is
- * chosen from the shape.  splits > 1 writes fp32 partials to workspace
+ * ring holding `stages` 64-wide k chunks (4, 6 or 8 for bm 128, 6 for bm
+ * 256), staged two chunks per slot when K / 64 is even and splits <= K / 128
+ * (as many two-chunk slots as shared memory holds, at least two), else one;
+ * any of bm / bn / splits / stages <= 0 is chosen from the shape.  splits > 1 writes fp32 partials to workspace
  * (fg_linear_workspace_size bytes for the same bm / bn / splits: splits x M x
  * N floats, 2N for SwiGLU) and a second kernel adds them in k order and
  * applies the epilogue.  K a multiple of 64, N a multiple of 8 (of bn for
